@@ -1,0 +1,121 @@
+/*
+ * lancius_cuda.h -- C ABI of the B200 (sm_100a) execution backend for Lancius.
+ *
+ * Replaces, below the unchanged IR / scheduler / memory-plan contract, the
+ * reference's CPU math:
+ *   execute_node_math()             bleeding/v11A1/src/runtime/lancius_scheduler.c:61-309
+ *   lancius_schedule_execute()      bleeding/v11A1/src/runtime/lancius_scheduler.c:311-362
+ *   lancius_execute_vision_op()     bleeding/v11A1/src/runtime/lancius_vision_ops.c:10-191
+ *   kernel_*()                      bleeding/v11A1/include/lancius/lancius_kernels.h:14-50
+ *
+ * Plain C types only (no CUDA or torch types): streams are passed as void*
+ * (a cudaStream_t, NULL = the context's stream for ctx calls / the legacy default
+ * stream for per-op calls); device buffers are float* device pointers.
+ * Every call reports failure through lancius_set_error() and its return value;
+ * nothing aborts. All device math is FP32 storage with one of the precision
+ * modes below.
+ */
+#ifndef LANCIUS_CUDA_H
+#define LANCIUS_CUDA_H
+
+#include "lancius/lancius_ir.h"
+#include "lancius/lancius_scheduler.h"
+#include "lancius/lancius_memory_planner.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Contraction precision (GEMM, conv, attention).
+ *  FP32_EXACT: 3xTF32 split on tcgen05 (a_hi*b_hi + a_hi*b_lo + a_lo*b_hi), FP32
+ *              accumulate; parity bar normwise rel 1e-4 vs the FP64 reference.
+ *  TF32:       one tcgen05 kind::tf32 pass; parity bar 2e-2.                  */
+typedef enum { LCU_MODE_FP32_EXACT = 0, LCU_MODE_TF32 = 1 } lcu_mode;
+
+/* Epilogue fused into GEMM / conv stores. */
+typedef enum { LCU_EPI_NONE = 0, LCU_EPI_RELU = 1, LCU_EPI_GELU = 2 } lcu_epilogue;
+
+typedef struct lcu_ctx lcu_ctx;
+
+/* ---- context: one per GPU, one host thread drives it ------------------- */
+lcu_ctx* lcu_create(int device);
+void lcu_destroy(lcu_ctx* ctx);
+lancius_error lcu_set_mode(lcu_ctx* ctx, lcu_mode mode);
+void* lcu_stream(lcu_ctx* ctx);                 /* the context's cudaStream_t */
+lancius_error lcu_synchronize(lcu_ctx* ctx);     /* also reports device watchdog flags */
+
+/* ---- graph binding: the memory plan's offsets map onto one device allocation.
+ * plan == NULL: the backend plans the FP32 device pool itself
+ * (lancius_build_memory_plan_ex(sched, g, 4, 256, 1)). A caller-supplied plan is
+ * validated first (lancius_memory_plan_validate with 4-byte elements) and
+ * rejected with LANCIUS_ERROR_INVALID_MODEL when live tensors would overlap.
+ * INPUT and CONST nodes get their own persistent slots after the pool.        */
+lancius_error lcu_bind_plan(lcu_ctx* ctx, lancius_schedule* sched, lancius_graph* g,
+                            const lancius_memory_plan* plan);
+
+/* Host <-> device copies of one node's slot. host_dtype is LANCIUS_DTYPE_FP64
+ * (reference-style double buffers, converted on the device) or FP32. */
+lancius_error lcu_upload(lcu_ctx* ctx, const lancius_node* n, const void* host, lancius_dtype host_dtype);
+lancius_error lcu_download(lcu_ctx* ctx, const lancius_node* n, void* host, lancius_dtype host_dtype);
+/* Uploads every INPUT node whose runtime_data (FP64) is bound on the host. */
+lancius_error lcu_upload_bound_inputs(lcu_ctx* ctx);
+float* lcu_node_device_ptr(lcu_ctx* ctx, const lancius_node* n);
+
+/* Runs every wave of the bound schedule on the context's stream (asynchronous;
+ * lcu_synchronize() or a download waits). Same shape as the reference's
+ * lancius_schedule_execute(schedule, scratch): the second argument is the
+ * device context instead of a host arena. Errors: lancius_get_error(). */
+void lancius_schedule_execute_cuda(lancius_schedule* sched, lcu_ctx* ctx);
+/* Number of kernels the last lancius_schedule_execute_cuda call launched. */
+int lcu_last_launch_count(lcu_ctx* ctx);
+/* 1 = replay the schedule through a captured CUDA graph after the first run. */
+lancius_error lcu_set_graph_replay(lcu_ctx* ctx, int enable);
+/* 1 (default) = fold MATMUL -> ADD(BROADCAST bias) -> RELU|GELU -> ADD(residual)
+ * chains into one GEMM epilogue when the backend plans memory itself. Nodes inside
+ * a folded chain share the chain's output slot (a download returns the chain's
+ * final value); a BROADCAST read only by a folded ADD is never materialised.
+ * Takes effect at the next lcu_bind_plan. */
+lancius_error lcu_set_fusion(lcu_ctx* ctx, int enable);
+
+/* Page-locked host buffers for fast lcu_upload / lcu_download. */
+void* lcu_host_alloc(size_t bytes);
+void lcu_host_free(void* p);
+
+/* ---- per-op launchers: argument order mirrors the reference kernel_* ------ */
+/* C[M,N] = A[M,K] * B[K,N] (+ bias[N]) (epilogue); row-major.
+ * Mirrors kernel_matmul (lancius_kernels.c:15-26) / executor MATMUL (scheduler.c:190-235). */
+lancius_error lcu_matmul(float* out, const float* a, const float* b, size_t M, size_t K, size_t N,
+                         const float* bias, int epilogue, int mode, void* stream);
+/* Causal (causal=1, kernel_attention lancius_kernels.c:278-332) or unmasked
+ * attention over B independent [S, H, D] blocks (heads concatenated). */
+lancius_error lcu_attention(float* out, const float* q, const float* k, const float* v,
+                            size_t B, size_t S, size_t H, size_t D, int causal, int mode, void* stream);
+/* NCHW input, OIHW weights, zero padding (kernel_conv2d_fwd / kernel_conv2d_relu_fwd,
+ * lancius_kernels.c:28-60,140-173). relu = 1 applies ReLU in the store. */
+lancius_error lcu_conv2d(float* out, const float* in, const float* w, size_t N, size_t C_in,
+                         size_t H_in, size_t W_in, size_t C_out, size_t K_h, size_t K_w,
+                         size_t stride, size_t pad, int relu, int mode, void* stream);
+/* kernel_layernorm (lancius_kernels.c:217-236): biased variance, eps. */
+lancius_error lcu_layernorm(float* out, const float* in, const float* gamma, const float* beta,
+                            size_t rows, size_t hidden, float eps, void* stream);
+lancius_error lcu_softmax(float* out, const float* in, size_t rows, size_t cols, void* stream);
+lancius_error lcu_gelu(float* out, const float* in, size_t n, void* stream);
+lancius_error lcu_tanh(float* out, const float* in, size_t n, void* stream);
+lancius_error lcu_relu(float* out, const float* in, size_t n, void* stream);
+lancius_error lcu_add(float* out, const float* a, const float* b, size_t n, void* stream);
+lancius_error lcu_sub(float* out, const float* a, const float* b, size_t n, void* stream);
+lancius_error lcu_mul(float* out, const float* a, const float* b, size_t n, void* stream);
+/* BROADCAST (scheduler.c:268-278): in_elems == 1 fills; else row vector -> [rows, cols]. */
+lancius_error lcu_broadcast(float* out, const float* in, size_t in_elems, size_t rows, size_t cols, void* stream);
+lancius_error lcu_fill(float* out, float value, size_t n, void* stream);
+lancius_error lcu_sum_axis1(float* out, const float* in, size_t rows, size_t cols, void* stream);
+lancius_error lcu_maxpool2d(float* out, const float* in, size_t N, size_t C, size_t H_in, size_t W_in,
+                            size_t K, size_t stride, void* stream);
+
+/* Library self-description for tests: the names of this build's kernels. */
+const char* lcu_build_info(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

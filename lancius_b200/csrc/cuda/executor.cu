@@ -1,0 +1,633 @@
+// Device context and graph executor: the B200 sibling of the reference's
+// lancius_schedule_execute (bleeding/v11A1/src/runtime/lancius_scheduler.c:311-362).
+//
+// lcu_bind_plan() turns (schedule, graph, plan) into a static launch list once:
+//   * every node gets a byte offset in ONE device allocation per context:
+//     [ planned pool | persistent INPUT/CONST slots | launch tables ];
+//   * the executor's own plan (plan == NULL) is built on a fused view of the graph:
+//     MATMUL -> ADD(BROADCAST(bias)) -> RELU|GELU -> ADD(residual) chains collapse
+//     into one GEMM with that epilogue, and RESHAPE/FLATTEN share their source's
+//     bytes; nodes inside a chain alias the chain's storage;
+//   * same-shaped nodes of one wave (the reference runs them concurrently on its
+//     thread pool, :364-413) become ONE launch over a device-resident pointer table.
+// lancius_schedule_execute_cuda() replays that list on the context's stream,
+// optionally through a captured CUDA graph.
+#include "lcu_internal.h"
+#include "../host/planner_internal.h"
+#include <map>
+#include <string>
+#include <tuple>
+#include <vector>
+#include <cstring>
+#include <cstdio>
+
+namespace {
+
+constexpr size_t NPOS = (size_t)-1;
+constexpr size_t SLOT_ALIGN = 256;
+
+enum StepKind { S_GEMM, S_ATTN, S_CONV, S_LN, S_SOFTMAX, S_SUMAX1, S_ELT, S_BCAST, S_MAXPOOL };
+
+struct Step {
+    StepKind kind;
+    int count = 1;
+    size_t table_off = 0;      // byte offset of the group table inside the allocation
+    size_t M = 0, N = 0, K = 0;
+    int epi = 0, op = 0, vec = 0, causal = 0, relu = 0;
+    size_t S = 0, H = 0, D = 0;
+    size_t cn = 0, ci = 0, h = 0, w = 0, co = 0, kh = 0, kw = 0, stride = 0, pad = 0;
+    size_t out = 0, in0 = 0, in1 = 0;   // node offsets for single-instance steps
+    size_t rows = 0, cols = 0, n = 0, in_elems = 0;
+    float eps = 1e-5f;
+};
+
+struct Chain {          // a MATMUL and the epilogue nodes folded into it
+    const lancius_node* bias_src = nullptr;
+    const lancius_node* resid = nullptr;
+    int epi = LCU_EPI_NONE;
+};
+
+size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+}  // namespace
+
+struct lcu_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int mode = LCU_MODE_FP32_EXACT;
+    int replay = 0;
+    int fusion = 1;
+    lancius_graph* g = nullptr;
+    lancius_schedule* s = nullptr;
+    char* dmem = nullptr;
+    size_t dmem_bytes = 0;
+    double* staging = nullptr;
+    size_t staging_elems = 0;
+    std::vector<size_t> off;            // node id -> byte offset in dmem (NPOS: no storage)
+    std::vector<Step> steps;
+    cudaGraphExec_t exec = nullptr;
+    int graph_launches = 0;
+    int last_launches = 0;
+};
+
+static lancius_error fail(lancius_error e) { lancius_set_error(e); return e; }
+static lancius_error cuda_fail(cudaError_t e) { return lcu_check_cuda(e); }
+
+static void release_binding(lcu_ctx* c) {
+    if (c->exec) { cudaGraphExecDestroy(c->exec); c->exec = nullptr; }
+    if (c->dmem) { cudaFree(c->dmem); c->dmem = nullptr; }
+    if (c->staging) { cudaFree(c->staging); c->staging = nullptr; }
+    c->dmem_bytes = 0; c->staging_elems = 0;
+    c->off.clear(); c->steps.clear();
+    c->g = nullptr; c->s = nullptr;
+}
+
+extern "C" {
+
+lcu_ctx* lcu_create(int device) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess || device < 0 || device >= n) {
+        cudaGetLastError();
+        lancius_set_error(LANCIUS_ERROR_INTERNAL);
+        return nullptr;
+    }
+    if (cudaSetDevice(device) != cudaSuccess) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return nullptr; }
+    lcu_ctx* c = new (std::nothrow) lcu_ctx();
+    if (!c) { lancius_set_error(LANCIUS_ERROR_OOM); return nullptr; }
+    c->device = device;
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        delete c;
+        lancius_set_error(LANCIUS_ERROR_INTERNAL);
+        return nullptr;
+    }
+    return c;
+}
+
+void lcu_destroy(lcu_ctx* c) {
+    if (!c) return;
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    release_binding(c);
+    cudaStreamDestroy(c->stream);
+    delete c;
+}
+
+lancius_error lcu_set_mode(lcu_ctx* c, lcu_mode mode) {
+    if (!c) return fail(LANCIUS_ERROR_NULL_PTR);
+    if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32) return fail(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+    if (c->mode != (int)mode && c->exec) { cudaGraphExecDestroy(c->exec); c->exec = nullptr; }
+    c->mode = mode;
+    return LANCIUS_ERROR_OK;
+}
+
+lancius_error lcu_set_graph_replay(lcu_ctx* c, int enable) {
+    if (!c) return fail(LANCIUS_ERROR_NULL_PTR);
+    c->replay = enable ? 1 : 0;
+    if (!c->replay && c->exec) { cudaGraphExecDestroy(c->exec); c->exec = nullptr; }
+    return LANCIUS_ERROR_OK;
+}
+
+lancius_error lcu_set_fusion(lcu_ctx* c, int enable) {
+    if (!c) return fail(LANCIUS_ERROR_NULL_PTR);
+    c->fusion = enable ? 1 : 0;
+    return LANCIUS_ERROR_OK;
+}
+
+void* lcu_stream(lcu_ctx* c) { return c ? (void*)c->stream : nullptr; }
+
+lancius_error lcu_synchronize(lcu_ctx* c) {
+    if (!c) return fail(LANCIUS_ERROR_NULL_PTR);
+    cudaSetDevice(c->device);
+    return cuda_fail(cudaStreamSynchronize(c->stream));
+}
+
+int lcu_last_launch_count(lcu_ctx* c) { return c ? c->last_launches : 0; }
+
+float* lcu_node_device_ptr(lcu_ctx* c, const lancius_node* n) {
+    if (!c || !n || !c->dmem || n->id >= c->off.size() || c->off[n->id] == NPOS) return nullptr;
+    return reinterpret_cast<float*>(c->dmem + c->off[n->id]);
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// binding
+
+namespace {
+
+struct Builder {
+    lcu_ctx* c;
+    lancius_graph* g;
+    lancius_schedule* s;
+    std::vector<uint32_t> wave_of;                 // node id -> wave
+    std::vector<std::vector<const lancius_node*>> users;
+    std::vector<Chain> chain;                      // indexed by MATMUL id
+    std::vector<uint8_t> is_chain_root;
+    std::vector<uint32_t> alias;                   // LCU_ALIAS_* or root id
+    std::vector<char> tables;                      // host image of all launch tables
+    std::vector<std::pair<size_t, size_t>> table_fix;  // (pos in tables, node offset) patched to device pointers
+
+    const lancius_node* sole_user(const lancius_node* n) const {
+        return users[n->id].size() == 1 ? users[n->id][0] : nullptr;
+    }
+    bool earlier(const lancius_node* a, const lancius_node* b) const { return wave_of[a->id] < wave_of[b->id]; }
+
+    // MATMUL -> [ADD bias] -> [RELU|GELU] -> [ADD residual]
+    void find_chains() {
+        for (uint32_t i = 0; i < g->node_count; i++) {
+            const lancius_node* m = g->nodes[i];
+            if (m->op != LANCIUS_OP_MATMUL || m->ndim != 2) continue;
+            size_t M = m->shape[0], N = m->shape[1];
+            Chain ch;
+            const lancius_node* tail = m;
+            const lancius_node* u = sole_user(tail);
+            if (u && u->op == LANCIUS_OP_ADD && u->input_count == 2 && u->ndim == 2) {
+                const lancius_node* other = u->inputs[0] == tail ? u->inputs[1] : u->inputs[0];
+                if (u->inputs[0] != u->inputs[1] && other->op == LANCIUS_OP_BROADCAST && other->ndim == 2 &&
+                    other->shape[0] == M && other->shape[1] == N && other->input_count == 1 &&
+                    lancius_node_elements(other->inputs[0]) == N && earlier(other->inputs[0], m) &&
+                    !other->inputs[0]->runtime_data_int8) {
+                    ch.bias_src = other->inputs[0];
+                    if (users[other->id].size() == 1) alias[other->id] = LCU_ALIAS_ELIDED;
+                    alias[u->id] = m->id;
+                    tail = u;
+                    u = sole_user(tail);
+                }
+            }
+            if (u && (u->op == LANCIUS_OP_RELU || u->op == LANCIUS_OP_GELU)) {
+                ch.epi = u->op == LANCIUS_OP_RELU ? LCU_EPI_RELU : LCU_EPI_GELU;
+                alias[u->id] = m->id;
+                tail = u;
+                u = sole_user(tail);
+            }
+            if (u && u->op == LANCIUS_OP_ADD && u->input_count == 2 && u->ndim == 2 && u->inputs[0] != u->inputs[1]) {
+                const lancius_node* other = u->inputs[0] == tail ? u->inputs[1] : u->inputs[0];
+                if (lancius_node_elements(other) == M * N && earlier(other, m) && other->op != LANCIUS_OP_NOP) {
+                    ch.resid = other;
+                    alias[u->id] = m->id;
+                    tail = u;
+                }
+            }
+            chain[m->id] = ch;
+            is_chain_root[m->id] = 1;
+        }
+    }
+
+    void alias_views() {
+        for (uint32_t i = 0; i < g->node_count; i++) {
+            const lancius_node* n = g->nodes[i];
+            if ((n->op == LANCIUS_OP_RESHAPE || n->op == LANCIUS_OP_FLATTEN) && n->input_count == 1 &&
+                lancius_node_elements(n) <= lancius_node_elements(n->inputs[0]))
+                alias[n->id] = n->inputs[0]->id;
+        }
+    }
+
+    template <class T>
+    size_t add_table(const std::vector<T>& v) {
+        size_t pos = align_up(tables.size(), 64);
+        tables.resize(pos + sizeof(T) * v.size());
+        memcpy(tables.data() + pos, v.data(), sizeof(T) * v.size());
+        return pos;
+    }
+};
+
+// device pointer placeholder: node byte offset + 1 (0 stays NULL) -- patched at upload
+inline const float* ptr_token(size_t off) { return reinterpret_cast<const float*>(off + 1); }
+
+}  // namespace
+
+static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fused) {
+    lcu_ctx* c = b.c;
+    auto O = [&](const lancius_node* n) { return off[n->id]; };
+    for (uint32_t w = 0; w < b.s->wave_count; w++) {
+        // group key -> list of node indices in this wave
+        std::map<std::string, std::vector<const lancius_node*>> groups;
+        std::vector<std::string> order;
+        for (uint32_t i = 0; i < b.s->waves[w].node_count; i++) {
+            const lancius_node* n = b.s->waves[w].nodes[i];
+            char key[256];
+            key[0] = 0;
+            switch (n->op) {
+                case LANCIUS_OP_INPUT: case LANCIUS_OP_CONST: case LANCIUS_OP_NOP:
+                    continue;
+                default: break;
+            }
+            if (fused && b.alias[n->id] != LCU_ALIAS_NONE) continue;   // folded into a chain / view / elided
+            for (uint32_t j = 0; j < n->input_count; j++) {
+                const lancius_node* in = n->inputs[j];
+                if (!in || off[in->id] == NPOS) return fail(LANCIUS_ERROR_NULL_PTR);
+                if (in->runtime_data_int8 || in->dtype == LANCIUS_DTYPE_INT8) return fail(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+            }
+            size_t E = lancius_node_elements(n);
+            switch (n->op) {
+                case LANCIUS_OP_MATMUL: {
+                    const lancius_node *a = n->inputs[0], *bb = n->inputs[1];
+                    size_t M = n->shape[0], N = n->shape[1], K = a->shape[a->ndim - 1];
+                    if (lancius_node_elements(a) < M * K || lancius_node_elements(bb) < K * N) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
+                    Chain ch = b.chain[n->id];
+                    snprintf(key, sizeof key, "G:%zu:%zu:%zu:%d:%d:%d", M, N, K, ch.epi, ch.bias_src != nullptr, ch.resid != nullptr);
+                } break;
+                case LANCIUS_OP_ADD: case LANCIUS_OP_SUB: case LANCIUS_OP_MUL:
+                    if (lancius_node_elements(n->inputs[0]) < E || lancius_node_elements(n->inputs[1]) < E)
+                        return fail(LANCIUS_ERROR_SHAPE_MISMATCH);   // the reference reads past the end here
+                    snprintf(key, sizeof key, "E:%d:%zu", (int)n->op, E);
+                    break;
+                case LANCIUS_OP_RELU: case LANCIUS_OP_GELU: case LANCIUS_OP_TANH:
+                case LANCIUS_OP_RESHAPE: case LANCIUS_OP_FLATTEN:
+                    if (lancius_node_elements(n->inputs[0]) < E) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
+                    snprintf(key, sizeof key, "E:%d:%zu", (int)n->op, E);
+                    break;
+                case LANCIUS_OP_LAYERNORM:
+                    if (n->ndim < 2 || lancius_node_elements(n->inputs[1]) < n->shape[1] ||
+                        lancius_node_elements(n->inputs[2]) < n->shape[1] || lancius_node_elements(n->inputs[0]) < E)
+                        return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
+                    snprintf(key, sizeof key, "L:%zu:%zu", n->shape[0], n->shape[1]);
+                    break;
+                case LANCIUS_OP_ATTENTION:
+                    if (n->ndim != 3) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
+                    for (int j = 0; j < 3; j++)
+                        if (lancius_node_elements(n->inputs[j]) < E) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
+                    if (n->shape[2] != 64 && n->shape[2] != 128) return fail(LANCIUS_ERROR_UNSUPPORTED_OP);
+                    snprintf(key, sizeof key, "A:%zu:%zu:%zu:%d", n->shape[0], n->shape[1], n->shape[2], n->attr_val != 1.0);
+                    break;
+                case LANCIUS_OP_SOFTMAX: case LANCIUS_OP_SUM_AXIS1: case LANCIUS_OP_BROADCAST:
+                case LANCIUS_OP_CONV2D: case LANCIUS_OP_CONV2D_RELU_FUSED: case LANCIUS_OP_MAXPOOL2D:
+                    snprintf(key, sizeof key, "U:%u", n->id);      // one launch per node
+                    break;
+                default:
+                    fprintf(stderr, "[LANCIUS CUDA] op %d (node %u) has no device kernel\n", (int)n->op, n->id);
+                    return fail(LANCIUS_ERROR_UNSUPPORTED_OP);
+            }
+            std::string k(key);
+            if (!groups.count(k)) order.push_back(k);
+            groups[k].push_back(n);
+        }
+        for (const std::string& k : order) {
+            const std::vector<const lancius_node*>& ns = groups[k];
+            const lancius_node* n = ns[0];
+            Step st;
+            st.count = (int)ns.size();
+            switch (n->op) {
+                case LANCIUS_OP_MATMUL: {
+                    st.kind = S_GEMM;
+                    st.M = n->shape[0]; st.N = n->shape[1]; st.K = n->inputs[0]->shape[n->inputs[0]->ndim - 1];
+                    st.epi = b.chain[n->id].epi;
+                    std::vector<LcuGemmGroup> t;
+                    for (const lancius_node* x : ns) {
+                        const Chain& ch = b.chain[x->id];
+                        t.push_back(LcuGemmGroup{ptr_token(O(x->inputs[0])), ptr_token(O(x->inputs[1])),
+                                                 (float*)ptr_token(O(x)),
+                                                 ch.bias_src ? ptr_token(O(ch.bias_src)) : nullptr,
+                                                 ch.resid ? ptr_token(O(ch.resid)) : nullptr});
+                    }
+                    st.table_off = b.add_table(t);
+                } break;
+                case LANCIUS_OP_ATTENTION: {
+                    st.kind = S_ATTN;
+                    st.S = n->shape[0]; st.H = n->shape[1]; st.D = n->shape[2]; st.causal = n->attr_val != 1.0;
+                    std::vector<LcuAttnGroup> t;
+                    for (const lancius_node* x : ns)
+                        t.push_back(LcuAttnGroup{ptr_token(O(x->inputs[0])), ptr_token(O(x->inputs[1])),
+                                                 ptr_token(O(x->inputs[2])), (float*)ptr_token(O(x))});
+                    st.table_off = b.add_table(t);
+                } break;
+                case LANCIUS_OP_LAYERNORM: {
+                    st.kind = S_LN; st.rows = n->shape[0]; st.cols = n->shape[1]; st.eps = 1e-5f; st.vec = 1;
+                    std::vector<LcuRowGroup> t;
+                    for (const lancius_node* x : ns)
+                        t.push_back(LcuRowGroup{(float*)ptr_token(O(x)), ptr_token(O(x->inputs[0])),
+                                                ptr_token(O(x->inputs[1])), ptr_token(O(x->inputs[2]))});
+                    st.table_off = b.add_table(t);
+                } break;
+                case LANCIUS_OP_ADD: case LANCIUS_OP_SUB: case LANCIUS_OP_MUL:
+                case LANCIUS_OP_RELU: case LANCIUS_OP_GELU: case LANCIUS_OP_TANH:
+                case LANCIUS_OP_RESHAPE: case LANCIUS_OP_FLATTEN: {
+                    st.kind = S_ELT;
+                    st.op = n->op == LANCIUS_OP_ADD ? 0 : n->op == LANCIUS_OP_SUB ? 1 : n->op == LANCIUS_OP_MUL ? 2
+                          : n->op == LANCIUS_OP_RELU ? 3 : n->op == LANCIUS_OP_GELU ? 4 : n->op == LANCIUS_OP_TANH ? 5 : 6;
+                    st.n = lancius_node_elements(n);
+                    st.vec = st.n % 4 == 0;
+                    std::vector<LcuEltGroup> t;
+                    for (const lancius_node* x : ns)
+                        t.push_back(LcuEltGroup{(float*)ptr_token(O(x)), ptr_token(O(x->inputs[0])),
+                                                x->input_count > 1 ? ptr_token(O(x->inputs[1])) : nullptr});
+                    st.table_off = b.add_table(t);
+                } break;
+                case LANCIUS_OP_SOFTMAX:
+                    st.kind = S_SOFTMAX; st.rows = n->shape[0]; st.cols = n->shape[1];
+                    st.out = O(n); st.in0 = O(n->inputs[0]);
+                    break;
+                case LANCIUS_OP_SUM_AXIS1:
+                    st.kind = S_SUMAX1; st.rows = n->inputs[0]->shape[0]; st.cols = n->inputs[0]->shape[1];
+                    st.out = O(n); st.in0 = O(n->inputs[0]);
+                    break;
+                case LANCIUS_OP_BROADCAST: {
+                    size_t ie = lancius_node_elements(n->inputs[0]);
+                    if (ie != 1 && ie < n->shape[1]) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
+                    st.kind = S_BCAST; st.in_elems = ie; st.out = O(n); st.in0 = O(n->inputs[0]);
+                    // scalar: fill every element; row vector: the first shape[0] x shape[1] block (scheduler.c:271-277)
+                    st.rows = ie == 1 ? lancius_node_elements(n) : n->shape[0];
+                    st.cols = ie == 1 ? 1 : n->shape[1];
+                } break;
+                case LANCIUS_OP_CONV2D: case LANCIUS_OP_CONV2D_RELU_FUSED: {
+                    const lancius_node *in = n->inputs[0], *wt = n->inputs[1];
+                    st.kind = S_CONV; st.relu = n->op == LANCIUS_OP_CONV2D_RELU_FUSED;
+                    st.cn = in->shape[0]; st.ci = in->shape[1]; st.h = in->shape[2]; st.w = in->shape[3];
+                    st.co = wt->shape[0]; st.kh = wt->shape[2]; st.kw = wt->shape[3]; st.stride = n->stride; st.pad = n->pad;
+                    if (in->ndim != 4 || wt->ndim != 4 || wt->shape[1] != st.ci || st.stride == 0) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
+                    st.out = O(n); st.in0 = O(in); st.in1 = O(wt);
+                } break;
+                case LANCIUS_OP_MAXPOOL2D: {
+                    const lancius_node* in = n->inputs[0];
+                    st.kind = S_MAXPOOL; st.cn = in->shape[0]; st.ci = in->shape[1]; st.h = in->shape[2]; st.w = in->shape[3];
+                    st.kh = n->kernel_h; st.stride = n->stride; st.out = O(n); st.in0 = O(in);
+                } break;
+                default: return fail(LANCIUS_ERROR_UNSUPPORTED_OP);
+            }
+            c->steps.push_back(st);
+        }
+    }
+    return LANCIUS_ERROR_OK;
+}
+
+extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_graph* g, const lancius_memory_plan* plan) {
+    if (!c || !s || !g) return fail(LANCIUS_ERROR_NULL_PTR);
+    cudaSetDevice(c->device);
+    cudaStreamSynchronize(c->stream);
+    release_binding(c);
+
+    Builder b;
+    b.c = c; b.g = g; b.s = s;
+    uint32_t ids = g->next_id;
+    b.wave_of.assign(ids, 0);
+    b.users.assign(ids, {});
+    b.chain.assign(ids, Chain());
+    b.is_chain_root.assign(ids, 0);
+    b.alias.assign(ids, LCU_ALIAS_NONE);
+    for (uint32_t w = 0; w < s->wave_count; w++)
+        for (uint32_t i = 0; i < s->waves[w].node_count; i++) b.wave_of[s->waves[w].nodes[i]->id] = w;
+    for (uint32_t i = 0; i < g->node_count; i++)
+        for (uint32_t j = 0; j < g->nodes[i]->input_count; j++)
+            if (g->nodes[i]->inputs[j]) b.users[g->nodes[i]->inputs[j]->id].push_back(g->nodes[i]);
+
+    bool fused = plan == nullptr;
+    lancius_memory_plan* own = nullptr;
+    if (fused) {
+        if (c->fusion) b.find_chains();
+        b.alias_views();
+        own = lcu_plan_aliased(s, g, 4, SLOT_ALIGN, b.alias.data());
+        if (!own) return fail(LANCIUS_ERROR_OOM);
+        plan = own;
+    } else if (lancius_memory_plan_validate(plan, s, g, 4) != LANCIUS_ERROR_OK) {
+        return fail(LANCIUS_ERROR_INVALID_MODEL);
+    }
+
+    // device layout: pool, then persistent INPUT/CONST slots
+    std::vector<size_t> off(ids, NPOS);
+    size_t cursor = align_up(plan->peak_memory, SLOT_ALIGN);
+    size_t max_io = 0;
+    for (uint32_t i = 0; i < g->node_count; i++) {
+        const lancius_node* n = g->nodes[i];
+        size_t E = lancius_node_elements(n);
+        if (E > max_io) max_io = E;
+        if (n->op == LANCIUS_OP_INPUT || n->op == LANCIUS_OP_CONST) {
+            off[n->id] = cursor;
+            cursor += align_up(E * 4 ? E * 4 : 4, SLOT_ALIGN);
+        } else if (plan->is_pooled[n->id] == 1) {
+            off[n->id] = plan->offsets[n->id];
+        }
+    }
+    // aliases (views / chain members) resolve to their storage root
+    for (int pass = 0; pass < 64; pass++) {
+        bool changed = false;
+        for (uint32_t i = 0; i < g->node_count; i++) {
+            const lancius_node* n = g->nodes[i];
+            uint32_t a = fused ? b.alias[n->id] : LCU_ALIAS_NONE;
+            if (a != LCU_ALIAS_NONE && a != LCU_ALIAS_ELIDED && off[n->id] == NPOS && off[a] != NPOS) {
+                off[n->id] = off[a]; changed = true;
+            }
+        }
+        if (!changed) break;
+    }
+    lancius_error e = build_steps(b, off, fused);
+    if (own) lancius_memory_plan_destroy(own);
+    if (e != LANCIUS_ERROR_OK) { c->steps.clear(); return e; }
+
+    size_t table_base = align_up(cursor, SLOT_ALIGN);
+    size_t total = table_base + align_up(b.tables.size(), SLOT_ALIGN);
+    cudaError_t ce = cudaMalloc(&c->dmem, total ? total : 256);
+    if (ce != cudaSuccess) { cudaGetLastError(); c->steps.clear(); return fail(LANCIUS_ERROR_OOM); }
+    c->dmem_bytes = total;
+    // patch pointer tokens (offset + 1) into device addresses
+    auto patch = [&](const float*& p) { if (p) p = reinterpret_cast<const float*>(c->dmem + ((size_t)p - 1)); };
+    for (Step& st : c->steps) {
+        char* base = b.tables.data() + st.table_off;
+        if (st.kind == S_GEMM) {
+            LcuGemmGroup* t = (LcuGemmGroup*)base;
+            for (int i = 0; i < st.count; i++) {
+                patch(t[i].a); patch(t[i].b); patch((const float*&)t[i].c); patch(t[i].bias); patch(t[i].resid);
+            }
+        } else if (st.kind == S_ATTN) {
+            LcuAttnGroup* t = (LcuAttnGroup*)base;
+            for (int i = 0; i < st.count; i++) { patch(t[i].q); patch(t[i].k); patch(t[i].v); patch((const float*&)t[i].o); }
+        } else if (st.kind == S_LN) {
+            LcuRowGroup* t = (LcuRowGroup*)base;
+            for (int i = 0; i < st.count; i++) { patch((const float*&)t[i].out); patch(t[i].in); patch(t[i].gamma); patch(t[i].beta); }
+        } else if (st.kind == S_ELT) {
+            LcuEltGroup* t = (LcuEltGroup*)base;
+            for (int i = 0; i < st.count; i++) { patch((const float*&)t[i].out); patch(t[i].a); patch(t[i].b); }
+        }
+        st.table_off += table_base;
+    }
+    if (!b.tables.empty()) {
+        ce = cudaMemcpyAsync(c->dmem + table_base, b.tables.data(), b.tables.size(), cudaMemcpyHostToDevice, c->stream);
+        if (ce != cudaSuccess) { release_binding(c); return cuda_fail(ce); }
+    }
+    ce = cudaMalloc(&c->staging, (max_io ? max_io : 1) * sizeof(double));
+    if (ce != cudaSuccess) { cudaGetLastError(); release_binding(c); return fail(LANCIUS_ERROR_OOM); }
+    c->staging_elems = max_io;
+    c->off = off;
+    c->g = g; c->s = s;
+    // CONST nodes hold attr_val from bind time on (the reference fills them on first execution, :330-342)
+    for (uint32_t i = 0; i < g->node_count; i++) {
+        const lancius_node* n = g->nodes[i];
+        if (n->op == LANCIUS_OP_CONST)
+            if (lcu_fill((float*)(c->dmem + off[n->id]), (float)n->attr_val, lancius_node_elements(n), c->stream) != LANCIUS_ERROR_OK) {
+                release_binding(c); return fail(LANCIUS_ERROR_INTERNAL);
+            }
+    }
+    ce = cudaStreamSynchronize(c->stream);
+    if (ce != cudaSuccess) { release_binding(c); return cuda_fail(ce); }
+    return LANCIUS_ERROR_OK;
+}
+
+// ---------------------------------------------------------------------------
+// transfers
+
+static bool node_slot(lcu_ctx* c, const lancius_node* n, float** p, size_t* E) {
+    if (!c || !n || !c->g || n->id >= c->off.size() || c->off[n->id] == NPOS) return false;
+    *p = reinterpret_cast<float*>(c->dmem + c->off[n->id]);
+    *E = lancius_node_elements(n);
+    return true;
+}
+
+extern "C" lancius_error lcu_upload(lcu_ctx* c, const lancius_node* n, const void* host, lancius_dtype dt) {
+    float* d; size_t E;
+    if (!host) return fail(LANCIUS_ERROR_NULL_PTR);
+    if (!node_slot(c, n, &d, &E)) return fail(LANCIUS_ERROR_NULL_PTR);
+    cudaSetDevice(c->device);
+    if (dt == LANCIUS_DTYPE_FP32)
+        return cuda_fail(cudaMemcpyAsync(d, host, E * 4, cudaMemcpyHostToDevice, c->stream));
+    if (dt != LANCIUS_DTYPE_FP64) return fail(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+    if (E > c->staging_elems) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
+    cudaError_t ce = cudaMemcpyAsync(c->staging, host, E * 8, cudaMemcpyHostToDevice, c->stream);
+    if (ce != cudaSuccess) return cuda_fail(ce);
+    return lcu_convert_f64_to_f32(d, c->staging, E, c->stream);
+}
+
+extern "C" lancius_error lcu_download(lcu_ctx* c, const lancius_node* n, void* host, lancius_dtype dt) {
+    float* d; size_t E;
+    if (!host) return fail(LANCIUS_ERROR_NULL_PTR);
+    if (!node_slot(c, n, &d, &E)) return fail(LANCIUS_ERROR_NULL_PTR);
+    cudaSetDevice(c->device);
+    cudaError_t ce;
+    if (dt == LANCIUS_DTYPE_FP32) {
+        ce = cudaMemcpyAsync(host, d, E * 4, cudaMemcpyDeviceToHost, c->stream);
+    } else if (dt == LANCIUS_DTYPE_FP64) {
+        if (E > c->staging_elems) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
+        lancius_error e = lcu_convert_f32_to_f64(c->staging, d, E, c->stream);
+        if (e != LANCIUS_ERROR_OK) return e;
+        ce = cudaMemcpyAsync(host, c->staging, E * 8, cudaMemcpyDeviceToHost, c->stream);
+    } else {
+        return fail(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+    }
+    if (ce != cudaSuccess) return cuda_fail(ce);
+    return cuda_fail(cudaStreamSynchronize(c->stream));
+}
+
+extern "C" lancius_error lcu_upload_bound_inputs(lcu_ctx* c) {
+    if (!c || !c->g) return fail(LANCIUS_ERROR_NULL_PTR);
+    for (uint32_t i = 0; i < c->g->node_count; i++) {
+        const lancius_node* n = c->g->nodes[i];
+        if (n->op == LANCIUS_OP_INPUT && n->runtime_data) {
+            lancius_error e = lcu_upload(c, n, n->runtime_data, LANCIUS_DTYPE_FP64);
+            if (e != LANCIUS_ERROR_OK) return e;
+        }
+    }
+    return LANCIUS_ERROR_OK;
+}
+
+extern "C" void* lcu_host_alloc(size_t bytes) {
+    void* p = nullptr;
+    if (cudaMallocHost(&p, bytes ? bytes : 1) != cudaSuccess) { cudaGetLastError(); lancius_set_error(LANCIUS_ERROR_OOM); return nullptr; }
+    return p;
+}
+extern "C" void lcu_host_free(void* p) { if (p) cudaFreeHost(p); }
+
+// ---------------------------------------------------------------------------
+// execution
+
+static lancius_error run_steps(lcu_ctx* c) {
+    char* base = c->dmem;
+    void* st = c->stream;
+    auto F = [&](size_t off) { return reinterpret_cast<float*>(base + off); };
+    for (const Step& s : c->steps) {
+        lancius_error e = LANCIUS_ERROR_OK;
+        switch (s.kind) {
+            case S_GEMM:
+                e = lcu_gemm_simt_grouped((const LcuGemmGroup*)(base + s.table_off), s.count, s.M, s.N, s.K, s.epi, st);
+                break;
+            case S_ATTN:
+                e = lcu_attention_simt((const LcuAttnGroup*)(base + s.table_off), nullptr, nullptr, nullptr, nullptr,
+                                       (size_t)s.count, s.S, s.H, s.D, s.causal, st);
+                break;
+            case S_LN:
+                e = lcu_layernorm_grouped((const LcuRowGroup*)(base + s.table_off), s.count,
+                                          LcuRowGroup{nullptr, nullptr, nullptr, nullptr}, s.rows, s.cols, s.eps, s.vec, st);
+                break;
+            case S_ELT:
+                e = lcu_eltwise_grouped(s.op, (const LcuEltGroup*)(base + s.table_off), s.count, s.n, s.vec, st);
+                break;
+            case S_SOFTMAX: e = lcu_softmax(F(s.out), F(s.in0), s.rows, s.cols, st); break;
+            case S_SUMAX1: e = lcu_sum_axis1(F(s.out), F(s.in0), s.rows, s.cols, st); break;
+            case S_BCAST: e = lcu_broadcast(F(s.out), F(s.in0), s.in_elems, s.rows, s.cols, st); break;
+            case S_CONV:
+                e = lcu_conv2d(F(s.out), F(s.in0), F(s.in1), s.cn, s.ci, s.h, s.w, s.co, s.kh, s.kw, s.stride, s.pad,
+                               s.relu, c->mode, st);
+                break;
+            case S_MAXPOOL: e = lcu_maxpool2d(F(s.out), F(s.in0), s.cn, s.ci, s.h, s.w, s.kh, s.stride, st); break;
+        }
+        if (e != LANCIUS_ERROR_OK) return e;
+    }
+    return LANCIUS_ERROR_OK;
+}
+
+extern "C" void lancius_schedule_execute_cuda(lancius_schedule* s, lcu_ctx* c) {
+    if (!c || !s) { lancius_set_error(LANCIUS_ERROR_NULL_PTR); return; }
+    if (s != c->s || !c->dmem) { lancius_set_error(LANCIUS_ERROR_INVALID_MODEL); return; }
+    cudaSetDevice(c->device);
+    lcu_reset_launch_count();
+    if (!c->replay) {
+        run_steps(c);
+        c->last_launches = lcu_launch_count();
+        return;
+    }
+    if (!c->exec) {
+        cudaGraph_t graph = nullptr;
+        cudaError_t ce = cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal);
+        if (ce != cudaSuccess) { cuda_fail(ce); return; }
+        lancius_error e = run_steps(c);
+        ce = cudaStreamEndCapture(c->stream, &graph);
+        if (e != LANCIUS_ERROR_OK || ce != cudaSuccess) {
+            if (graph) cudaGraphDestroy(graph);
+            if (ce != cudaSuccess) cuda_fail(ce);
+            return;
+        }
+        ce = cudaGraphInstantiate(&c->exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ce != cudaSuccess) { c->exec = nullptr; cuda_fail(ce); return; }
+        c->graph_launches = lcu_launch_count();
+    }
+    cuda_fail(cudaGraphLaunch(c->exec, c->stream));
+    c->last_launches = c->graph_launches;
+}

@@ -1,0 +1,35 @@
+// Internal launcher interface shared by the executor and the per-op C ABI.
+// Group tables (device-resident arrays of per-instance pointers) let one launch
+// cover every same-shaped node of a wave.
+#pragma once
+#include "common.cuh"
+
+struct LcuGemmGroup {        // one independent product C = act(A*B + bias) + resid
+    const float* a;
+    const float* b;
+    float* c;
+    const float* bias;   // [N] row vector added to every row, or NULL
+    const float* resid;  // [M,N] added after the activation, or NULL
+};
+struct LcuAttnGroup { const float* q; const float* k; const float* v; float* o; };
+struct LcuEltGroup { float* out; const float* a; const float* b; };
+struct LcuRowGroup { float* out; const float* in; const float* gamma; const float* beta; };
+
+extern "C" {
+lancius_error lcu_gemm_simt_grouped(const LcuGemmGroup* d_groups, int count, size_t M, size_t N, size_t K, int epi,
+                                    void* stream);
+lancius_error lcu_gemm_simt(float* c, const float* a, const float* b, size_t M, size_t K, size_t N, const float* bias,
+                            int epi, void* stream);
+lancius_error lcu_conv2d_simt(float* out, const float* in, const float* w, size_t N, size_t Ci, size_t H, size_t W,
+                              size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu, void* stream);
+lancius_error lcu_attention_simt(const LcuAttnGroup* d_table, const float* q, const float* k, const float* v, float* o,
+                                 size_t B, size_t S, size_t H, size_t D, int causal, void* stream);
+lancius_error lcu_eltwise_grouped(int op, const LcuEltGroup* d_table, int count, size_t n, int vec, void* s);
+lancius_error lcu_layernorm_grouped(const LcuRowGroup* d_table, int count, LcuRowGroup one, size_t rows, size_t hidden,
+                                    float eps, int vec, void* s);
+lancius_error lcu_copy_f32(float* o, const float* a, size_t n, void* s);
+lancius_error lcu_convert_f64_to_f32(float* o, const double* a, size_t n, void* s);
+lancius_error lcu_convert_f32_to_f64(double* o, const float* a, size_t n, void* s);
+void lcu_reset_launch_count(void);
+int lcu_launch_count(void);
+}

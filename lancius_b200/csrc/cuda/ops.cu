@@ -1,0 +1,45 @@
+// Per-op C ABI (lancius_cuda.h): argument checks and kernel selection.
+#include "lcu_internal.h"
+#include <string.h>
+
+static thread_local int tl_launches = 0;
+extern "C" void lcu_note_launch(void) { tl_launches++; }
+extern "C" void lcu_reset_launch_count(void) { tl_launches = 0; }
+extern "C" int lcu_launch_count(void) { return tl_launches; }
+
+static lancius_error bad(lancius_error e) { lancius_set_error(e); return e; }
+
+extern "C" {
+
+lancius_error lcu_matmul(float* out, const float* a, const float* b, size_t M, size_t K, size_t N, const float* bias,
+                         int epilogue, int mode, void* stream) {
+    if (!out || (K && (!a || !b))) return bad(LANCIUS_ERROR_NULL_PTR);
+    if (epilogue < LCU_EPI_NONE || epilogue > LCU_EPI_GELU) return bad(LANCIUS_ERROR_UNSUPPORTED_OP);
+    if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+    if (M == 0 || N == 0) return LANCIUS_ERROR_OK;
+    // K == 0 is valid: the product is zero, bias and epilogue still apply
+    return lcu_gemm_simt(out, a, b, M, K, N, bias, epilogue, stream);
+}
+
+lancius_error lcu_attention(float* out, const float* q, const float* k, const float* v, size_t B, size_t S, size_t H,
+                            size_t D, int causal, int mode, void* stream) {
+    if (!out || !q || !k || !v) return bad(LANCIUS_ERROR_NULL_PTR);
+    if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+    if (D != 64 && D != 128) return bad(LANCIUS_ERROR_UNSUPPORTED_OP);
+    return lcu_attention_simt(nullptr, q, k, v, out, B, S, H, D, causal ? 1 : 0, stream);
+}
+
+lancius_error lcu_conv2d(float* out, const float* in, const float* w, size_t N, size_t C_in, size_t H_in, size_t W_in,
+                         size_t C_out, size_t K_h, size_t K_w, size_t stride, size_t pad, int relu, int mode,
+                         void* stream) {
+    if (!out || !in || !w) return bad(LANCIUS_ERROR_NULL_PTR);
+    if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+    if (stride == 0 || H_in + 2 * pad < K_h || W_in + 2 * pad < K_w) return bad(LANCIUS_ERROR_SHAPE_MISMATCH);
+    return lcu_conv2d_simt(out, in, w, N, C_in, H_in, W_in, C_out, K_h, K_w, stride, pad, relu, stream);
+}
+
+const char* lcu_build_info(void) {
+    return "lancius_b200 sm_100a: gemm_simt conv_simt attention_simt layernorm softmax sum_axis1 maxpool eltwise";
+}
+
+}  // extern "C"
