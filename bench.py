@@ -1,0 +1,365 @@
+"""Benchmark for the Lancius B200 backend (one JSON line on rank 0).
+
+Default workload: FP32 causal multi-head attention, batch 8
+x seq 512 x 8 heads x head_dim 64 per GPU, built through the Lancius graph API and
+run by lancius_schedule_execute_cuda. Metric: attention GB/s (algorithmic bytes =
+Q,K,V read + O written once, FP32 = 16*B*S*H*D per graph). Weak scaling: every
+rank runs its own batch of 8; there is no data-path collective.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                  [--config attention|mlp|conv|encoder|gemm4096|...]
+"""
+import argparse
+import ctypes as C
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_FLUSH_BYTES = 256 << 20     # > 126 MB L2: written between timed steps
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return {"hbm_gbs": p["hbm_gbs"], "bf16_tflops": p["bf16_tflops"], "src": "measured"}
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+# per-config workload description -------------------------------------------------
+def build(cfg, graph, rank):
+    from lancius_b200 import configs
+    if cfg == "attention":
+        return configs.attention(graph, batch=8, seq=512, heads=8, head_dim=64, seed=1 + 1000 * rank)
+    if cfg == "mlp":
+        return configs.mlp(graph, batch=64, seed=0 + 1000 * rank)
+    if cfg == "conv":
+        return configs.conv_stack(graph, batch=32, hw=224, seed=2 + 1000 * rank)
+    if cfg == "encoder":
+        return configs.encoder(graph, batch=16, seq=512, layers=12, seed=3 + 1000 * rank)
+    if cfg.startswith("gemm"):
+        return configs.gemm(graph, int(cfg[4:]), seed=4 + 1000 * rank)
+    raise SystemExit(f"unknown config {cfg}")
+
+
+METRIC = {
+    "attention": ("attention GB/s", "GB/s", "attention_b8_s512_h8_d64_causal_fp32"),
+    "mlp": ("graph inferences/sec", "graphs/s", "mlp_784_256_10_b64_fp32"),
+    "conv": ("conv stack TFLOP/s", "TFLOP/s", "conv_stack_b32_224_fp32"),
+    "encoder": ("encoder TFLOP/s", "TFLOP/s", "encoder_bert_base_l12_b16_s512_fp32"),
+}
+
+
+def metric_of(cfg, built, seconds_per_graph):
+    if cfg in ("attention",):
+        return built.bytes / seconds_per_graph / 1e9
+    if cfg == "mlp":
+        return 1.0 / seconds_per_graph
+    return built.flops / seconds_per_graph / 1e12   # conv, encoder, gemm: TFLOP/s
+
+
+def metric_names(cfg):
+    if cfg in METRIC:
+        return METRIC[cfg]
+    return ("GEMM TFLOP/s", "TFLOP/s", f"{cfg}_square_fp32")
+
+
+# clocks sampled during the timed region --------------------------------------------
+class Clocks:
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if not self.proc:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# CPU baseline: the reference's own code (oracle/_ref) on this host's cores -----------
+def cpu_baseline(cfg, steps=None):
+    """Times the reference's arena-mode executor on a bounded sample of the workload.
+    Returns (value in the metric's unit, description dict)."""
+    import oracle
+    from lancius_b200 import Graph, configs
+    if not oracle.reference_available():
+        return None
+    ref = oracle.reference()
+    cores = os.cpu_count()
+    if cfg == "attention":
+        # sample: 2 of the 8 batch elements (one ATTENTION node each), scaled per graph
+        g = Graph(ref)
+        b = configs.attention(g, batch=2, seq=512, heads=8, head_dim=64, seed=1)
+        b.bind_host()
+        t0 = time.perf_counter()
+        reps = 0
+        while True:
+            oracle.run_reference_graph(ref, g, b.outputs[:1])
+            reps += 1
+            if time.perf_counter() - t0 > 3.0 or (steps and reps >= steps):
+                break
+        sec = (time.perf_counter() - t0) / reps * 4.0    # 2 elements -> 8
+        val = 16.0 * 8 * 512 * 512 / sec / 1e9
+        return val, {"kind": "reference", "cores": cores,
+                     "sample": f"{reps} runs of 2 of 8 batch elements (S512 H8 D64 causal) through "
+                               "lancius_schedule_execute, scaled x4 to one batch-8 graph; "
+                               f"OMP threads = {os.environ.get('OMP_NUM_THREADS', cores)}"}
+    return None
+
+
+# the B200 arm -----------------------------------------------------------------------
+def run_b200(args, rank, world, local_rank):
+    import torch
+    import lancius_b200 as L
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+
+    dev = L.Device(local_rank)
+    g = L.Graph()
+    built = build(args.config, g, rank)
+    sched = g.schedule()
+    dev.set_graph_replay(True)
+    dev.bind(sched)
+    for node, arr in built.inputs:
+        dev.upload(node, arr)
+
+    ext = torch.cuda.ExternalStream(dev.stream)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+
+    def step_device(ev0, ev1):
+        with torch.cuda.stream(ext):
+            flush.fill_(1.0)                 # evict L2 between timed steps
+            ev0.record(ext)
+        dev.execute(sched)
+        with torch.cuda.stream(ext):
+            ev1.record(ext)
+
+    for _ in range(args.warmup):
+        step_device(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+    torch.cuda.synchronize()
+
+    clocks = Clocks(local_rank)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks.start()
+    for e0, e1 in evs:
+        step_device(e0, e1)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clk = clocks.stop()
+    dev_ms = [e0.elapsed_time(e1) for e0, e1 in evs]
+    launches_per_step = dev.last_launch_count
+    total_ms = sum(dev_ms)
+
+    # e2e through the public API with pinned host buffers: H2D inputs, execute, D2H outputs
+    in_bytes = sum(arr.size * 4 for _, arr in built.inputs if _is_activation(args.config, _))
+    hosts_in = []
+    for node, arr in built.inputs:
+        if not _is_activation(args.config, node):
+            continue
+        p = dev.lib.lcu_host_alloc(arr.size * 4)
+        np.ctypeslib.as_array(C.cast(p, C.POINTER(C.c_float)), shape=(arr.size,))[:] = arr.ravel()
+        hosts_in.append((node, p))
+    hosts_out = [(o, dev.lib.lcu_host_alloc(o.size * 4)) for o in built.outputs]
+    out_bytes = sum(o.size * 4 for o in built.outputs)
+
+    def step_e2e():
+        for node, p in hosts_in:
+            dev.upload_ptr(node, p, 2)
+        dev.execute(sched)
+        for node, p in hosts_out:
+            dev.download_ptr(node, p, 2)      # synchronous: waits for the result
+
+    for _ in range(max(1, args.warmup)):
+        step_e2e()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for _ in range(args.steps):
+        step_e2e()
+    e1.record(ext)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        dist.barrier()
+    for _, p in hosts_in + hosts_out:
+        dev.lib.lcu_host_free(p)
+
+    if dist:
+        t = torch.tensor([total_ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = t.tolist()
+    return built, total_ms, e2e_ms, dev_ms, launches_per_step, clk, in_bytes, out_bytes, dist
+
+
+def _is_activation(cfg, node):
+    # per-step inputs (weights stay resident): attention Q/K/V, conv/mlp/encoder X, gemm A and B
+    return True if cfg in ("attention",) or cfg.startswith("gemm") else node.id == 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--config", default="attention")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+    metric, unit, workload = metric_names(args.config)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        res = reference_arm(args, metric, unit, workload)
+        print(json.dumps(res))
+        return
+
+    built, total_ms, e2e_ms, dev_ms, launches, clk, in_b, out_b, dist = run_b200(args, rank, world, local_rank)
+    if rank != 0:
+        if dist:
+            dist.destroy_process_group()
+        return
+    sec_per_graph = total_ms / 1e3 / args.steps
+    value = metric_of(args.config, built, sec_per_graph) * world
+    e2e_val = metric_of(args.config, built, e2e_ms / 1e3 / args.steps) * world
+    pk = peaks()
+    roof = None
+    if args.config == "attention":
+        achieved = built.bytes / (sec_per_graph) / 1e9
+        roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                "kernel": "attention (one grouped launch over the 8 ATTENTION nodes)",
+                "peak_src": pk["src"] + " hbm_gbs (burst copy)"}
+    else:
+        achieved = built.flops / sec_per_graph / 1e12
+        roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": None, "peak_src": pk["src"] + " bf16"}
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        try:
+            r = cpu_baseline(args.config)
+            if r:
+                cpu = dict(value=round(r[0], 4), unit=unit, **r[1])
+        except Exception as ex:  # the baseline is reported, never required
+            cpu = {"error": str(ex)[:200]}
+    line = {
+        "metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), splitmix64)",
+        "config": {"workload": workload, "per_gpu_batch": built.meta.get("batch"), "mode": "fp32_exact",
+                   "l2": "flushed between timed steps (256 MiB write)", "parallelism": f"batch-sharded x{world}"},
+        "roofline": roof,
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_val, 3), "unit": unit, "h2d_bytes_per_step": in_b, "d2h_bytes_per_step": out_b},
+        "gpu_launches": launches * args.steps,
+        "clocks": clk,
+        "step_ms_min_max": [round(min(dev_ms), 5), round(max(dev_ms), 5)],
+    }
+    print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+
+
+def reference_arm(args, metric, unit, workload):
+    import oracle
+    from lancius_b200 import Graph, configs
+    if not oracle.reference_available():
+        return {"impl": "reference", "unavailable": "oracle/_ref/liblancius_ref.so was not built"}
+    if args.config != "attention":
+        return {"impl": "reference", "unavailable": f"reference arm implemented for the attention workload only"}
+    ref = oracle.reference()
+    g = Graph(ref)
+    b = configs.attention(g, batch=8, seq=512, heads=8, head_dim=64, seed=1)
+    b.bind_host()
+    sched = ref.lancius_ir_schedule(g.ptr)
+    arena = ref.lancius_arena_create(256 << 20)
+    times = []
+    # the executor recomputes every node on every call; buffers from the first call are reused
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        ref.lancius_schedule_execute(sched, arena)
+        t1 = time.perf_counter()
+        if i >= args.warmup:
+            times.append(t1 - t0)
+    ref.lancius_arena_destroy(arena)
+    ref.lancius_schedule_destroy(sched)
+    sec = sum(times) / len(times)
+    val = b.bytes / sec / 1e9
+    cores = os.cpu_count()
+    return {"impl": "reference", "metric": metric, "value": round(val, 4), "unit": unit, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded N(0,1), splitmix64)",
+            "config": {"workload": workload, "per_gpu_batch": 8, "executor": "lancius_schedule_execute (arena mode)"},
+            "cpu_baseline": {"value": round(val, 4), "unit": unit, "kind": "reference", "cores": cores,
+                             "sample": "the full batch-8 graph per step on the host CPU, reference C sources "
+                                       "compiled by oracle/Makefile; OpenMP threads = all host cores"},
+            "e2e": {"value": round(val, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+if __name__ == "__main__":
+    main()
