@@ -34,6 +34,8 @@ struct Step {
     size_t table_off = 0;      // byte offset of the group table inside the allocation
     size_t M = 0, N = 0, K = 0;
     int epi = 0, op = 0, vec = 0, causal = 0, relu = 0;
+    int tc = 0, gb = 1;        // tensor-core GEMM; distinct B operands in the group
+    int plan_idx = -1, plan_mode = -1;
     size_t S = 0, H = 0, D = 0;
     size_t cn = 0, ci = 0, h = 0, w = 0, co = 0, kh = 0, kw = 0, stride = 0, pad = 0;
     size_t out = 0, in0 = 0, in1 = 0;   // node offsets for single-instance steps
@@ -63,6 +65,9 @@ struct lcu_ctx {
     size_t dmem_bytes = 0;
     double* staging = nullptr;
     size_t staging_elems = 0;
+    void* scratch = nullptr;            // tensor-core GEMM hi/lo operand copies
+    size_t scratch_bytes = 0;
+    std::vector<LcuTcGemmPlan> tc_plans;
     std::vector<size_t> off;            // node id -> byte offset in dmem (NPOS: no storage)
     std::vector<Step> steps;
     cudaGraphExec_t exec = nullptr;
@@ -77,7 +82,9 @@ static void release_binding(lcu_ctx* c) {
     if (c->exec) { cudaGraphExecDestroy(c->exec); c->exec = nullptr; }
     if (c->dmem) { cudaFree(c->dmem); c->dmem = nullptr; }
     if (c->staging) { cudaFree(c->staging); c->staging = nullptr; }
-    c->dmem_bytes = 0; c->staging_elems = 0;
+    if (c->scratch) { cudaFree(c->scratch); c->scratch = nullptr; }
+    c->dmem_bytes = 0; c->staging_elems = 0; c->scratch_bytes = 0;
+    c->tc_plans.clear();
     c->off.clear(); c->steps.clear();
     c->g = nullptr; c->s = nullptr;
 }
@@ -312,6 +319,19 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                     st.kind = S_GEMM;
                     st.M = n->shape[0]; st.N = n->shape[1]; st.K = n->inputs[0]->shape[n->inputs[0]->ndim - 1];
                     st.epi = b.chain[n->id].epi;
+                    st.tc = lcu_use_tensor_cores(st.M, st.N, st.K);
+                    st.gb = ns.size();
+                    {
+                        bool shared_b = true;
+                        for (const lancius_node* x : ns) shared_b &= x->inputs[1] == n->inputs[1];
+                        if (shared_b) st.gb = 1;
+                    }
+                    if (st.tc) {
+                        size_t need = lcu_gemm_tc_scratch_bytes(st.M, st.N, st.K, st.count, st.gb, 3);
+                        if (need > c->scratch_bytes) c->scratch_bytes = need;
+                        st.plan_idx = (int)c->tc_plans.size();
+                        c->tc_plans.push_back(LcuTcGemmPlan());
+                    }
                     std::vector<LcuGemmGroup> t;
                     for (const lancius_node* x : ns) {
                         const Chain& ch = b.chain[x->id];
@@ -483,6 +503,10 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
         ce = cudaMemcpyAsync(c->dmem + table_base, b.tables.data(), b.tables.size(), cudaMemcpyHostToDevice, c->stream);
         if (ce != cudaSuccess) { release_binding(c); return cuda_fail(ce); }
     }
+    if (c->scratch_bytes) {
+        ce = cudaMalloc(&c->scratch, c->scratch_bytes);
+        if (ce != cudaSuccess) { cudaGetLastError(); release_binding(c); return fail(LANCIUS_ERROR_OOM); }
+    }
     ce = cudaMalloc(&c->staging, (max_io ? max_io : 1) * sizeof(double));
     if (ce != cudaSuccess) { cudaGetLastError(); release_binding(c); return fail(LANCIUS_ERROR_OOM); }
     c->staging_elems = max_io;
@@ -575,7 +599,17 @@ static lancius_error run_steps(lcu_ctx* c) {
         lancius_error e = LANCIUS_ERROR_OK;
         switch (s.kind) {
             case S_GEMM:
-                e = lcu_gemm_simt_grouped((const LcuGemmGroup*)(base + s.table_off), s.count, s.M, s.N, s.K, s.epi, st);
+                if (s.tc) {
+                    LcuTcGemmPlan& p = c->tc_plans[s.plan_idx];
+                    int passes = c->mode == LCU_MODE_TF32 ? 1 : 3;
+                    if (p.passes != passes || p.M != s.M) {
+                        e = lcu_gemm_tc_prepare(&p, c->scratch, s.M, s.N, s.K, s.count, s.gb, passes);
+                        if (e != LANCIUS_ERROR_OK) break;
+                    }
+                    e = lcu_gemm_tc_run(&p, (const LcuGemmGroup*)(base + s.table_off), s.epi, st);
+                } else {
+                    e = lcu_gemm_simt_grouped((const LcuGemmGroup*)(base + s.table_off), s.count, s.M, s.N, s.K, s.epi, st);
+                }
                 break;
             case S_ATTN:
                 e = lcu_attention_simt((const LcuAttnGroup*)(base + s.table_off), nullptr, nullptr, nullptr, nullptr,

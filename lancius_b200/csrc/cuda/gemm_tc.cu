@@ -1,0 +1,397 @@
+// FP32 GEMM on the 5th-generation tensor cores (tcgen05, kind::tf32) with the
+// 3xTF32 split for FP32-exact results:
+//     A*B ~= Ahi*Bhi + Ahi*Blo + Alo*Bhi,   hi = rna_tf32(x), lo = x - hi,
+// accumulated in FP32 in TMEM. A split pass writes hi/lo copies of both operands
+// into scratch with 16-byte-aligned row pitches (any M, N, K is then TMA-legal);
+// the GEMM kernel streams them with TMA through a 4-stage mbarrier ring:
+//
+//   warp 0      TMA producer (one elected lane)
+//   warp 1      TMEM allocation + tcgen05.mma issue (one lane)
+//   warps 2-5   epilogue: tcgen05.ld -> +bias -> ReLU/GELU -> +residual -> global
+//
+// Tile 128 x 256 x 16: A K-major in 64-byte swizzle, B N-major in the 128-byte
+// swizzle with 32-byte atoms (the only N-major layout tcgen05 accepts for TF32;
+// eight 32-column chunks), accumulator 128 lanes x 256 TMEM columns.
+// Every mbarrier wait is bounded (tc::kSpinLimit); a timeout sets the watchdog
+// word, unwinds the CTA and frees its TMEM.
+#include "tc_common.cuh"
+#include <cstdio>
+#ifndef LCU_GEMM_DEBUG
+#define LCU_GEMM_DEBUG 0
+#endif
+#include <mutex>
+#include <vector>
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4, THREADS = 192;
+constexpr int A_TILE = BM * BK * 4;                  // 8 KB
+constexpr int B_CHUNK = BK * 32 * 4;                 // 2 KB: 16 k-rows x 32 n
+constexpr int B_TILE = BN * BK * 4;                  // 16 KB
+constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE; // 48 KB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr uint32_t TMEM_COLS = 256;
+
+__device__ int g_gemm_watchdog = 0;
+
+struct Smem {
+    uint64_t full[STAGES];
+    uint64_t empty[STAGES];
+    uint64_t accum;
+    uint64_t drain;
+    uint32_t tmem_base;
+    int abort;
+    int consumed;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
+          const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
+          const LcuGemmGroup* __restrict__ groups, int M, int N, int K, int epi, int passes, int b_shared,
+          int splits, int kchunk, float* __restrict__ partial) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Smem* sm = reinterpret_cast<Smem*>(tiles + STAGES * STAGE_BYTES);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // blockIdx.z = group * splits + split; a split covers k in [k_begin, k_begin + kchunk)
+    const int g = blockIdx.z / splits, split = blockIdx.z % splits, gb = b_shared ? 0 : g;
+    const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+    const int k_begin = split * kchunk;
+    const int k_end = min(K, k_begin + kchunk);
+    const int KT = (k_end - k_begin + BK - 1) / BK;
+    volatile int* abort = &sm->abort;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) { tc::mbar_init(&sm->full[s], 1); tc::mbar_init(&sm->empty[s], 1); }
+        tc::mbar_init(&sm->accum, 1);
+        tc::mbar_init(&sm->drain, 1);
+        sm->abort = 0;
+        sm->consumed = 0;
+        tc::fence_barrier_init();
+        tc::prefetch_tmap(&ta_hi); tc::prefetch_tmap(&tb_hi);
+        if (passes > 1) { tc::prefetch_tmap(&ta_lo); tc::prefetch_tmap(&tb_lo); }
+    }
+    if (warp == 1) tc::tmem_alloc(&sm->tmem_base, TMEM_COLS);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = sm->tmem_base;
+    int issued = 0;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer ----------------
+        const uint32_t tx = passes > 1 ? STAGE_BYTES : A_TILE + B_TILE;
+        for (int kt = 0; kt < KT; kt++) {
+            int s = kt % STAGES;
+            if (kt >= STAGES && !tc::mbar_wait(&sm->empty[s], ((kt / STAGES) - 1) & 1, abort, &g_gemm_watchdog, 1)) break;
+            uint8_t* st = tiles + s * STAGE_BYTES;
+            tc::mbar_expect_tx(&sm->full[s], tx);
+            int k0 = k_begin + kt * BK;
+            tc::tma_load_3d(st, &ta_hi, &sm->full[s], k0, m0, g);
+            for (int j = 0; j < BN / 32; j++)
+                tc::tma_load_3d(st + 2 * A_TILE + j * B_CHUNK, &tb_hi, &sm->full[s], n0 + 32 * j, k0, gb);
+            if (passes > 1) {
+                tc::tma_load_3d(st + A_TILE, &ta_lo, &sm->full[s], k0, m0, g);
+                for (int j = 0; j < BN / 32; j++)
+                    tc::tma_load_3d(st + 2 * A_TILE + B_TILE + j * B_CHUNK, &tb_lo, &sm->full[s], n0 + 32 * j, k0, gb);
+            }
+            issued = kt + 1;
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer ----------------
+        constexpr uint32_t idesc = tc::idesc_tf32(BM, BN, false, true);
+        bool ok = true;
+        for (int kt = 0; kt < KT && ok; kt++) {
+            int s = kt % STAGES;
+            if (!tc::mbar_wait(&sm->full[s], (kt / STAGES) & 1, abort, &g_gemm_watchdog, 2)) { ok = false; break; }
+            tc::tc_fence_after();
+            if (LCU_GEMM_DEBUG && blockIdx.x == 0 && blockIdx.y == 0 && kt == 0) {
+                const float* fa = reinterpret_cast<const float*>(tiles + s * STAGE_BYTES);
+                const float* fb = reinterpret_cast<const float*>(tiles + s * STAGE_BYTES + 2 * A_TILE);
+                printf("tmem=%08x A[0..7]=%g %g %g %g %g %g %g %g  A[16..19]=%g %g %g %g\n", tmem, fa[0], fa[1], fa[2], fa[3], fa[4], fa[5], fa[6], fa[7], fa[16], fa[17], fa[18], fa[19]);
+                printf("B[0..7]=%g %g %g %g %g %g %g %g B[32..35]=%g %g %g %g B[512]=%g\n", fb[0], fb[1], fb[2], fb[3], fb[4], fb[5], fb[6], fb[7], fb[32], fb[33], fb[34], fb[35], fb[512]);
+            }
+            uint32_t st = tc::smem_u32(tiles + s * STAGE_BYTES);
+            uint32_t a_hi = st, a_lo = st + A_TILE, b_hi = st + 2 * A_TILE, b_lo = st + 2 * A_TILE + B_TILE;
+#pragma unroll
+            for (int kb = 0; kb < BK / 8; kb++) {
+                uint64_t dah = tc::smem_desc(a_hi + kb * 32, 16, 512, tc::SWZ_64B);
+                uint64_t dbh = tc::smem_desc(b_hi + kb * 1024, B_CHUNK, 512, tc::SWZ_128B_BASE32B);
+                uint32_t acc = (kt | kb) ? 1u : 0u;
+                if (passes > 1) {
+                    uint64_t dal = tc::smem_desc(a_lo + kb * 32, 16, 512, tc::SWZ_64B);
+                    uint64_t dbl = tc::smem_desc(b_lo + kb * 1024, B_CHUNK, 512, tc::SWZ_128B_BASE32B);
+                    tc::mma_tf32(tmem, dal, dbh, idesc, acc);      // small terms first
+                    tc::mma_tf32(tmem, dah, dbl, idesc, 1u);
+                    tc::mma_tf32(tmem, dah, dbh, idesc, 1u);
+                } else {
+                    tc::mma_tf32(tmem, dah, dbh, idesc, acc);
+                }
+            }
+            tc::mma_commit(&sm->empty[s]);          // stage s is free once these MMAs retire
+            sm->consumed = kt + 1;
+        }
+        if (ok) tc::mma_commit(&sm->accum);
+    } else if (warp >= 2) {
+        // ---------------- epilogue ----------------
+        if (tc::mbar_wait(&sm->accum, 0, abort, &g_gemm_watchdog, 3)) {
+            tc::tc_fence_after();
+            LcuGemmGroup gr = groups[g];
+            if (splits > 1) {   // raw partial sums; the reduction applies the epilogue
+                gr.c = partial + (size_t)blockIdx.z * M * N;
+                gr.bias = nullptr; gr.resid = nullptr;
+            }
+            const int epi_here = splits > 1 ? LCU_EPI_NONE : epi;
+            const int q = warp & 3;                    // TMEM lane quadrant of this warp
+            const int row = m0 + 32 * q + lane;
+            const bool vec = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(gr.c) & 15) == 0) &&
+                             (!gr.resid || (reinterpret_cast<uintptr_t>(gr.resid) & 15) == 0);
+            for (int c = 0; c < BN; c += 32) {
+                if (n0 + c >= N) break;                // warp-uniform
+                float v[32];
+                tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
+                if (LCU_GEMM_DEBUG && blockIdx.x == 0 && blockIdx.y == 0 && c == 0 && (lane == 0 || lane == 1) && q == 0)
+                    printf("row %d v=%g %g %g %g %g %g\n", row, v[0], v[1], v[2], v[3], v[4], v[5]);
+                if (row >= M) continue;
+                const int col0 = n0 + c;
+                float* dst = gr.c + (size_t)row * N + col0;
+                const float* res = gr.resid ? gr.resid + (size_t)row * N + col0 : nullptr;
+                if (vec && col0 + 32 <= N) {
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4) {
+                        float4 o;
+                        float* ov = reinterpret_cast<float*>(&o);
+#pragma unroll
+                        for (int t = 0; t < 4; t++) {
+                            float x = v[j + t];
+                            if (gr.bias) x += __ldg(gr.bias + col0 + j + t);
+                            ov[t] = lcu_apply_epi(x, epi_here);
+                        }
+                        if (res) {
+                            float4 r = *reinterpret_cast<const float4*>(res + j);
+                            o.x += r.x; o.y += r.y; o.z += r.z; o.w += r.w;
+                        }
+                        *reinterpret_cast<float4*>(dst + j) = o;
+                    }
+                } else {
+                    for (int j = 0; j < 32 && col0 + j < N; j++) {
+                        float x = v[j];
+                        if (gr.bias) x += __ldg(gr.bias + col0 + j);
+                        x = lcu_apply_epi(x, epi_here);
+                        if (res) x += res[j];
+                        dst[j] = x;
+                    }
+                }
+            }
+        }
+    }
+
+    tc::tc_fence_before();
+    __syncthreads();
+    if (sm->abort) {
+        // unwind: let in-flight TMA copies land and in-flight MMAs retire before the
+        // CTA's shared memory and TMEM go away (both waits bounded as well)
+        int never = 0;
+        if (warp == 0 && lane == 0)
+            for (int kt = sm->consumed; kt < issued; kt++)
+                if (!tc::mbar_wait(&sm->full[kt % STAGES], (kt / STAGES) & 1, &never, nullptr, 0)) break;
+        if (warp == 1 && lane == 0) {
+            tc::mma_commit(&sm->drain);
+            tc::mbar_wait(&sm->drain, 0, &never, nullptr, 0);
+        }
+        __syncthreads();
+    }
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// hi/lo split of `count` row-major [rows, cols] operands into pitched scratch
+__global__ void k_split(const LcuGemmGroup* __restrict__ groups, int which, size_t rows, size_t cols, size_t pitch,
+                        float* __restrict__ hi, float* __restrict__ lo) {
+    const float* src = which == 0 ? groups[blockIdx.y].a : groups[blockIdx.y].b;
+    size_t base = (size_t)blockIdx.y * rows * pitch;
+    size_t n = rows * cols;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        size_t r = i / cols, c = i % cols;
+        float x = src[i];
+        float h = tc::tf32_rna(x);
+        hi[base + r * pitch + c] = h;
+        if (lo) lo[base + r * pitch + c] = tc::tf32_rna(x - h);   // TF32-exact: no truncation bias in the MMA
+    }
+}
+
+// out = act(sum over splits of the partials + bias) + resid, splits summed in order
+__global__ void k_splitk_reduce(const LcuGemmGroup* __restrict__ groups, const float* __restrict__ partial, int splits,
+                                size_t M, size_t N, int epi) {
+    const LcuGemmGroup gr = groups[blockIdx.y];
+    const float* p = partial + (size_t)blockIdx.y * splits * M * N;
+    size_t n = M * N;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        float acc = 0.f;
+        for (int s = 0; s < splits; s++) acc += p[(size_t)s * n + i];
+        if (gr.bias) acc += __ldg(gr.bias + i % N);
+        acc = lcu_apply_epi(acc, epi);
+        if (gr.resid) acc += gr.resid[i];
+        gr.c[i] = acc;
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+// 3D map over [G][rows][pitch] floats, box {box_inner, box_rows, 1}
+bool make_map(CUtensorMap* m, const float* base, size_t inner, size_t rows, size_t groups, size_t pitch,
+              uint32_t box_inner, uint32_t box_rows, CUtensorMapSwizzle swz) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {inner, rows, groups};
+    cuuint64_t strides[2] = {pitch * 4, rows * pitch * 4};
+    cuuint32_t box[3] = {box_inner, box_rows, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t pad4(size_t v) { return (v + 3) & ~size_t(3); }
+size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// Prepared launch: tensor maps over a scratch region, built once (the executor
+// binds them at plan time; the per-op entry point builds them per call).
+
+// K is cut into chunks of at most kMaxChunk: the tensor core's FP32 accumulation
+// error grows with the reduction length, and per-chunk partials summed in FP32 keep
+// the 3xTF32 result within 1e-4 at K = 16384 (measured normwise: 3e-5 at K = 4096,
+// 6.3e-5 at 8192, 1.1e-4 at 16384 without the split, 3e-5 with 4096-chunks).
+constexpr int kMaxChunk = 8192;
+int split_count(size_t K) { return K > (size_t)kMaxChunk ? (int)((K + kMaxChunk - 1) / kMaxChunk) : 1; }
+
+extern "C" size_t lcu_gemm_tc_scratch_bytes(size_t M, size_t N, size_t K, int G, int Gb, int passes) {
+    size_t a = al256((size_t)G * M * pad4(K) * 4), b = al256((size_t)Gb * K * pad4(N) * 4);
+    int sp = split_count(K);
+    size_t part = sp > 1 ? al256((size_t)G * sp * M * N * 4) : 0;
+    return (passes > 1 ? 2 * (a + b) : a + b) + part;
+}
+
+extern "C" lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, size_t M, size_t N, size_t K, int G,
+                                             int Gb, int passes) {
+    p->M = M; p->N = N; p->K = K; p->Kp = pad4(K); p->Np = pad4(N); p->G = G; p->Gb = Gb; p->passes = passes;
+    size_t a = al256((size_t)G * M * p->Kp * 4), b = al256((size_t)Gb * K * p->Np * 4);
+    char* s = static_cast<char*>(scratch);
+    p->s_ahi = (float*)s; s += a;
+    p->s_bhi = (float*)s; s += b;
+    p->s_alo = passes > 1 ? (float*)s : nullptr; if (passes > 1) s += a;
+    p->s_blo = passes > 1 ? (float*)s : nullptr; if (passes > 1) s += b;
+    p->splits = split_count(K);
+    p->kchunk = p->splits > 1 ? (int)(((K + p->splits - 1) / p->splits + BK - 1) / BK * BK) : (int)(K ? K : 1);
+    p->partial = p->splits > 1 ? (float*)s : nullptr;
+    bool ok = make_map(&p->a_hi, p->s_ahi, K, M, G, p->Kp, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B) &&
+              make_map(&p->b_hi, p->s_bhi, N, K, Gb, p->Np, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    if (ok && passes > 1)
+        ok = make_map(&p->a_lo, p->s_alo, K, M, G, p->Kp, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B) &&
+             make_map(&p->b_lo, p->s_blo, N, K, Gb, p->Np, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    else if (ok) { p->a_lo = p->a_hi; p->b_lo = p->b_hi; }
+    if (!ok) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    return LANCIUS_ERROR_OK;
+}
+
+extern "C" lancius_error lcu_gemm_tc_run(const LcuTcGemmPlan* p, const LcuGemmGroup* d_groups, int epi, void* stream) {
+    static bool configured = false;
+    if (!configured) {
+        if (cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+            return lcu_launch_status();
+        configured = true;
+    }
+    cudaStream_t st = lcu_as_stream(stream);
+    float* lo_a = p->passes > 1 ? p->s_alo : nullptr;
+    float* lo_b = p->passes > 1 ? p->s_blo : nullptr;
+    if (p->K > 0) {
+        k_split<<<dim3(lcu_blocks(p->M * p->K, 256 * 8, 148 * 4), p->G), 256, 0, st>>>(d_groups, 0, p->M, p->K, p->Kp, p->s_ahi, lo_a);
+        lcu_note_launch();
+        k_split<<<dim3(lcu_blocks(p->K * p->N, 256 * 8, 148 * 4), p->Gb), 256, 0, st>>>(d_groups, 1, p->K, p->N, p->Np, p->s_bhi, lo_b);
+        lcu_note_launch();
+    }
+    dim3 grid((unsigned)((p->N + BN - 1) / BN), (unsigned)((p->M + BM - 1) / BM), (unsigned)(p->G * p->splits));
+    k_gemm_tc<<<grid, THREADS, SMEM_BYTES, st>>>(p->a_hi, p->a_lo, p->b_hi, p->b_lo, d_groups, (int)p->M, (int)p->N,
+                                                 (int)p->K, epi, p->passes, p->Gb == 1 && p->G > 1 ? 1 : 0,
+                                                 p->splits, p->kchunk, p->partial);
+    lcu_note_launch();
+    if (p->splits > 1) {
+        k_splitk_reduce<<<dim3(lcu_blocks(p->M * p->N, 256 * 4, 148 * 8), p->G), 256, 0, st>>>(d_groups, p->partial, p->splits,
+                                                                                               p->M, p->N, epi);
+        lcu_note_launch();
+    }
+    return lcu_launch_status();
+}
+
+// Watchdog word of the tensor-core kernels: 0 = no timeout, else the role that gave up.
+extern "C" int lcu_gemm_watchdog_read_and_clear(void) {
+    int v = 0, z = 0;
+    cudaMemcpyFromSymbol(&v, g_gemm_watchdog, sizeof(int));
+    if (v) cudaMemcpyToSymbol(g_gemm_watchdog, &z, sizeof(int));
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// Per-op entry: scratch comes from a per-device cache that grows on demand.
+
+namespace {
+struct ScratchCache { void* p = nullptr; size_t bytes = 0; };
+std::mutex g_scratch_mu;
+std::vector<ScratchCache> g_scratch;
+}
+
+extern "C" void* lcu_scratch_acquire(size_t bytes) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    if ((int)g_scratch.size() <= dev) g_scratch.resize(dev + 1);
+    ScratchCache& c = g_scratch[dev];
+    if (c.bytes < bytes) {
+        if (c.p) { cudaDeviceSynchronize(); cudaFree(c.p); c.p = nullptr; c.bytes = 0; }
+        if (cudaMalloc(&c.p, bytes) != cudaSuccess) { cudaGetLastError(); c.p = nullptr; return nullptr; }
+        c.bytes = bytes;
+    }
+    return c.p;
+}
+
+extern "C" lancius_error lcu_gemm_tc(float* c, const float* a, const float* b, size_t M, size_t K, size_t N,
+                                     const float* bias, int epi, int mode, void* stream) {
+    int passes = mode == LCU_MODE_TF32 ? 1 : 3;
+    size_t need = lcu_gemm_tc_scratch_bytes(M, N, K, 1, 1, passes) + 256;
+    char* scratch = static_cast<char*>(lcu_scratch_acquire(need));
+    if (!scratch) { lancius_set_error(LANCIUS_ERROR_OOM); return LANCIUS_ERROR_OOM; }
+    // the one-entry group table lives at the end of the scratch region
+    LcuGemmGroup* d_group = reinterpret_cast<LcuGemmGroup*>(scratch + need - 256);
+    LcuGemmGroup h{a, b, c, bias, nullptr};
+    cudaStream_t st = lcu_as_stream(stream);
+    cudaError_t ce = cudaMemcpyAsync(d_group, &h, sizeof(h), cudaMemcpyHostToDevice, st);
+    if (ce != cudaSuccess) return lcu_check_cuda(ce);
+    LcuTcGemmPlan p;
+    lancius_error e = lcu_gemm_tc_prepare(&p, scratch, M, N, K, 1, 1, passes);
+    if (e != LANCIUS_ERROR_OK) return e;
+    e = lcu_gemm_tc_run(&p, d_group, epi, stream);
+    // the host-side group record must stay valid until the copy ran
+    if (e == LANCIUS_ERROR_OK) e = lcu_check_cuda(cudaStreamSynchronize(st));
+    return e;
+}

@@ -3,6 +3,7 @@
 // cover every same-shaped node of a wave.
 #pragma once
 #include "common.cuh"
+#include <cuda.h>
 
 struct LcuGemmGroup {        // one independent product C = act(A*B + bias) + resid
     const float* a;
@@ -15,7 +16,20 @@ struct LcuAttnGroup { const float* q; const float* k; const float* v; float* o; 
 struct LcuEltGroup { float* out; const float* a; const float* b; };
 struct LcuRowGroup { float* out; const float* in; const float* gamma; const float* beta; };
 
+// A prepared tensor-core GEMM: TMA maps over the hi/lo scratch copies of A and B.
+struct LcuTcGemmPlan {
+    CUtensorMap a_hi, a_lo, b_hi, b_lo;
+    float *s_ahi, *s_alo, *s_bhi, *s_blo;
+    size_t M, N, K, Kp, Np;
+    int G, Gb, passes;
+    int splits, kchunk;          // K cut into `splits` chunks of kchunk (multiple of 16)
+    float* partial;              // [G][splits][M][N] partial sums when splits > 1
+};
+
 extern "C" {
+size_t lcu_gemm_tc_scratch_bytes(size_t M, size_t N, size_t K, int G, int Gb, int passes);
+lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, size_t M, size_t N, size_t K, int G, int Gb, int passes);
+lancius_error lcu_gemm_tc_run(const LcuTcGemmPlan* p, const LcuGemmGroup* d_groups, int epi, void* stream);
 lancius_error lcu_gemm_simt_grouped(const LcuGemmGroup* d_groups, int count, size_t M, size_t N, size_t K, int epi,
                                     void* stream);
 lancius_error lcu_gemm_simt(float* c, const float* a, const float* b, size_t M, size_t K, size_t N, const float* bias,
@@ -30,6 +44,10 @@ lancius_error lcu_layernorm_grouped(const LcuRowGroup* d_table, int count, LcuRo
 lancius_error lcu_copy_f32(float* o, const float* a, size_t n, void* s);
 lancius_error lcu_convert_f64_to_f32(float* o, const double* a, size_t n, void* s);
 lancius_error lcu_convert_f32_to_f64(double* o, const float* a, size_t n, void* s);
+lancius_error lcu_gemm_tc(float* c, const float* a, const float* b, size_t M, size_t K, size_t N, const float* bias,
+                          int epi, int mode, void* stream);
+int lcu_gemm_watchdog_read_and_clear(void);
+int lcu_use_tensor_cores(size_t M, size_t N, size_t K);
 void lcu_reset_launch_count(void);
 int lcu_launch_count(void);
 }

@@ -1,11 +1,25 @@
 // Per-op C ABI (lancius_cuda.h): argument checks and kernel selection.
 #include "lcu_internal.h"
 #include <string.h>
+#include <stdlib.h>
 
 static thread_local int tl_launches = 0;
 extern "C" void lcu_note_launch(void) { tl_launches++; }
 extern "C" void lcu_reset_launch_count(void) { tl_launches = 0; }
 extern "C" int lcu_launch_count(void) { return tl_launches; }
+
+// Tensor-core path from 2^24 multiply-adds up (below that the CUDA-core kernel's
+// single launch beats split + GEMM); LCU_FORCE_SIMT=1 / LCU_FORCE_TC=1 override.
+extern "C" int lcu_use_tensor_cores(size_t M, size_t N, size_t K) {
+    static int force = -1;
+    if (force < 0) {
+        const char* s = getenv("LCU_FORCE_SIMT");
+        const char* t = getenv("LCU_FORCE_TC");
+        force = (s && s[0] == '1') ? 0 : (t && t[0] == '1') ? 1 : 2;
+    }
+    if (force != 2) return force && K > 0;
+    return K > 0 && (double)M * (double)N * (double)K >= 16777216.0;
+}
 
 static lancius_error bad(lancius_error e) { lancius_set_error(e); return e; }
 
@@ -18,6 +32,7 @@ lancius_error lcu_matmul(float* out, const float* a, const float* b, size_t M, s
     if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
     if (M == 0 || N == 0) return LANCIUS_ERROR_OK;
     // K == 0 is valid: the product is zero, bias and epilogue still apply
+    if (lcu_use_tensor_cores(M, N, K)) return lcu_gemm_tc(out, a, b, M, K, N, bias, epilogue, mode, stream);
     return lcu_gemm_simt(out, a, b, M, K, N, bias, epilogue, stream);
 }
 
@@ -39,7 +54,7 @@ lancius_error lcu_conv2d(float* out, const float* in, const float* w, size_t N, 
 }
 
 const char* lcu_build_info(void) {
-    return "lancius_b200 sm_100a: gemm_simt conv_simt attention_simt layernorm softmax sum_axis1 maxpool eltwise";
+    return "lancius_b200 sm_100a: gemm_tcgen05_3xtf32 gemm_simt conv_simt attention_simt layernorm softmax sum_axis1 maxpool eltwise";
 }
 
 }  // extern "C"

@@ -64,6 +64,18 @@ def test_matmul(lib, orc, M, K, N, epi):
     assert_close(out.cpu().numpy(), ref, 1e-4)
 
 
+@pytest.mark.parametrize("M,K,N", [(256, 16384, 256), (300, 4099, 130), (128, 64, 256), (1000, 2000, 3000)])
+def test_matmul_tensor_core_exact(lib, orc, M, K, N):
+    """3xTF32 path (these shapes are above the tensor-core threshold) stays within 1e-4
+    even at K = 16384, the largest reduction of the GEMM sweep."""
+    a = data.uniform(6, (M, K), -1, 1)
+    b = data.uniform(7, (K, N), -1, 1)
+    ref = orc.matmul(a, b)
+    out = torch.empty((M, N), device="cuda")
+    run(lib.lcu_matmul(P(out), P(dev(a)), P(dev(b)), M, K, N, None, EPI_NONE, MODE_FP32_EXACT, None))
+    assert_close(out.cpu().numpy(), ref, 1e-4)
+
+
 @pytest.mark.parametrize("M,K,N", [(512, 768, 3072), (2048, 2048, 2048)])
 def test_matmul_tf32_mode(lib, orc, M, K, N):
     a = data.uniform(4, (M, K), -1, 1)
