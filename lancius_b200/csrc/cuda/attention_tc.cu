@@ -1,0 +1,346 @@
+// Flash attention on the tcgen05 tensor cores, FP32-exact (3xTF32), head_dim 64.
+// Restates kernel_attention (lancius_kernels.c:278-332): per query row an online
+// softmax over all keys (causal: keys j > i masked), scale 1/sqrt(D); the score
+// matrix never leaves the SM.
+//
+// One CTA = (128-query tile, head, batch element). Roles:
+//   warps 0-3  softmax: one query row per thread (= its TMEM lane). Loads the Q row
+//              and splits it into TF32 hi/lo TMEM columns; per key tile reads S,
+//              writes P = exp2(S - m) as hi/lo TMEM columns and keeps the row sum.
+//              The running max m is only raised when a tile's max exceeds it by more
+//              than 2^8 (then the O accumulator in TMEM is rescaled); any fixed offset
+//              gives the same softmax, so this is exact, and P stays <= 256.
+//   warp 4     TMEM allocation + MMA issue (one lane), in the order
+//                S_0, S_1, PV_0, S_2, PV_1, ...
+//              S_j = Q K_j^T (A = Q from TMEM), O += P_j V_j (A = P_j from TMEM);
+//              each product is 3 passes: lo*hi + hi*lo + hi*hi
+//   warps 5-8  loaders: K_j, V_j from global (coalesced float4, next tile prefetched
+//              into registers), split hi/lo, stored in the swizzled layouts tcgen05
+//              reads (K: K-major 128B swizzle; V: N-major 128B swizzle, 32B atoms)
+// TMEM columns: Q hi [0,64) lo [64,128); S [128,192); O [192,256);
+// P buffers (double) hi/lo [256,384) and [384,512). Every mbarrier wait is bounded.
+#include "tc_common.cuh"
+
+namespace {
+
+constexpr int D = 64, BQ = 128, BKV = 64, NS = 2;
+constexpr int THREADS = 288;
+constexpr int KV_HALF = BKV * D * 4;            // 16 KB: one hi or lo tile
+constexpr int STAGE = 2 * KV_HALF;              // hi + lo
+constexpr int SMEM_BYTES = 2 * NS * STAGE + 1024 + 512;
+constexpr uint32_t TM_QHI = 0, TM_QLO = 64, TM_S = 128, TM_O = 192, TM_P = 256, TM_COLS = 512;
+constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
+
+__device__ int g_attn_watchdog = 0;
+
+struct Bars {
+    uint64_t k_full[NS], k_empty[NS], v_full[NS], v_empty[NS];
+    uint64_t s_full, s_free, q_ready, drain;
+    uint64_t p_ready[2], pv_done[2];   // per P buffer: keeps every waiter within one phase
+    uint32_t tmem;
+    int abort;
+};
+
+__device__ __forceinline__ uint32_t k_off(int j, int d) {     // K-major, 128B swizzle, 2 atoms of 32 d
+    return (uint32_t)((d >> 5) * (BKV * 128) + j * 128 + ((((d & 31) >> 2) ^ (j & 7)) << 4));
+}
+__device__ __forceinline__ uint32_t v_off(int j, int d) {     // N-major, 128B swizzle of 32B atoms
+    return (uint32_t)((d >> 5) * (BKV * 128) + j * 128 + ((((d & 31) >> 3) ^ (j & 3)) << 5) + ((d & 7) << 2));
+}
+// TF32 split: hi keeps the top 10 mantissa bits (exactly what the tensor core reads),
+// lo = x - hi is exact in FP32 and carries the next bits.
+__device__ __forceinline__ float hi_part(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+__device__ __forceinline__ float ex2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstride, int S, int H, int causal,
+          float scale_log2) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* kst = tiles;                          // NS stages of K hi|lo
+    uint8_t* vst = tiles + NS * STAGE;             // NS stages of V hi|lo
+    Bars* bar = reinterpret_cast<Bars*>(tiles + 2 * NS * STAGE);
+
+    LcuAttnGroup p;
+    if (table) p = table[blockIdx.z];
+    else {
+        size_t off = (size_t)blockIdx.z * bstride;
+        p.q = base.q + off; p.k = base.k + off; p.v = base.v + off; p.o = base.o + off;
+    }
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int h = blockIdx.y;
+    const int qt = gridDim.x - 1 - blockIdx.x;      // longest (causal) tiles first
+    const int q0 = qt * BQ;
+    const int kv_end = causal ? min(S, q0 + BQ) : S;
+    const int T = (kv_end + BKV - 1) / BKV;
+    const size_t rs = (size_t)H * D;                // row stride of [S, H, D]
+    volatile int* abort = &bar->abort;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NS; s++) {
+            tc::mbar_init(&bar->k_full[s], 128); tc::mbar_init(&bar->k_empty[s], 1);
+            tc::mbar_init(&bar->v_full[s], 128); tc::mbar_init(&bar->v_empty[s], 1);
+        }
+        tc::mbar_init(&bar->s_full, 1);
+        tc::mbar_init(&bar->s_free, 128);
+        tc::mbar_init(&bar->q_ready, 128);
+        for (int b = 0; b < 2; b++) { tc::mbar_init(&bar->p_ready[b], 128); tc::mbar_init(&bar->pv_done[b], 1); }
+        tc::mbar_init(&bar->drain, 1);
+        bar->abort = 0;
+        tc::fence_barrier_init();
+    }
+    if (warp == 4) tc::tmem_alloc(&bar->tmem, TM_COLS);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tm = bar->tmem;
+
+    if (warp < 4) {
+        // ======================= softmax warps =======================
+        const int row = 32 * warp + lane;              // TMEM lane == query row in tile
+        const int qi = q0 + row;
+        const uint32_t lb = tm + ((uint32_t)(32 * warp) << 16);
+        {   // Q row -> TMEM hi/lo
+            float hi[32], lo[32];
+#pragma unroll 1
+            for (int half = 0; half < 2; half++) {
+                const float4* src = reinterpret_cast<const float4*>(p.q + (size_t)qi * rs + (size_t)h * D + half * 32);
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    float4 v = qi < S ? __ldg(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    float x[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                    for (int t = 0; t < 4; t++) { hi[4 * c + t] = hi_part(x[t]); lo[4 * c + t] = x[t] - hi[4 * c + t]; }
+                }
+                tc::tmem_st32(lb + TM_QHI + half * 32, hi);
+                tc::tmem_st32(lb + TM_QLO + half * 32, lo);
+            }
+            tc::tmem_st_wait();
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bar->q_ready);
+        }
+        float m = -INFINITY, l = 0.f;
+        bool ok = true;
+        for (int j = 0; j < T && ok; j++) {
+            if (!tc::mbar_wait(&bar->s_full, j & 1, abort, &g_attn_watchdog, 11)) { ok = false; break; }
+            tc::tc_fence_after();
+            float s[64];
+            {
+                float a[32], b[32];
+                tc::tmem_ld32(lb + TM_S, a);
+                tc::tmem_ld32(lb + TM_S + 32, b);
+#pragma unroll
+                for (int c = 0; c < 32; c++) { s[c] = a[c] * scale_log2; s[32 + c] = b[c] * scale_log2; }
+            }
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bar->s_free);               // the MMA warp may overwrite S now
+            const int k0 = j * BKV;
+            if (k0 + BKV > S || (causal && k0 + BKV - 1 > q0)) {   // tile touches the diagonal or the end
+#pragma unroll
+                for (int c = 0; c < 64; c++)
+                    if (k0 + c >= S || (causal && k0 + c > qi)) s[c] = -INFINITY;
+            }
+            float mx = s[0];
+#pragma unroll
+            for (int c = 1; c < 64; c++) mx = fmaxf(mx, s[c]);
+            const bool raise = mx > m + RESCALE_THRESHOLD;
+            if (__any_sync(0xffffffffu, raise)) {
+                const float mn = raise ? mx : m;
+                const float f = ex2(m - mn);             // 0 on the first tile, 1 for rows that keep m
+                if (j > 0) {   // O holds P_0..P_{j-1} V: wait for it, rescale the rows that moved
+                    if (!tc::mbar_wait(&bar->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, &g_attn_watchdog, 12)) { ok = false; break; }
+                    tc::tc_fence_after();
+#pragma unroll 1
+                    for (int half = 0; half < 2; half++) {
+                        float o[32];
+                        tc::tmem_ld32(lb + TM_O + half * 32, o);
+#pragma unroll
+                        for (int c = 0; c < 32; c++) o[c] *= f;
+                        tc::tmem_st32(lb + TM_O + half * 32, o);
+                    }
+                    tc::tmem_st_wait();
+                }
+                l *= f;
+                m = mn;
+            }
+            float rsum = 0.f;
+            const uint32_t pb = lb + TM_P + (uint32_t)(j & 1) * 128;
+            // P buffer j&1 was last read by PV_{j-2}
+            if (j >= 2 && !tc::mbar_wait(&bar->pv_done[j & 1], ((j - 2) >> 1) & 1, abort, &g_attn_watchdog, 14)) { ok = false; break; }
+#pragma unroll
+            for (int half = 0; half < 2; half++) {
+                float hi[32], lo[32];
+#pragma unroll
+                for (int c = 0; c < 32; c++) {
+                    float e = ex2(s[half * 32 + c] - m);
+                    rsum += e;
+                    hi[c] = hi_part(e);
+                    lo[c] = e - hi[c];
+                }
+                tc::tmem_st32(pb + half * 32, hi);
+                tc::tmem_st32(pb + 64 + half * 32, lo);
+            }
+            l += rsum;
+            tc::tmem_st_wait();
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bar->p_ready[j & 1]);
+        }
+        if (ok && T > 0 && tc::mbar_wait(&bar->pv_done[(T - 1) & 1], ((T - 1) >> 1) & 1, abort, &g_attn_watchdog, 13)) {
+            tc::tc_fence_after();
+            const float inv = 1.f / l;
+#pragma unroll 1
+            for (int half = 0; half < 2; half++) {
+                float o[32];
+                tc::tmem_ld32(lb + TM_O + half * 32, o);
+                if (qi < S) {
+                    float4* dst = reinterpret_cast<float4*>(p.o + (size_t)qi * rs + (size_t)h * D + half * 32);
+#pragma unroll
+                    for (int c = 0; c < 8; c++)
+                        dst[c] = make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv, o[4 * c + 3] * inv);
+                }
+            }
+        }
+    } else if (warp == 4) {
+        // ======================= MMA issuer =======================
+        if (lane == 0) {
+            constexpr uint32_t id_s = tc::idesc_tf32(BQ, BKV, false, false);
+            constexpr uint32_t id_o = tc::idesc_tf32(BQ, D, false, true);
+            bool ok = tc::mbar_wait(&bar->q_ready, 0, abort, &g_attn_watchdog, 21);
+            auto issue_s = [&](int j) -> bool {
+                const int st = j % NS;
+                if (!tc::mbar_wait(&bar->k_full[st], (j / NS) & 1, abort, &g_attn_watchdog, 22)) return false;
+                if (j >= 1 && !tc::mbar_wait(&bar->s_free, (j - 1) & 1, abort, &g_attn_watchdog, 23)) return false;
+                tc::tc_fence_after();
+                const uint32_t khi = tc::smem_u32(kst + st * STAGE), klo = khi + KV_HALF;
+#pragma unroll
+                for (int kb = 0; kb < D / 8; kb++) {
+                    const uint32_t off = (uint32_t)((kb >> 2) * (BKV * 128) + (kb & 3) * 32);
+                    const uint64_t bh = tc::smem_desc(khi + off, 16, 1024, tc::SWZ_128B);
+                    const uint64_t bl = tc::smem_desc(klo + off, 16, 1024, tc::SWZ_128B);
+                    tc::mma_tf32_ts(tm + TM_S, tm + TM_QLO + kb * 8, bh, id_s, kb ? 1u : 0u);
+                    tc::mma_tf32_ts(tm + TM_S, tm + TM_QHI + kb * 8, bl, id_s, 1u);
+                    tc::mma_tf32_ts(tm + TM_S, tm + TM_QHI + kb * 8, bh, id_s, 1u);
+                }
+                tc::mma_commit(&bar->s_full);
+                tc::mma_commit(&bar->k_empty[st]);
+                return true;
+            };
+            if (ok && T > 0) ok = issue_s(0);
+            for (int j = 0; j < T && ok; j++) {
+                if (j + 1 < T && !(ok = issue_s(j + 1))) break;
+                const int st = j % NS;
+                if (!tc::mbar_wait(&bar->p_ready[j & 1], (j >> 1) & 1, abort, &g_attn_watchdog, 24) ||
+                    !tc::mbar_wait(&bar->v_full[st], (j / NS) & 1, abort, &g_attn_watchdog, 25)) { ok = false; break; }
+                tc::tc_fence_after();
+                const uint32_t vhi = tc::smem_u32(vst + st * STAGE), vlo = vhi + KV_HALF;
+                const uint32_t pb = tm + TM_P + (uint32_t)(j & 1) * 128;
+#pragma unroll
+                for (int kb = 0; kb < BKV / 8; kb++) {
+                    const uint64_t bh = tc::smem_desc(vhi + kb * 1024, BKV * 128, 512, tc::SWZ_128B_BASE32B);
+                    const uint64_t bl = tc::smem_desc(vlo + kb * 1024, BKV * 128, 512, tc::SWZ_128B_BASE32B);
+                    const uint32_t acc0 = (j | kb) ? 1u : 0u;
+                    tc::mma_tf32_ts(tm + TM_O, pb + 64 + kb * 8, bh, id_o, acc0);
+                    tc::mma_tf32_ts(tm + TM_O, pb + kb * 8, bl, id_o, 1u);
+                    tc::mma_tf32_ts(tm + TM_O, pb + kb * 8, bh, id_o, 1u);
+                }
+                tc::mma_commit(&bar->pv_done[j & 1]);
+                tc::mma_commit(&bar->v_empty[st]);
+            }
+        }
+    } else {
+        // ======================= loaders (warps 5-8) =======================
+        const int t = threadIdx.x - 160;                 // 0..127
+        const int jr = t >> 1, d0 = (t & 1) * 32;        // key row within tile, d half
+        float4 kv[8], vv[8];
+        auto fetch = [&](int j) {
+            const int key = j * BKV + jr;
+            const float4* ks = reinterpret_cast<const float4*>(p.k + (size_t)key * rs + (size_t)h * D + d0);
+            const float4* vs = reinterpret_cast<const float4*>(p.v + (size_t)key * rs + (size_t)h * D + d0);
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                kv[c] = key < S ? __ldg(ks + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                vv[c] = key < S ? __ldg(vs + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        };
+        if (T > 0) fetch(0);
+        for (int j = 0; j < T; j++) {
+            const int st = j % NS;
+            float4 kn[8], vn[8];
+#pragma unroll
+            for (int c = 0; c < 8; c++) { kn[c] = kv[c]; vn[c] = vv[c]; }
+            if (j + 1 < T) fetch(j + 1);                 // next tile in flight while this one is stored
+            if (j >= NS && !tc::mbar_wait(&bar->k_empty[st], ((j / NS) - 1) & 1, abort, &g_attn_watchdog, 31)) break;
+            uint8_t* kh = kst + st * STAGE;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                float x[4] = {kn[c].x, kn[c].y, kn[c].z, kn[c].w}, hi[4], lo[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) { hi[u] = hi_part(x[u]); lo[u] = x[u] - hi[u]; }
+                const uint32_t o = k_off(jr, d0 + 4 * c);
+                *reinterpret_cast<float4*>(kh + o) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<float4*>(kh + KV_HALF + o) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+            }
+            tc::fence_proxy_async();
+            tc::mbar_arrive(&bar->k_full[st]);
+            if (j >= NS && !tc::mbar_wait(&bar->v_empty[st], ((j / NS) - 1) & 1, abort, &g_attn_watchdog, 32)) break;
+            uint8_t* vh = vst + st * STAGE;
+#pragma unroll
+            for (int c = 0; c < 8; c++) {
+                float x[4] = {vn[c].x, vn[c].y, vn[c].z, vn[c].w}, hi[4], lo[4];
+#pragma unroll
+                for (int u = 0; u < 4; u++) { hi[u] = hi_part(x[u]); lo[u] = x[u] - hi[u]; }
+                const uint32_t o = v_off(jr, d0 + 4 * c);
+                *reinterpret_cast<float4*>(vh + o) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<float4*>(vh + KV_HALF + o) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+            }
+            tc::fence_proxy_async();
+            tc::mbar_arrive(&bar->v_full[st]);
+        }
+    }
+
+    tc::tc_fence_before();
+    __syncthreads();
+    if (bar->abort && warp == 4 && lane == 0) {    // let issued MMAs retire before TMEM is released
+        int never = 0;
+        tc::mma_commit(&bar->drain);
+        tc::mbar_wait(&bar->drain, 0, &never, nullptr, 0);
+    }
+    __syncthreads();
+    if (warp == 4) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tm, TM_COLS);
+    }
+}
+
+}  // namespace
+
+extern "C" int lcu_attention_tc_supported(size_t D_) { return D_ == (size_t)D; }
+
+extern "C" lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, const float* k, const float* v,
+                                          float* o, size_t B, size_t S, size_t H, int causal, void* stream) {
+    if (B == 0 || S == 0 || H == 0) return LANCIUS_ERROR_OK;
+    static bool configured = false;
+    if (!configured) {
+        if (cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+            return lcu_launch_status();
+        configured = true;
+    }
+    LcuAttnGroup base{q, k, v, o};
+    float scale_log2 = (float)(1.4426950408889634 / 8.0);   // log2(e) / sqrt(64)
+    dim3 grid((unsigned)((S + BQ - 1) / BQ), (unsigned)H, (unsigned)B);
+    k_attn_tc<<<grid, THREADS, SMEM_BYTES, lcu_as_stream(stream)>>>(d_table, base, S * H * D, (int)S, (int)H, causal,
+                                                                     scale_log2);
+    lcu_note_launch();
+    return lcu_launch_status();
+}
+
+extern "C" int lcu_attention_watchdog_read_and_clear(void) {
+    int v = 0, z = 0;
+    cudaMemcpyFromSymbol(&v, g_attn_watchdog, sizeof(int));
+    if (v) cudaMemcpyToSymbol(g_attn_watchdog, &z, sizeof(int));
+    return v;
+}

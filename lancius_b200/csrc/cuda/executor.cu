@@ -612,8 +612,12 @@ static lancius_error run_steps(lcu_ctx* c) {
                 }
                 break;
             case S_ATTN:
-                e = lcu_attention_simt((const LcuAttnGroup*)(base + s.table_off), nullptr, nullptr, nullptr, nullptr,
-                                       (size_t)s.count, s.S, s.H, s.D, s.causal, st);
+                if (lcu_attention_tc_supported(s.D) && !lcu_force_simt())
+                    e = lcu_attention_tc((const LcuAttnGroup*)(base + s.table_off), nullptr, nullptr, nullptr, nullptr,
+                                         (size_t)s.count, s.S, s.H, s.causal, st);
+                else
+                    e = lcu_attention_simt((const LcuAttnGroup*)(base + s.table_off), nullptr, nullptr, nullptr, nullptr,
+                                           (size_t)s.count, s.S, s.H, s.D, s.causal, st);
                 break;
             case S_LN:
                 e = lcu_layernorm_grouped((const LcuRowGroup*)(base + s.table_off), s.count,

@@ -48,6 +48,11 @@ lancius_error lcu_gemm_tc(float* c, const float* a, const float* b, size_t M, si
                           int epi, int mode, void* stream);
 int lcu_gemm_watchdog_read_and_clear(void);
 int lcu_use_tensor_cores(size_t M, size_t N, size_t K);
+int lcu_attention_tc_supported(size_t D);
+int lcu_force_simt(void);
+lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, const float* k, const float* v, float* o,
+                               size_t B, size_t S, size_t H, int causal, void* stream);
+int lcu_attention_watchdog_read_and_clear(void);
 void lcu_reset_launch_count(void);
 int lcu_launch_count(void);
 }

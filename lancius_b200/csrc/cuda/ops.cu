@@ -10,13 +10,18 @@ extern "C" int lcu_launch_count(void) { return tl_launches; }
 
 // Tensor-core path from 2^24 multiply-adds up (below that the CUDA-core kernel's
 // single launch beats split + GEMM); LCU_FORCE_SIMT=1 / LCU_FORCE_TC=1 override.
-extern "C" int lcu_use_tensor_cores(size_t M, size_t N, size_t K) {
+static int force_mode() {
     static int force = -1;
     if (force < 0) {
         const char* s = getenv("LCU_FORCE_SIMT");
         const char* t = getenv("LCU_FORCE_TC");
         force = (s && s[0] == '1') ? 0 : (t && t[0] == '1') ? 1 : 2;
     }
+    return force;
+}
+extern "C" int lcu_force_simt(void) { return force_mode() == 0; }
+extern "C" int lcu_use_tensor_cores(size_t M, size_t N, size_t K) {
+    int force = force_mode();
     if (force != 2) return force && K > 0;
     return K > 0 && (double)M * (double)N * (double)K >= 16777216.0;
 }
@@ -41,6 +46,9 @@ lancius_error lcu_attention(float* out, const float* q, const float* k, const fl
     if (!out || !q || !k || !v) return bad(LANCIUS_ERROR_NULL_PTR);
     if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
     if (D != 64 && D != 128) return bad(LANCIUS_ERROR_UNSUPPORTED_OP);
+    if ((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15u)) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+    if (lcu_attention_tc_supported(D) && !lcu_force_simt())
+        return lcu_attention_tc(nullptr, q, k, v, out, B, S, H, causal ? 1 : 0, stream);
     return lcu_attention_simt(nullptr, q, k, v, out, B, S, H, D, causal ? 1 : 0, stream);
 }
 
@@ -54,7 +62,7 @@ lancius_error lcu_conv2d(float* out, const float* in, const float* w, size_t N, 
 }
 
 const char* lcu_build_info(void) {
-    return "lancius_b200 sm_100a: gemm_tcgen05_3xtf32 gemm_simt conv_simt attention_simt layernorm softmax sum_axis1 maxpool eltwise";
+    return "lancius_b200 sm_100a: gemm_tcgen05_3xtf32 attention_tcgen05_3xtf32 gemm_simt conv_simt attention_simt layernorm softmax sum_axis1 maxpool eltwise";
 }
 
 }  // extern "C"
