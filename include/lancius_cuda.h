@@ -112,6 +112,20 @@ lancius_error lcu_sum_axis1(float* out, const float* in, size_t rows, size_t col
 lancius_error lcu_maxpool2d(float* out, const float* in, size_t N, size_t C, size_t H_in, size_t W_in,
                             size_t K, size_t stride, void* stream);
 
+/* lcu_matmul without device allocation (no counterpart in the reference, whose
+ * kernels run on the host). For callers that may not call cudaMalloc once they are
+ * running -- device memory owned by another allocator or a fixed memory budget.
+ * Same arguments and results as lcu_matmul (tensor-core path, M, N, K >= 1); its
+ * scratch is a 64 MiB array compiled into the library, one per GPU, kept until
+ * exit: problems needing more (lcu_gemm_tc scratch ~ 16*(M*K+K*N) bytes in
+ * FP32-exact mode) return LANCIUS_ERROR_OVERFLOW. All calls on a GPU share the
+ * array, so calls that overlap on the GPU race; serialize them. The first call on
+ * each device looks up the array's address; make it before any stream capture.
+ * Blocks until the product is written. */
+lancius_error lcu_matmul_noalloc(float* out, const float* a, const float* b, size_t M, size_t K, size_t N,
+                                 const float* bias, int epilogue, int mode, void* stream);
+size_t lcu_noalloc_scratch_capacity(void);
+
 /* Library self-description for tests: the names of this build's kernels. */
 const char* lcu_build_info(void);
 

@@ -130,6 +130,8 @@ B200_FUNCS = {
     "lcu_sum_axis1": (C.c_int, [P, P, c_size, c_size, P]),
     "lcu_maxpool2d": (C.c_int, [P, P, c_size, c_size, c_size, c_size, c_size, c_size, P]),
     "lcu_build_info": (C.c_char_p, []),
+    "lcu_matmul_noalloc": (C.c_int, [P, P, P, c_size, c_size, c_size, P, C.c_int, C.c_int, P]),
+    "lcu_noalloc_scratch_capacity": (c_size, []),
 }
 
 
