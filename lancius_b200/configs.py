@@ -42,10 +42,15 @@ def _linear(g, b, x, w_arr, bias_arr, rows):
     return g.add(g.matmul(x, w), g.broadcast(bias, rows, N))
 
 
-def mlp(g, batch=64, seed=0):
-    """Config 1: 784 -> 256 (+bias, ReLU) -> 10 (+bias) -> softmax."""
+def mlp(g, batch=64, seed=0, rows=None):
+    """Config 1: 784 -> 256 (+bias, ReLU) -> 10 (+bias) -> softmax.
+    rows=(start, stop) builds the graph for that block of the seeded batch (sharding)."""
     b = Built("mlp", g)
-    x = _inp(b, g.input(batch, 784), data.uniform(seed, (batch, 784), 0.0, 1.0))
+    xfull = data.uniform(seed, (batch, 784), 0.0, 1.0)
+    if rows is not None:
+        xfull = xfull[rows[0]:rows[1]]
+        batch = xfull.shape[0]
+    x = _inp(b, g.input(batch, 784), xfull)
     w1 = data.normal(data.sub_seed(seed, 1), (784, 256), 0.0, 1.0 / np.sqrt(784))
     w2 = data.normal(data.sub_seed(seed, 2), (256, 10), 0.0, 1.0 / np.sqrt(256))
     h = g.relu(_linear(g, b, x, w1, np.zeros(256), batch))
