@@ -33,6 +33,19 @@ constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
 
 __device__ int g_attn_watchdog = 0;
 
+// Optional per-CTA phase timestamps (%globaltimer) for tuning; compiled out unless
+// built with -DLCU_ATTN_TRACE=1.
+#ifndef LCU_ATTN_TRACE
+#define LCU_ATTN_TRACE 0
+#endif
+#if LCU_ATTN_TRACE
+__device__ unsigned long long g_trace[512][64];
+__device__ __forceinline__ unsigned long long gtime() { unsigned long long t; asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t)); return t; }
+#define TRACE(slot) do { unsigned cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z); if (cta < 512 && (slot) < 64) g_trace[cta][slot] = gtime(); } while (0)
+#else
+#define TRACE(slot) do {} while (0)
+#endif
+
 struct Bars {
     uint64_t k_full[NS], k_empty[NS], v_full[NS], v_empty[NS];
     uint64_t s_full, s_free, q_ready, drain;
@@ -98,6 +111,7 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tm = bar->tmem;
+    if (threadIdx.x == 0) TRACE(0);
 
     if (warp < 4) {
         // ======================= softmax warps =======================
@@ -122,11 +136,13 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
             tc::tmem_st_wait();
             tc::tc_fence_before();
             tc::mbar_arrive(&bar->q_ready);
+            if (threadIdx.x == 0) TRACE(1);
         }
         float m = -INFINITY, l = 0.f;
         bool ok = true;
         for (int j = 0; j < T && ok; j++) {
             if (!tc::mbar_wait(&bar->s_full, j & 1, abort, &g_attn_watchdog, 11)) { ok = false; break; }
+            if (threadIdx.x == 0 && j < 8) TRACE(2 + 4 * j);
             tc::tc_fence_after();
             float s[64];
             {
@@ -167,6 +183,7 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                 l *= f;
                 m = mn;
             }
+            if (threadIdx.x == 0 && j < 8) TRACE(3 + 4 * j);
             float rsum = 0.f;
             const uint32_t pb = lb + TM_P + (uint32_t)(j & 1) * 128;
             // P buffer j&1 was last read by PV_{j-2}
@@ -185,9 +202,11 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                 tc::tmem_st32(pb + 64 + half * 32, lo);
             }
             l += rsum;
+            if (threadIdx.x == 0 && j < 8) TRACE(4 + 4 * j);
             tc::tmem_st_wait();
             tc::tc_fence_before();
             tc::mbar_arrive(&bar->p_ready[j & 1]);
+            if (threadIdx.x == 0 && j < 8) TRACE(5 + 4 * j);
         }
         if (ok && T > 0 && tc::mbar_wait(&bar->pv_done[(T - 1) & 1], ((T - 1) >> 1) & 1, abort, &g_attn_watchdog, 13)) {
             tc::tc_fence_after();
@@ -227,6 +246,7 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                 }
                 tc::mma_commit(&bar->s_full);
                 tc::mma_commit(&bar->k_empty[st]);
+                if (j < 8) TRACE(34 + j);
                 return true;
             };
             if (ok && T > 0) ok = issue_s(0);
@@ -248,6 +268,7 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                     tc::mma_tf32_ts(tm + TM_O, pb + kb * 8, bh, id_o, 1u);
                 }
                 tc::mma_commit(&bar->pv_done[j & 1]);
+                if (j < 8) TRACE(42 + j);
                 tc::mma_commit(&bar->v_empty[st]);
             }
         }
@@ -286,6 +307,7 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
             }
             tc::fence_proxy_async();
             tc::mbar_arrive(&bar->k_full[st]);
+            if (t == 0 && j < 7) TRACE(50 + j);
             if (j >= NS && !tc::mbar_wait(&bar->v_empty[st], ((j / NS) - 1) & 1, abort, &g_attn_watchdog, 32)) break;
             uint8_t* vh = vst + st * STAGE;
 #pragma unroll
@@ -299,11 +321,13 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
             }
             tc::fence_proxy_async();
             tc::mbar_arrive(&bar->v_full[st]);
+            if (t == 0 && j < 6) TRACE(57 + j);
         }
     }
 
     tc::tc_fence_before();
     __syncthreads();
+    if (threadIdx.x == 0) TRACE(63);
     if (bar->abort && warp == 4 && lane == 0) {    // let issued MMAs retire before TMEM is released
         int never = 0;
         tc::mma_commit(&bar->drain);
@@ -336,6 +360,15 @@ extern "C" lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const flo
                                                                      scale_log2);
     lcu_note_launch();
     return lcu_launch_status();
+}
+
+extern "C" int lcu_attention_trace(unsigned long long* host, int n) {
+#if LCU_ATTN_TRACE
+    return cudaMemcpyFromSymbol(host, g_trace, sizeof(unsigned long long) * 64 * (n < 512 ? n : 512)) == cudaSuccess;
+#else
+    (void)host; (void)n;
+    return 0;
+#endif
 }
 
 extern "C" int lcu_attention_watchdog_read_and_clear(void) {

@@ -396,6 +396,18 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                     st.co = wt->shape[0]; st.kh = wt->shape[2]; st.kw = wt->shape[3]; st.stride = n->stride; st.pad = n->pad;
                     if (in->ndim != 4 || wt->ndim != 4 || wt->shape[1] != st.ci || st.stride == 0) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
                     st.out = O(n); st.in0 = O(in); st.in1 = O(wt);
+                    size_t ho = (st.h + 2 * st.pad - st.kh) / st.stride + 1, wo = (st.w + 2 * st.pad - st.kw) / st.stride + 1;
+                    st.M = st.co; st.N = st.cn * ho * wo; st.K = st.ci * st.kh * st.kw;
+                    st.tc = st.cn && st.ci && lcu_use_tensor_cores(st.M, st.N, st.K);
+                    if (st.tc) {
+                        size_t need = lcu_gemm_tc_scratch_bytes(st.M, st.N, st.K, 1, 1, 3);
+                        if (need > c->scratch_bytes) c->scratch_bytes = need;
+                        st.plan_idx = (int)c->tc_plans.size();
+                        c->tc_plans.push_back(LcuTcGemmPlan());
+                        std::vector<LcuGemmGroup> t{LcuGemmGroup{ptr_token(O(wt)), ptr_token(O(in)), (float*)ptr_token(O(n)),
+                                                                 nullptr, nullptr}};
+                        st.table_off = b.add_table(t);
+                    }
                 } break;
                 case LANCIUS_OP_MAXPOOL2D: {
                     const lancius_node* in = n->inputs[0];
@@ -482,7 +494,7 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
     auto patch = [&](const float*& p) { if (p) p = reinterpret_cast<const float*>(c->dmem + ((size_t)p - 1)); };
     for (Step& st : c->steps) {
         char* base = b.tables.data() + st.table_off;
-        if (st.kind == S_GEMM) {
+        if (st.kind == S_GEMM || (st.kind == S_CONV && st.tc)) {
             LcuGemmGroup* t = (LcuGemmGroup*)base;
             for (int i = 0; i < st.count; i++) {
                 patch(t[i].a); patch(t[i].b); patch((const float*&)t[i].c); patch(t[i].bias); patch(t[i].resid);
@@ -630,6 +642,19 @@ static lancius_error run_steps(lcu_ctx* c) {
             case S_SUMAX1: e = lcu_sum_axis1(F(s.out), F(s.in0), s.rows, s.cols, st); break;
             case S_BCAST: e = lcu_broadcast(F(s.out), F(s.in0), s.in_elems, s.rows, s.cols, st); break;
             case S_CONV:
+                if (s.tc) {
+                    LcuTcGemmPlan& p = c->tc_plans[s.plan_idx];
+                    int passes = c->mode == LCU_MODE_TF32 ? 1 : 3;
+                    if (p.passes != passes || p.M != s.M) {
+                        e = lcu_gemm_tc_prepare(&p, c->scratch, s.M, s.N, s.K, 1, 1, passes);
+                        if (e != LANCIUS_ERROR_OK) break;
+                        size_t ho = (s.h + 2 * s.pad - s.kh) / s.stride + 1, wo = (s.w + 2 * s.pad - s.kw) / s.stride + 1;
+                        p.conv = LcuConvShape{(int)s.cn, (int)s.ci, (int)s.h, (int)s.w, (int)s.co, (int)s.kh, (int)s.kw,
+                                              (int)s.stride, (int)s.pad, (int)ho, (int)wo};
+                    }
+                    e = lcu_gemm_tc_run(&p, (const LcuGemmGroup*)(base + s.table_off), s.relu ? LCU_EPI_RELU : LCU_EPI_NONE, st);
+                    break;
+                }
                 e = lcu_conv2d(F(s.out), F(s.in0), F(s.in1), s.cn, s.ci, s.h, s.w, s.co, s.kh, s.kw, s.stride, s.pad,
                                s.relu, c->mode, st);
                 break;

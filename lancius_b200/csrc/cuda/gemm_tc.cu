@@ -48,7 +48,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
           const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
           const LcuGemmGroup* __restrict__ groups, int M, int N, int K, int epi, int passes, int b_shared,
-          int splits, int kchunk, float* __restrict__ partial) {
+          int splits, int kchunk, float* __restrict__ partial, int conv_hw) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Smem* sm = reinterpret_cast<Smem*>(tiles + STAGES * STAGE_BYTES);
@@ -155,6 +155,22 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
                     printf("row %d v=%g %g %g %g %g %g\n", row, v[0], v[1], v[2], v[3], v[4], v[5]);
                 if (row >= M) continue;
                 const int col0 = n0 + c;
+                if (conv_hw && splits == 1) {
+                    // implicit-GEMM conv: row = output channel, column = n*HoWo + pixel -> NCHW
+                    if (conv_hw % 32 == 0 && col0 + 32 <= N && (reinterpret_cast<uintptr_t>(gr.c) & 15) == 0) {
+                        float* d = gr.c + (size_t)(col0 / conv_hw) * M * conv_hw + (size_t)row * conv_hw + col0 % conv_hw;
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *reinterpret_cast<float4*>(d + j) = make_float4(lcu_apply_epi(v[j], epi_here), lcu_apply_epi(v[j + 1], epi_here),
+                                                                            lcu_apply_epi(v[j + 2], epi_here), lcu_apply_epi(v[j + 3], epi_here));
+                    } else {
+                        for (int j = 0; j < 32 && col0 + j < N; j++) {
+                            const int cc = col0 + j;
+                            gr.c[(size_t)(cc / conv_hw) * M * conv_hw + (size_t)row * conv_hw + cc % conv_hw] = lcu_apply_epi(v[j], epi_here);
+                        }
+                    }
+                    continue;
+                }
                 float* dst = gr.c + (size_t)row * N + col0;
                 const float* res = gr.resid ? gr.resid + (size_t)row * N + col0 : nullptr;
                 if (vec && col0 + 32 <= N) {
@@ -223,9 +239,33 @@ __global__ void k_split(const LcuGemmGroup* __restrict__ groups, int which, size
     }
 }
 
+// hi/lo im2col of an NCHW input into pitched [K = Ci*Kh*Kw][P = N*Ho*Wo] scratch
+// (zero padding), the B operand of the implicit-GEMM conv; reads groups[0].b.
+__global__ void k_im2col_split(const LcuGemmGroup* __restrict__ groups, LcuConvShape cs, size_t pitch,
+                               float* __restrict__ hi, float* __restrict__ lo) {
+    // grid.y = k (one im2col row), grid.x strides over the N*Ho*Wo columns (32-bit index math)
+    const float* in = groups[0].b;
+    const int k = blockIdx.y;
+    const int kw = k % cs.kw, kh = (k / cs.kw) % cs.kh, ci = k / (cs.kw * cs.kh);
+    const int hw = cs.ho * cs.wo, P = cs.n * hw;
+    float* hrow = hi + (size_t)k * pitch;
+    float* lrow = lo ? lo + (size_t)k * pitch : nullptr;
+    for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < P; p += gridDim.x * blockDim.x) {
+        const int n = p / hw, r = p - n * hw;
+        const int ho = r / cs.wo, wo = r - ho * cs.wo;
+        const int ih = ho * cs.stride - cs.pad + kh, iw = wo * cs.stride - cs.pad + kw;
+        float x = 0.f;
+        if (ih >= 0 && iw >= 0 && ih < cs.h && iw < cs.w)
+            x = __ldg(in + (((size_t)n * cs.ci + ci) * cs.h + ih) * (size_t)cs.w + iw);
+        const float h = tc::tf32_rna(x);
+        hrow[p] = h;
+        if (lrow) lrow[p] = tc::tf32_rna(x - h);
+    }
+}
+
 // out = act(sum over splits of the partials + bias) + resid, splits summed in order
 __global__ void k_splitk_reduce(const LcuGemmGroup* __restrict__ groups, const float* __restrict__ partial, int splits,
-                                size_t M, size_t N, int epi) {
+                                size_t M, size_t N, int epi, size_t conv_hw) {
     const LcuGemmGroup gr = groups[blockIdx.y];
     const float* p = partial + (size_t)blockIdx.y * splits * M * N;
     size_t n = M * N;
@@ -235,7 +275,12 @@ __global__ void k_splitk_reduce(const LcuGemmGroup* __restrict__ groups, const f
         if (gr.bias) acc += __ldg(gr.bias + i % N);
         acc = lcu_apply_epi(acc, epi);
         if (gr.resid) acc += gr.resid[i];
-        gr.c[i] = acc;
+        if (conv_hw) {
+            size_t r = i / N, c = i % N;
+            gr.c[(c / conv_hw) * M * conv_hw + r * conv_hw + c % conv_hw] = acc;
+        } else {
+            gr.c[i] = acc;
+        }
     }
 }
 
@@ -296,6 +341,7 @@ extern "C" size_t lcu_gemm_tc_scratch_bytes(size_t M, size_t N, size_t K, int G,
 extern "C" lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, size_t M, size_t N, size_t K, int G,
                                              int Gb, int passes) {
     p->M = M; p->N = N; p->K = K; p->Kp = pad4(K); p->Np = pad4(N); p->G = G; p->Gb = Gb; p->passes = passes;
+    p->conv = LcuConvShape{};
     size_t a = al256((size_t)G * M * p->Kp * 4), b = al256((size_t)Gb * K * p->Np * 4);
     char* s = static_cast<char*>(scratch);
     p->s_ahi = (float*)s; s += a;
@@ -316,11 +362,14 @@ extern "C" lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, si
 }
 
 extern "C" lancius_error lcu_gemm_tc_run(const LcuTcGemmPlan* p, const LcuGemmGroup* d_groups, int epi, void* stream) {
-    static bool configured = false;
-    if (!configured) {
+    static bool configured[64] = {};     // the attribute is per device
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    if (!configured[dev]) {
         if (cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
             return lcu_launch_status();
-        configured = true;
+        configured[dev] = true;
     }
     cudaStream_t st = lcu_as_stream(stream);
     float* lo_a = p->passes > 1 ? p->s_alo : nullptr;
@@ -328,17 +377,22 @@ extern "C" lancius_error lcu_gemm_tc_run(const LcuTcGemmPlan* p, const LcuGemmGr
     if (p->K > 0) {
         k_split<<<dim3(lcu_blocks(p->M * p->K, 256 * 8, 148 * 4), p->G), 256, 0, st>>>(d_groups, 0, p->M, p->K, p->Kp, p->s_ahi, lo_a);
         lcu_note_launch();
-        k_split<<<dim3(lcu_blocks(p->K * p->N, 256 * 8, 148 * 4), p->Gb), 256, 0, st>>>(d_groups, 1, p->K, p->N, p->Np, p->s_bhi, lo_b);
+        if (p->conv.n)
+            k_im2col_split<<<dim3((unsigned)((p->N + 1023) / 1024 < 64 ? (p->N + 1023) / 1024 : 64), (unsigned)p->K), 256, 0, st>>>(
+                d_groups, p->conv, p->Np, p->s_bhi, lo_b);
+        else
+            k_split<<<dim3(lcu_blocks(p->K * p->N, 256 * 8, 148 * 4), p->Gb), 256, 0, st>>>(d_groups, 1, p->K, p->N, p->Np, p->s_bhi, lo_b);
         lcu_note_launch();
     }
     dim3 grid((unsigned)((p->N + BN - 1) / BN), (unsigned)((p->M + BM - 1) / BM), (unsigned)(p->G * p->splits));
     k_gemm_tc<<<grid, THREADS, SMEM_BYTES, st>>>(p->a_hi, p->a_lo, p->b_hi, p->b_lo, d_groups, (int)p->M, (int)p->N,
                                                  (int)p->K, epi, p->passes, p->Gb == 1 && p->G > 1 ? 1 : 0,
-                                                 p->splits, p->kchunk, p->partial);
+                                                 p->splits, p->kchunk, p->partial, p->conv.n ? p->conv.ho * p->conv.wo : 0);
     lcu_note_launch();
     if (p->splits > 1) {
         k_splitk_reduce<<<dim3(lcu_blocks(p->M * p->N, 256 * 4, 148 * 8), p->G), 256, 0, st>>>(d_groups, p->partial, p->splits,
-                                                                                               p->M, p->N, epi);
+                                                                                               p->M, p->N, epi,
+                                                                                               p->conv.n ? (size_t)p->conv.ho * p->conv.wo : 0);
         lcu_note_launch();
     }
     return lcu_launch_status();
@@ -392,6 +446,29 @@ extern "C" lancius_error lcu_gemm_tc(float* c, const float* a, const float* b, s
     if (e != LANCIUS_ERROR_OK) return e;
     e = lcu_gemm_tc_run(&p, d_group, epi, stream);
     // the host-side group record must stay valid until the copy ran
+    if (e == LANCIUS_ERROR_OK) e = lcu_check_cuda(cudaStreamSynchronize(st));
+    return e;
+}
+
+// Implicit-GEMM conv on the tensor cores: C[Co, N*Ho*Wo] = W[Co, Ci*Kh*Kw] * im2col(in),
+// stored straight into NCHW by the epilogue (ReLU fused). Scratch from the per-device cache.
+extern "C" lancius_error lcu_conv2d_tc(float* out, const float* in, const float* w, LcuConvShape cs, int relu, int mode,
+                                       void* stream) {
+    const int passes = mode == LCU_MODE_TF32 ? 1 : 3;
+    const size_t M = cs.co, K = (size_t)cs.ci * cs.kh * cs.kw, N = (size_t)cs.n * cs.ho * cs.wo;
+    const size_t need = lcu_gemm_tc_scratch_bytes(M, N, K, 1, 1, passes) + 256;
+    char* scratch = static_cast<char*>(lcu_scratch_acquire(need));
+    if (!scratch) { lancius_set_error(LANCIUS_ERROR_OOM); return LANCIUS_ERROR_OOM; }
+    LcuGemmGroup* d_group = reinterpret_cast<LcuGemmGroup*>(scratch + need - 256);
+    LcuGemmGroup h{w, in, out, nullptr, nullptr};
+    cudaStream_t st = lcu_as_stream(stream);
+    cudaError_t ce = cudaMemcpyAsync(d_group, &h, sizeof(h), cudaMemcpyHostToDevice, st);
+    if (ce != cudaSuccess) return lcu_check_cuda(ce);
+    LcuTcGemmPlan p;
+    lancius_error e = lcu_gemm_tc_prepare(&p, scratch, M, N, K, 1, 1, passes);
+    if (e != LANCIUS_ERROR_OK) return e;
+    p.conv = cs;
+    e = lcu_gemm_tc_run(&p, d_group, relu ? LCU_EPI_RELU : LCU_EPI_NONE, stream);
     if (e == LANCIUS_ERROR_OK) e = lcu_check_cuda(cudaStreamSynchronize(st));
     return e;
 }

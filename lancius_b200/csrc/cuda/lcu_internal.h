@@ -16,6 +16,8 @@ struct LcuAttnGroup { const float* q; const float* k; const float* v; float* o; 
 struct LcuEltGroup { float* out; const float* a; const float* b; };
 struct LcuRowGroup { float* out; const float* in; const float* gamma; const float* beta; };
 
+struct LcuConvShape { int n, ci, h, w, co, kh, kw, stride, pad, ho, wo; };   // n == 0: not a conv
+
 // A prepared tensor-core GEMM: TMA maps over the hi/lo scratch copies of A and B.
 struct LcuTcGemmPlan {
     CUtensorMap a_hi, a_lo, b_hi, b_lo;
@@ -24,6 +26,7 @@ struct LcuTcGemmPlan {
     int G, Gb, passes;
     int splits, kchunk;          // K cut into `splits` chunks of kchunk (multiple of 16)
     float* partial;              // [G][splits][M][N] partial sums when splits > 1
+    LcuConvShape conv;           // conv.n > 0: B is the im2col of groups[0].b, C is stored NCHW
 };
 
 extern "C" {
@@ -50,6 +53,8 @@ int lcu_gemm_watchdog_read_and_clear(void);
 int lcu_use_tensor_cores(size_t M, size_t N, size_t K);
 int lcu_attention_tc_supported(size_t D);
 int lcu_force_simt(void);
+lancius_error lcu_conv2d_tc(float* out, const float* in, const float* w, LcuConvShape cs, int relu, int mode, void* stream);
+void* lcu_scratch_acquire(size_t bytes);
 lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, const float* k, const float* v, float* o,
                                size_t B, size_t S, size_t H, int causal, void* stream);
 int lcu_attention_watchdog_read_and_clear(void);

@@ -58,11 +58,17 @@ lancius_error lcu_conv2d(float* out, const float* in, const float* w, size_t N, 
     if (!out || !in || !w) return bad(LANCIUS_ERROR_NULL_PTR);
     if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
     if (stride == 0 || H_in + 2 * pad < K_h || W_in + 2 * pad < K_w) return bad(LANCIUS_ERROR_SHAPE_MISMATCH);
+    size_t Ho = (H_in + 2 * pad - K_h) / stride + 1, Wo = (W_in + 2 * pad - K_w) / stride + 1;
+    if (N && C_in && lcu_use_tensor_cores(C_out, N * Ho * Wo, C_in * K_h * K_w)) {
+        LcuConvShape cs{(int)N, (int)C_in, (int)H_in, (int)W_in, (int)C_out, (int)K_h, (int)K_w, (int)stride, (int)pad,
+                        (int)Ho, (int)Wo};
+        return lcu_conv2d_tc(out, in, w, cs, relu, mode, stream);
+    }
     return lcu_conv2d_simt(out, in, w, N, C_in, H_in, W_in, C_out, K_h, K_w, stride, pad, relu, stream);
 }
 
 const char* lcu_build_info(void) {
-    return "lancius_b200 sm_100a: gemm_tcgen05_3xtf32 attention_tcgen05_3xtf32 gemm_simt conv_simt attention_simt layernorm softmax sum_axis1 maxpool eltwise";
+    return "lancius_b200 sm_100a: gemm_tcgen05_3xtf32 attention_tcgen05_3xtf32 conv_tcgen05_3xtf32 gemm_simt conv_simt attention_simt layernorm softmax sum_axis1 maxpool eltwise";
 }
 
 }  // extern "C"
