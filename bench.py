@@ -37,7 +37,7 @@ def peaks():
 
 
 # per-config workload description -------------------------------------------------
-def build(cfg, graph, rank):
+def build(cfg, graph, rank, world=1):
     from lancius_b200 import configs
     if cfg == "attention":
         return configs.attention(graph, batch=8, seq=512, heads=8, head_dim=64, seed=1 + 1000 * rank)
@@ -46,7 +46,11 @@ def build(cfg, graph, rank):
     if cfg == "conv":
         return configs.conv_stack(graph, batch=32, hw=224, seed=2 + 1000 * rank)
     if cfg == "encoder":
-        return configs.encoder(graph, batch=16, seq=512, layers=12, seed=3 + 1000 * rank)
+        return configs.encoder(graph, batch=16, seq=512, layers=12, seed=3, first=16 * rank)
+    if cfg == "encoder_b256":      # batch 256 sharded over the ranks
+        from lancius_b200.shard import shard_range
+        lo, hi = shard_range(256, rank, world)
+        return configs.encoder(graph, batch=hi - lo, seq=512, layers=12, seed=3, first=lo)
     if cfg.startswith("gemm"):
         return configs.gemm(graph, int(cfg[4:]), seed=4 + 1000 * rank)
     raise SystemExit(f"unknown config {cfg}")
@@ -57,6 +61,7 @@ METRIC = {
     "mlp": ("graph inferences/sec", "graphs/s", "mlp_784_256_10_b64_fp32"),
     "conv": ("conv stack TFLOP/s", "TFLOP/s", "conv_stack_b32_224_fp32"),
     "encoder": ("encoder TFLOP/s", "TFLOP/s", "encoder_bert_base_l12_b16_s512_fp32"),
+    "encoder_b256": ("encoder TFLOP/s", "TFLOP/s", "encoder_bert_base_l12_b256_s512_fp32_batch_sharded"),
 }
 
 
@@ -170,7 +175,7 @@ def run_b200(args, rank, world, local_rank):
 
     dev = L.Device(local_rank)
     g = L.Graph()
-    built = build(args.config, g, rank)
+    built = build(args.config, g, rank, world)
     sched = g.schedule()
     dev.set_graph_replay(True)
     dev.bind(sched)
@@ -251,6 +256,95 @@ def run_b200(args, rank, world, local_rank):
     return built, total_ms, e2e_ms, dev_ms, launches_per_step, clk, in_bytes, out_bytes, dist
 
 
+def run_colsplit(args, rank, world, local_rank, n):
+    """GEMM n^3 split by columns over the ranks: lcu_gemm_colsplit = local 3xTF32 GEMM on
+    the rank's slab + NCCL all-gather + repack. Total work fixed (strong scaling)."""
+    import torch
+    import torch.distributed as dist
+    import lancius_b200 as L
+    from lancius_b200 import data
+    torch.cuda.set_device(local_rank)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    lib = L.load()
+    uid = C.create_string_buffer(128)
+    if rank == 0:
+        assert lib.lcu_comm_unique_id(uid, 128) == 0
+    t = torch.tensor(list(uid.raw), dtype=torch.uint8, device="cuda")
+    dist.broadcast(t, 0)
+    comm = lib.lcu_comm_create(world, rank, C.c_char_p(bytes(t.cpu().tolist())), local_rank)
+    assert comm, "lcu_comm_create failed"
+    ns = n // world
+    a_h = data.uniform(data.sub_seed(4, 1), (n, n), -1, 1).astype(np.float32)
+    b_full = data.uniform(data.sub_seed(4, 2), (n, n), -1, 1).astype(np.float32)
+    b_h = np.ascontiguousarray(b_full[:, rank * ns:(rank + 1) * ns])
+    del b_full
+    a = torch.from_numpy(a_h).cuda()
+    b = torch.from_numpy(b_h).cuda()
+    c = torch.empty((n, n), device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device="cuda")
+
+    def step():
+        rc = lib.lcu_gemm_colsplit(comm, C.c_void_p(c.data_ptr()), C.c_void_p(a.data_ptr()), C.c_void_p(b.data_ptr()),
+                                   n, n, n, 0, sp)
+        assert rc == 0, rc
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    dist.barrier()
+    evs = []
+    clocks = Clocks(local_rank)
+    clocks.start()
+    for _ in range(args.steps):
+        flush.fill_(1.0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(); step(); e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    dist.barrier()
+    clk = clocks.stop()
+    total_ms = sum(e0.elapsed_time(e1) for e0, e1 in evs)
+    # e2e: pinned host A and slab in, full C out, every step
+    a_pin, b_pin, c_pin = (torch.empty(x.shape, dtype=torch.float32).pin_memory() for x in (a_h, b_h, a_h))
+    a_pin.copy_(torch.from_numpy(a_h)); b_pin.copy_(torch.from_numpy(b_h))
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        a.copy_(a_pin, non_blocking=True); b.copy_(b_pin, non_blocking=True)
+        step()
+        c_pin.copy_(c, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    tt = torch.tensor([total_ms, e2e_ms], device="cuda")
+    dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+    total_ms, e2e_ms = tt.tolist()
+    lib.lcu_comm_destroy(comm)
+    if rank == 0:
+        flops = 2.0 * n ** 3
+        pk = peaks()
+        val = flops / (total_ms / 1e3 / args.steps) / 1e12
+        line = {
+            "metric": "GEMM TFLOP/s", "value": round(val, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded U[-1,1), splitmix64)",
+            "config": {"workload": f"gemm{n}_square_fp32_column_split_allgather", "mode": "fp32_exact",
+                       "l2": "flushed between timed steps (256 MiB write)", "parallelism": f"column-split x{world}"},
+            "roofline": {"bound": "tensor", "achieved": round(val / world, 2), "peak": pk["bf16_tflops"],
+                         "unit": "TFLOP/s per GPU", "frac": round(val / world / pk["bf16_tflops"], 4), "traffic": None,
+                         "peak_src": pk["src"] + " bf16 (3xTF32 issues 3 TF32 MMAs per product)"},
+            "cpu_baseline": None,
+            "e2e": {"value": round(flops / (e2e_ms / 1e3 / args.steps) / 1e12, 3), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": int(a_h.nbytes + b_h.nbytes), "d2h_bytes_per_step": int(4 * n * n)},
+            "gpu_launches": 4 * args.steps, "clocks": clk,
+        }
+        print(json.dumps(line))
+    dist.destroy_process_group()
+
+
 def _is_activation(cfg, node):
     # per-step inputs (weights stay resident): attention Q/K/V, conv/mlp/encoder X, gemm A and B
     return True if cfg in ("attention",) or cfg.startswith("gemm") else node.id == 0
@@ -278,6 +372,9 @@ def main():
         print(json.dumps(res))
         return
 
+    if args.config.startswith("gemm") and world > 1:
+        run_colsplit(args, rank, world, local_rank, int(args.config[4:]))
+        return
     built, total_ms, e2e_ms, dev_ms, launches, clk, in_b, out_b, dist = run_b200(args, rank, world, local_rank)
     if rank != 0:
         if dist:
@@ -309,7 +406,8 @@ def main():
     line = {
         "metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded N(0,1), splitmix64)",
+        "scaling": "strong" if args.config == "encoder_b256" else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1), splitmix64)",
         "config": {"workload": workload, "per_gpu_batch": built.meta.get("batch"), "mode": "fp32_exact",
                    "l2": "flushed between timed steps (256 MiB write)", "parallelism": f"batch-sharded x{world}"},
         "roofline": roof,

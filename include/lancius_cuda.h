@@ -112,6 +112,22 @@ lancius_error lcu_sum_axis1(float* out, const float* in, size_t rows, size_t col
 lancius_error lcu_maxpool2d(float* out, const float* in, size_t N, size_t C, size_t H_in, size_t W_in,
                             size_t K, size_t stride, void* stream);
 
+/* ---- multi-GPU: column-split GEMM with an NCCL all-gather over NVLink -------
+ * No counterpart in the reference (CPU only, distributed execution deferred,
+ * KNOWN_LIMITATIONS.md:24); the BASELINE sweep splits the 16384^3 GEMM by columns.
+ * One process (or thread) per GPU. Rank 0 creates the id and shares its 128 bytes
+ * with the others out of band (torch.distributed, a file, MPI ...). */
+typedef struct lcu_comm lcu_comm;
+lancius_error lcu_comm_unique_id(void* out, size_t bytes);            /* bytes >= 128 */
+lcu_comm* lcu_comm_create(int nranks, int rank, const void* unique_id, int device);
+void lcu_comm_destroy(lcu_comm* comm);
+void lcu_comm_abort(lcu_comm* comm);      /* failure path: peers gone; never blocks */
+int lcu_comm_size(const lcu_comm* comm);
+/* C [M, N] on every rank = A [M, K] * [B_0 | B_1 | ...]; this rank passes its slab
+ * b_slab [K, N / nranks]. N % nranks == 0. */
+lancius_error lcu_gemm_colsplit(lcu_comm* comm, float* c, const float* a, const float* b_slab, size_t M, size_t K,
+                                size_t N, int mode, void* stream);
+
 /* lcu_matmul without device allocation (no counterpart in the reference, whose
  * kernels run on the host). For callers that may not call cudaMalloc once they are
  * running -- device memory owned by another allocator or a fixed memory budget.

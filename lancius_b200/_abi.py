@@ -130,6 +130,12 @@ B200_FUNCS = {
     "lcu_sum_axis1": (C.c_int, [P, P, c_size, c_size, P]),
     "lcu_maxpool2d": (C.c_int, [P, P, c_size, c_size, c_size, c_size, c_size, c_size, P]),
     "lcu_build_info": (C.c_char_p, []),
+    "lcu_comm_unique_id": (C.c_int, [P, c_size]),
+    "lcu_comm_create": (P, [C.c_int, C.c_int, P, C.c_int]),
+    "lcu_comm_destroy": (None, [P]),
+    "lcu_comm_abort": (None, [P]),
+    "lcu_comm_size": (C.c_int, [P]),
+    "lcu_gemm_colsplit": (C.c_int, [P, P, P, P, c_size, c_size, c_size, C.c_int, P]),
     "lcu_matmul_noalloc": (C.c_int, [P, P, P, c_size, c_size, c_size, P, C.c_int, C.c_int, P]),
     "lcu_noalloc_scratch_capacity": (c_size, []),
 }

@@ -105,14 +105,15 @@ def conv_stack(g, batch=32, hw=224, seed=2, fuse=True):
     return b
 
 
-def encoder(g, batch=16, seq=512, layers=12, d_model=768, heads=12, ffn=3072, seed=3):
+def encoder(g, batch=16, seq=512, layers=12, d_model=768, heads=12, ffn=3072, seed=3, first=0):
     """Config 4: pre-LN BERT-shape encoder, GELU FFN, unmasked attention, eps 1e-5.
 
     One subgraph per batch element (the IR has no slice op); weight INPUT nodes are
-    shared by all batch elements."""
+    shared by all batch elements. `first` numbers the batch elements from there (a
+    rank's shard of a larger batch draws the same sequences as the full batch)."""
     b = Built("encoder", g)
     hd = d_model // heads
-    xs = [_inp(b, g.input(seq, d_model), data.normal(data.sub_seed(seed, 100000 + e), (seq, d_model)))
+    xs = [_inp(b, g.input(seq, d_model), data.normal(data.sub_seed(seed, 100000 + first + e), (seq, d_model)))
           for e in range(batch)]
     k = 0
 

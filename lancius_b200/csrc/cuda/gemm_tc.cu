@@ -415,12 +415,12 @@ std::mutex g_scratch_mu;
 std::vector<ScratchCache> g_scratch;
 }
 
-extern "C" void* lcu_scratch_acquire(size_t bytes) {
+static void* acquire_from(std::vector<ScratchCache>& cache, size_t bytes) {
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lk(g_scratch_mu);
-    if ((int)g_scratch.size() <= dev) g_scratch.resize(dev + 1);
-    ScratchCache& c = g_scratch[dev];
+    if ((int)cache.size() <= dev) cache.resize(dev + 1);
+    ScratchCache& c = cache[dev];
     if (c.bytes < bytes) {
         if (c.p) { cudaDeviceSynchronize(); cudaFree(c.p); c.p = nullptr; c.bytes = 0; }
         if (cudaMalloc(&c.p, bytes) != cudaSuccess) { cudaGetLastError(); c.p = nullptr; return nullptr; }
@@ -428,6 +428,12 @@ extern "C" void* lcu_scratch_acquire(size_t bytes) {
     }
     return c.p;
 }
+
+namespace { std::vector<ScratchCache> g_gather; }
+// Per-device cached buffers that grow on demand: GEMM/conv operand scratch, and a
+// second one for the column-split all-gather (both alive during one colsplit call).
+extern "C" void* lcu_scratch_acquire(size_t bytes) { return acquire_from(g_scratch, bytes); }
+extern "C" void* lcu_scratch_acquire_gather(size_t bytes) { return acquire_from(g_gather, bytes); }
 
 extern "C" lancius_error lcu_gemm_tc(float* c, const float* a, const float* b, size_t M, size_t K, size_t N,
                                      const float* bias, int epi, int mode, void* stream) {

@@ -55,6 +55,7 @@ int lcu_attention_tc_supported(size_t D);
 int lcu_force_simt(void);
 lancius_error lcu_conv2d_tc(float* out, const float* in, const float* w, LcuConvShape cs, int relu, int mode, void* stream);
 void* lcu_scratch_acquire(size_t bytes);
+void* lcu_scratch_acquire_gather(size_t bytes);
 lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, const float* k, const float* v, float* o,
                                size_t B, size_t S, size_t H, int causal, void* stream);
 int lcu_attention_watchdog_read_and_clear(void);
