@@ -132,6 +132,17 @@ class Clocks:
 
 
 # CPU baseline: the reference's own code (oracle/_ref) on this host's cores -----------
+def _all_host_threads():
+    """torchrun sets OMP_NUM_THREADS=1 for multi-rank jobs; the reference CPU path must
+    use every host core, so raise the OpenMP team size explicitly."""
+    try:
+        gomp = C.CDLL("libgomp.so.1")
+        gomp.omp_set_num_threads(os.cpu_count())
+    except OSError:
+        pass
+    return os.cpu_count()
+
+
 def cpu_baseline(cfg, steps=None):
     """Times the reference's arena-mode executor on a bounded sample of the workload.
     Returns (value in the metric's unit, description dict)."""
@@ -140,7 +151,7 @@ def cpu_baseline(cfg, steps=None):
     if not oracle.reference_available():
         return None
     ref = oracle.reference()
-    cores = os.cpu_count()
+    cores = _all_host_threads()
     if cfg == "attention":
         # sample: 2 of the 8 batch elements (one ATTENTION node each), scaled per graph
         g = Graph(ref)
@@ -158,7 +169,7 @@ def cpu_baseline(cfg, steps=None):
         return val, {"kind": "reference", "cores": cores,
                      "sample": f"{reps} runs of 2 of 8 batch elements (S512 H8 D64 causal) through "
                                "lancius_schedule_execute, scaled x4 to one batch-8 graph; "
-                               f"OMP threads = {os.environ.get('OMP_NUM_THREADS', cores)}"}
+                               f"OpenMP threads = {cores}"}
     return None
 
 
@@ -430,6 +441,7 @@ def reference_arm(args, metric, unit, workload):
     if args.config != "attention":
         return {"impl": "reference", "unavailable": f"reference arm implemented for the attention workload only"}
     ref = oracle.reference()
+    _all_host_threads()
     g = Graph(ref)
     b = configs.attention(g, batch=8, seq=512, heads=8, head_dim=64, seed=1)
     b.bind_host()
