@@ -12,13 +12,16 @@
 //              gives the same softmax, so this is exact, and P stays <= 256.
 //   warp 4     TMEM allocation + MMA issue (one lane), in the order
 //                S_0, S_1, PV_0, S_2, PV_1, ...
-//              S_j = Q K_j^T (A = Q from TMEM), O += P_j V_j (A = P_j from TMEM);
-//              each product is 3 passes: lo*hi + hi*lo + hi*hi
+//              S_j = Q K_j^T (A = Q from TMEM), O += P_j V_j (A = P_j from TMEM).
+//              tcgen05 costs about the same per instruction whatever its N, so the
+//              hi/lo halves of B are concatenated along N: Q_hi*[K_hi|K_lo] and
+//              Q_lo*[K_hi|K_lo] (N = 128) accumulate hh+lh in the left and hl+ll in
+//              the right half of S, and S = left + right; same for P*[V_hi|V_lo] into O
 //   warps 5-8  loaders: K_j, V_j from global (coalesced float4, next tile prefetched
 //              into registers), split hi/lo, stored in the swizzled layouts tcgen05
 //              reads (K: K-major 128B swizzle; V: N-major 128B swizzle, 32B atoms)
-// TMEM columns: Q hi [0,64) lo [64,128); S [128,192); O [192,256);
-// P buffers (double) hi/lo [256,384) and [384,512). Every mbarrier wait is bounded.
+// TMEM columns: Q hi [0,64) lo [64,128); S halves [128,256); O halves [256,384);
+// P hi [384,448) lo [448,512). Every mbarrier wait is bounded.
 #include "tc_common.cuh"
 
 namespace {
@@ -28,7 +31,7 @@ constexpr int THREADS = 288;
 constexpr int KV_HALF = BKV * D * 4;            // 16 KB: one hi or lo tile
 constexpr int STAGE = 2 * KV_HALF;              // hi + lo
 constexpr int SMEM_BYTES = 2 * NS * STAGE + 1024 + 512;
-constexpr uint32_t TM_QHI = 0, TM_QLO = 64, TM_S = 128, TM_O = 192, TM_P = 256, TM_COLS = 512;
+constexpr uint32_t TM_QHI = 0, TM_QLO = 64, TM_S = 128, TM_O = 256, TM_P = 384, TM_COLS = 512;
 constexpr float RESCALE_THRESHOLD = 8.0f;       // log2 units
 
 __device__ int g_attn_watchdog = 0;
@@ -49,15 +52,19 @@ __device__ __forceinline__ unsigned long long gtime() { unsigned long long t; as
 struct Bars {
     uint64_t k_full[NS], k_empty[NS], v_full[NS], v_empty[NS];
     uint64_t s_full, s_free, q_ready, drain;
-    uint64_t p_ready[2], pv_done[2];   // per P buffer: keeps every waiter within one phase
+    uint64_t p_ready, pv_done;
     uint32_t tmem;
     int abort;
 };
 
-__device__ __forceinline__ uint32_t k_off(int j, int d) {     // K-major, 128B swizzle, 2 atoms of 32 d
-    return (uint32_t)((d >> 5) * (BKV * 128) + j * 128 + ((((d & 31) >> 2) ^ (j & 7)) << 4));
+// K stage: per 32-d atom, 128 rows of 128 B: rows 0-63 = K_hi keys, rows 64-127 = K_lo keys
+// (K-major, 128B swizzle), so one descriptor spans [K_hi | K_lo] as N = 128.
+__device__ __forceinline__ uint32_t k_off(int row, int d) {
+    return (uint32_t)((d >> 5) * (2 * BKV * 128) + row * 128 + ((((d & 31) >> 2) ^ (row & 7)) << 4));
 }
-__device__ __forceinline__ uint32_t v_off(int j, int d) {     // N-major, 128B swizzle of 32B atoms
+// V stage: 32-d chunks of 64 key rows (N-major, 128B swizzle of 32B atoms); V_hi fills
+// chunks 0-1 and V_lo chunks 2-3, so one descriptor spans [V_hi | V_lo] as N = 128.
+__device__ __forceinline__ uint32_t v_off(int j, int d) {
     return (uint32_t)((d >> 5) * (BKV * 128) + j * 128 + ((((d & 31) >> 3) ^ (j & 3)) << 5) + ((d & 7) << 2));
 }
 // TF32 split: hi keeps the top 10 mantissa bits (exactly what the tensor core reads),
@@ -101,7 +108,8 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
         tc::mbar_init(&bar->s_full, 1);
         tc::mbar_init(&bar->s_free, 128);
         tc::mbar_init(&bar->q_ready, 128);
-        for (int b = 0; b < 2; b++) { tc::mbar_init(&bar->p_ready[b], 128); tc::mbar_init(&bar->pv_done[b], 1); }
+        tc::mbar_init(&bar->p_ready, 128);
+        tc::mbar_init(&bar->pv_done, 1);
         tc::mbar_init(&bar->drain, 1);
         bar->abort = 0;
         tc::fence_barrier_init();
@@ -145,12 +153,13 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
             if (threadIdx.x == 0 && j < 8) TRACE(2 + 4 * j);
             tc::tc_fence_after();
             float s[64];
-            {
-                float a[32], b[32];
-                tc::tmem_ld32(lb + TM_S, a);
-                tc::tmem_ld32(lb + TM_S + 32, b);
 #pragma unroll
-                for (int c = 0; c < 32; c++) { s[c] = a[c] * scale_log2; s[32 + c] = b[c] * scale_log2; }
+            for (int half = 0; half < 2; half++) {
+                float a[32], b[32];
+                tc::tmem_ld32(lb + TM_S + half * 32, a);         // Q_hi K_hi + Q_lo K_hi
+                tc::tmem_ld32(lb + TM_S + 64 + half * 32, b);    // Q_hi K_lo + Q_lo K_lo
+#pragma unroll
+                for (int c = 0; c < 32; c++) s[half * 32 + c] = (a[c] + b[c]) * scale_log2;
             }
             tc::tc_fence_before();
             tc::mbar_arrive(&bar->s_free);               // the MMA warp may overwrite S now
@@ -168,10 +177,10 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                 const float mn = raise ? mx : m;
                 const float f = ex2(m - mn);             // 0 on the first tile, 1 for rows that keep m
                 if (j > 0) {   // O holds P_0..P_{j-1} V: wait for it, rescale the rows that moved
-                    if (!tc::mbar_wait(&bar->pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, abort, &g_attn_watchdog, 12)) { ok = false; break; }
+                    if (!tc::mbar_wait(&bar->pv_done, (j - 1) & 1, abort, &g_attn_watchdog, 12)) { ok = false; break; }
                     tc::tc_fence_after();
 #pragma unroll 1
-                    for (int half = 0; half < 2; half++) {
+                    for (int half = 0; half < 4; half++) {
                         float o[32];
                         tc::tmem_ld32(lb + TM_O + half * 32, o);
 #pragma unroll
@@ -185,9 +194,9 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
             }
             if (threadIdx.x == 0 && j < 8) TRACE(3 + 4 * j);
             float rsum = 0.f;
-            const uint32_t pb = lb + TM_P + (uint32_t)(j & 1) * 128;
-            // P buffer j&1 was last read by PV_{j-2}
-            if (j >= 2 && !tc::mbar_wait(&bar->pv_done[j & 1], ((j - 2) >> 1) & 1, abort, &g_attn_watchdog, 14)) { ok = false; break; }
+            const uint32_t pb = lb + TM_P;
+            // the P columns were last read by PV_{j-1}
+            if (j >= 1 && !tc::mbar_wait(&bar->pv_done, (j - 1) & 1, abort, &g_attn_watchdog, 14)) { ok = false; break; }
 #pragma unroll
             for (int half = 0; half < 2; half++) {
                 float hi[32], lo[32];
@@ -205,16 +214,19 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
             if (threadIdx.x == 0 && j < 8) TRACE(4 + 4 * j);
             tc::tmem_st_wait();
             tc::tc_fence_before();
-            tc::mbar_arrive(&bar->p_ready[j & 1]);
+            tc::mbar_arrive(&bar->p_ready);
             if (threadIdx.x == 0 && j < 8) TRACE(5 + 4 * j);
         }
-        if (ok && T > 0 && tc::mbar_wait(&bar->pv_done[(T - 1) & 1], ((T - 1) >> 1) & 1, abort, &g_attn_watchdog, 13)) {
+        if (ok && T > 0 && tc::mbar_wait(&bar->pv_done, (T - 1) & 1, abort, &g_attn_watchdog, 13)) {
             tc::tc_fence_after();
             const float inv = 1.f / l;
 #pragma unroll 1
             for (int half = 0; half < 2; half++) {
-                float o[32];
-                tc::tmem_ld32(lb + TM_O + half * 32, o);
+                float o[32], o2[32];
+                tc::tmem_ld32(lb + TM_O + half * 32, o);         // P_hi V_hi + P_lo V_hi
+                tc::tmem_ld32(lb + TM_O + 64 + half * 32, o2);   // P_hi V_lo + P_lo V_lo
+#pragma unroll
+                for (int c = 0; c < 32; c++) o[c] += o2[c];
                 if (qi < S) {
                     float4* dst = reinterpret_cast<float4*>(p.o + (size_t)qi * rs + (size_t)h * D + half * 32);
 #pragma unroll
@@ -226,23 +238,21 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
     } else if (warp == 4) {
         // ======================= MMA issuer =======================
         if (lane == 0) {
-            constexpr uint32_t id_s = tc::idesc_tf32(BQ, BKV, false, false);
-            constexpr uint32_t id_o = tc::idesc_tf32(BQ, D, false, true);
+            constexpr uint32_t id_s = tc::idesc_tf32(BQ, 2 * BKV, false, false);
+            constexpr uint32_t id_o = tc::idesc_tf32(BQ, 2 * D, false, true);
             bool ok = tc::mbar_wait(&bar->q_ready, 0, abort, &g_attn_watchdog, 21);
             auto issue_s = [&](int j) -> bool {
                 const int st = j % NS;
                 if (!tc::mbar_wait(&bar->k_full[st], (j / NS) & 1, abort, &g_attn_watchdog, 22)) return false;
                 if (j >= 1 && !tc::mbar_wait(&bar->s_free, (j - 1) & 1, abort, &g_attn_watchdog, 23)) return false;
                 tc::tc_fence_after();
-                const uint32_t khi = tc::smem_u32(kst + st * STAGE), klo = khi + KV_HALF;
+                const uint32_t kb0 = tc::smem_u32(kst + st * STAGE);
 #pragma unroll
                 for (int kb = 0; kb < D / 8; kb++) {
-                    const uint32_t off = (uint32_t)((kb >> 2) * (BKV * 128) + (kb & 3) * 32);
-                    const uint64_t bh = tc::smem_desc(khi + off, 16, 1024, tc::SWZ_128B);
-                    const uint64_t bl = tc::smem_desc(klo + off, 16, 1024, tc::SWZ_128B);
-                    tc::mma_tf32_ts(tm + TM_S, tm + TM_QLO + kb * 8, bh, id_s, kb ? 1u : 0u);
-                    tc::mma_tf32_ts(tm + TM_S, tm + TM_QHI + kb * 8, bl, id_s, 1u);
-                    tc::mma_tf32_ts(tm + TM_S, tm + TM_QHI + kb * 8, bh, id_s, 1u);
+                    const uint32_t off = (uint32_t)((kb >> 2) * (2 * BKV * 128) + (kb & 3) * 32);
+                    const uint64_t bk = tc::smem_desc(kb0 + off, 16, 1024, tc::SWZ_128B);   // [K_hi | K_lo]
+                    tc::mma_tf32_ts(tm + TM_S, tm + TM_QLO + kb * 8, bk, id_s, kb ? 1u : 0u);
+                    tc::mma_tf32_ts(tm + TM_S, tm + TM_QHI + kb * 8, bk, id_s, 1u);
                 }
                 tc::mma_commit(&bar->s_full);
                 tc::mma_commit(&bar->k_empty[st]);
@@ -253,21 +263,19 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
             for (int j = 0; j < T && ok; j++) {
                 if (j + 1 < T && !(ok = issue_s(j + 1))) break;
                 const int st = j % NS;
-                if (!tc::mbar_wait(&bar->p_ready[j & 1], (j >> 1) & 1, abort, &g_attn_watchdog, 24) ||
+                if (!tc::mbar_wait(&bar->p_ready, j & 1, abort, &g_attn_watchdog, 24) ||
                     !tc::mbar_wait(&bar->v_full[st], (j / NS) & 1, abort, &g_attn_watchdog, 25)) { ok = false; break; }
                 tc::tc_fence_after();
-                const uint32_t vhi = tc::smem_u32(vst + st * STAGE), vlo = vhi + KV_HALF;
-                const uint32_t pb = tm + TM_P + (uint32_t)(j & 1) * 128;
+                const uint32_t vb0 = tc::smem_u32(vst + st * STAGE);
+                const uint32_t pb = tm + TM_P;
 #pragma unroll
                 for (int kb = 0; kb < BKV / 8; kb++) {
-                    const uint64_t bh = tc::smem_desc(vhi + kb * 1024, BKV * 128, 512, tc::SWZ_128B_BASE32B);
-                    const uint64_t bl = tc::smem_desc(vlo + kb * 1024, BKV * 128, 512, tc::SWZ_128B_BASE32B);
+                    const uint64_t bv = tc::smem_desc(vb0 + kb * 1024, BKV * 128, 512, tc::SWZ_128B_BASE32B);   // [V_hi | V_lo]
                     const uint32_t acc0 = (j | kb) ? 1u : 0u;
-                    tc::mma_tf32_ts(tm + TM_O, pb + 64 + kb * 8, bh, id_o, acc0);
-                    tc::mma_tf32_ts(tm + TM_O, pb + kb * 8, bl, id_o, 1u);
-                    tc::mma_tf32_ts(tm + TM_O, pb + kb * 8, bh, id_o, 1u);
+                    tc::mma_tf32_ts(tm + TM_O, pb + 64 + kb * 8, bv, id_o, acc0);
+                    tc::mma_tf32_ts(tm + TM_O, pb + kb * 8, bv, id_o, 1u);
                 }
-                tc::mma_commit(&bar->pv_done[j & 1]);
+                tc::mma_commit(&bar->pv_done);
                 if (j < 8) TRACE(42 + j);
                 tc::mma_commit(&bar->v_empty[st]);
             }
@@ -301,9 +309,8 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                 float x[4] = {kn[c].x, kn[c].y, kn[c].z, kn[c].w}, hi[4], lo[4];
 #pragma unroll
                 for (int u = 0; u < 4; u++) { hi[u] = hi_part(x[u]); lo[u] = x[u] - hi[u]; }
-                const uint32_t o = k_off(jr, d0 + 4 * c);
-                *reinterpret_cast<float4*>(kh + o) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<float4*>(kh + KV_HALF + o) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+                *reinterpret_cast<float4*>(kh + k_off(jr, d0 + 4 * c)) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<float4*>(kh + k_off(jr + BKV, d0 + 4 * c)) = make_float4(lo[0], lo[1], lo[2], lo[3]);
             }
             tc::fence_proxy_async();
             tc::mbar_arrive(&bar->k_full[st]);
