@@ -51,7 +51,7 @@ __device__ __forceinline__ unsigned long long gtime() { unsigned long long t; as
 
 struct Bars {
     uint64_t k_full[NS], k_empty[NS], v_full[NS], v_empty[NS];
-    uint64_t s_full, s_free, q_ready, drain;
+    uint64_t s_full, s_free, q_ready, o_free, drain;
     uint64_t p_ready, pv_done;
     uint32_t tmem;
     int abort;
@@ -76,8 +76,29 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
+struct Item { LcuAttnGroup p; int h, q0, T; };
+
+// Work item i of the persistent grid: heaviest query tiles first (causal cost grows
+// with the tile index), then batch element, then head.
+__device__ __forceinline__ Item get_item(int i, const LcuAttnGroup* table, const LcuAttnGroup& base, size_t bstride,
+                                         int B, int H, int nqt, int S, int causal) {
+    Item it;
+    const int per = B * H;
+    const int qt = nqt - 1 - i / per, r = i % per, b = r / H;
+    it.h = r % H;
+    if (table) it.p = table[b];
+    else {
+        size_t off = (size_t)b * bstride;
+        it.p.q = base.q + off; it.p.k = base.k + off; it.p.v = base.v + off; it.p.o = base.o + off;
+    }
+    it.q0 = qt * BQ;
+    const int kv_end = causal ? min(S, it.q0 + BQ) : S;
+    it.T = (kv_end + BKV - 1) / BKV;
+    return it;
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
-k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstride, int S, int H, int causal,
+k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstride, int B, int S, int H, int causal,
           float scale_log2) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -85,18 +106,9 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
     uint8_t* vst = tiles + NS * STAGE;             // NS stages of V hi|lo
     Bars* bar = reinterpret_cast<Bars*>(tiles + 2 * NS * STAGE);
 
-    LcuAttnGroup p;
-    if (table) p = table[blockIdx.z];
-    else {
-        size_t off = (size_t)blockIdx.z * bstride;
-        p.q = base.q + off; p.k = base.k + off; p.v = base.v + off; p.o = base.o + off;
-    }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = blockIdx.y;
-    const int qt = gridDim.x - 1 - blockIdx.x;      // longest (causal) tiles first
-    const int q0 = qt * BQ;
-    const int kv_end = causal ? min(S, q0 + BQ) : S;
-    const int T = (kv_end + BKV - 1) / BKV;
+    const int nqt = (S + BQ - 1) / BQ;
+    const int n_items = nqt * B * H;
     const size_t rs = (size_t)H * D;                // row stride of [S, H, D]
     volatile int* abort = &bar->abort;
 
@@ -108,6 +120,7 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
         tc::mbar_init(&bar->s_full, 1);
         tc::mbar_init(&bar->s_free, 128);
         tc::mbar_init(&bar->q_ready, 128);
+        tc::mbar_init(&bar->o_free, 128);
         tc::mbar_init(&bar->p_ready, 128);
         tc::mbar_init(&bar->pv_done, 1);
         tc::mbar_init(&bar->drain, 1);
@@ -121,130 +134,137 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
     const uint32_t tm = bar->tmem;
     if (threadIdx.x == 0) TRACE(0);
 
+    // Every role walks the same item sequence; `gt` numbers this CTA's key tiles across
+    // items and drives all ring stages and barrier phases.
     if (warp < 4) {
         // ======================= softmax warps =======================
         const int row = 32 * warp + lane;              // TMEM lane == query row in tile
-        const int qi = q0 + row;
         const uint32_t lb = tm + ((uint32_t)(32 * warp) << 16);
-        {   // Q row -> TMEM hi/lo
-            float hi[32], lo[32];
-#pragma unroll 1
-            for (int half = 0; half < 2; half++) {
-                const float4* src = reinterpret_cast<const float4*>(p.q + (size_t)qi * rs + (size_t)h * D + half * 32);
-#pragma unroll
-                for (int c = 0; c < 8; c++) {
-                    float4 v = qi < S ? __ldg(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-                    float x[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                    for (int t = 0; t < 4; t++) { hi[4 * c + t] = hi_part(x[t]); lo[4 * c + t] = x[t] - hi[4 * c + t]; }
-                }
-                tc::tmem_st32(lb + TM_QHI + half * 32, hi);
-                tc::tmem_st32(lb + TM_QLO + half * 32, lo);
-            }
-            tc::tmem_st_wait();
-            tc::tc_fence_before();
-            tc::mbar_arrive(&bar->q_ready);
-            if (threadIdx.x == 0) TRACE(1);
-        }
-        float m = -INFINITY, l = 0.f;
+        int gt = 0;
         bool ok = true;
-        for (int j = 0; j < T && ok; j++) {
-            if (!tc::mbar_wait(&bar->s_full, j & 1, abort, &g_attn_watchdog, 11)) { ok = false; break; }
-            if (threadIdx.x == 0 && j < 8) TRACE(2 + 4 * j);
-            tc::tc_fence_after();
-            float s[64];
-#pragma unroll
-            for (int half = 0; half < 2; half++) {
-                float a[32], b[32];
-                tc::tmem_ld32(lb + TM_S + half * 32, a);         // Q_hi K_hi + Q_lo K_hi
-                tc::tmem_ld32(lb + TM_S + 64 + half * 32, b);    // Q_hi K_lo + Q_lo K_lo
-#pragma unroll
-                for (int c = 0; c < 32; c++) s[half * 32 + c] = (a[c] + b[c]) * scale_log2;
-            }
-            tc::tc_fence_before();
-            tc::mbar_arrive(&bar->s_free);               // the MMA warp may overwrite S now
-            const int k0 = j * BKV;
-            if (k0 + BKV > S || (causal && k0 + BKV - 1 > q0)) {   // tile touches the diagonal or the end
-#pragma unroll
-                for (int c = 0; c < 64; c++)
-                    if (k0 + c >= S || (causal && k0 + c > qi)) s[c] = -INFINITY;
-            }
-            float mx = s[0];
-#pragma unroll
-            for (int c = 1; c < 64; c++) mx = fmaxf(mx, s[c]);
-            const bool raise = mx > m + RESCALE_THRESHOLD;
-            if (__any_sync(0xffffffffu, raise)) {
-                const float mn = raise ? mx : m;
-                const float f = ex2(m - mn);             // 0 on the first tile, 1 for rows that keep m
-                if (j > 0) {   // O holds P_0..P_{j-1} V: wait for it, rescale the rows that moved
-                    if (!tc::mbar_wait(&bar->pv_done, (j - 1) & 1, abort, &g_attn_watchdog, 12)) { ok = false; break; }
-                    tc::tc_fence_after();
-#pragma unroll 1
-                    for (int half = 0; half < 4; half++) {
-                        float o[32];
-                        tc::tmem_ld32(lb + TM_O + half * 32, o);
-#pragma unroll
-                        for (int c = 0; c < 32; c++) o[c] *= f;
-                        tc::tmem_st32(lb + TM_O + half * 32, o);
-                    }
-                    tc::tmem_st_wait();
-                }
-                l *= f;
-                m = mn;
-            }
-            if (threadIdx.x == 0 && j < 8) TRACE(3 + 4 * j);
-            float rsum = 0.f;
-            const uint32_t pb = lb + TM_P;
-            // the P columns were last read by PV_{j-1}
-            if (j >= 1 && !tc::mbar_wait(&bar->pv_done, (j - 1) & 1, abort, &g_attn_watchdog, 14)) { ok = false; break; }
-#pragma unroll
-            for (int half = 0; half < 2; half++) {
+        for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+            const Item it = get_item(i, table, base, bstride, B, H, nqt, S, causal);
+            const int qi = it.q0 + row;
+            {   // Q row -> TMEM hi/lo (the previous item is fully read out at this point)
                 float hi[32], lo[32];
-#pragma unroll
-                for (int c = 0; c < 32; c++) {
-                    float e = ex2(s[half * 32 + c] - m);
-                    rsum += e;
-                    hi[c] = hi_part(e);
-                    lo[c] = e - hi[c];
-                }
-                tc::tmem_st32(pb + half * 32, hi);
-                tc::tmem_st32(pb + 64 + half * 32, lo);
-            }
-            l += rsum;
-            if (threadIdx.x == 0 && j < 8) TRACE(4 + 4 * j);
-            tc::tmem_st_wait();
-            tc::tc_fence_before();
-            tc::mbar_arrive(&bar->p_ready);
-            if (threadIdx.x == 0 && j < 8) TRACE(5 + 4 * j);
-        }
-        if (ok && T > 0 && tc::mbar_wait(&bar->pv_done, (T - 1) & 1, abort, &g_attn_watchdog, 13)) {
-            tc::tc_fence_after();
-            const float inv = 1.f / l;
 #pragma unroll 1
-            for (int half = 0; half < 2; half++) {
-                float o[32], o2[32];
-                tc::tmem_ld32(lb + TM_O + half * 32, o);         // P_hi V_hi + P_lo V_hi
-                tc::tmem_ld32(lb + TM_O + 64 + half * 32, o2);   // P_hi V_lo + P_lo V_lo
+                for (int half = 0; half < 2; half++) {
+                    const float4* src = reinterpret_cast<const float4*>(it.p.q + (size_t)qi * rs + (size_t)it.h * D + half * 32);
 #pragma unroll
-                for (int c = 0; c < 32; c++) o[c] += o2[c];
-                if (qi < S) {
-                    float4* dst = reinterpret_cast<float4*>(p.o + (size_t)qi * rs + (size_t)h * D + half * 32);
+                    for (int c = 0; c < 8; c++) {
+                        float4 v = qi < S ? __ldg(src + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                        float x[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                    for (int c = 0; c < 8; c++)
-                        dst[c] = make_float4(o[4 * c] * inv, o[4 * c + 1] * inv, o[4 * c + 2] * inv, o[4 * c + 3] * inv);
+                        for (int t = 0; t < 4; t++) { hi[4 * c + t] = hi_part(x[t]); lo[4 * c + t] = x[t] - hi[4 * c + t]; }
+                    }
+                    tc::tmem_st32(lb + TM_QHI + half * 32, hi);
+                    tc::tmem_st32(lb + TM_QLO + half * 32, lo);
+                }
+                tc::tmem_st_wait();
+                tc::tc_fence_before();
+                tc::mbar_arrive(&bar->q_ready);
+                if (threadIdx.x == 0) TRACE(1);
+            }
+            float m = -INFINITY, l = 0.f;
+            for (int j = 0; j < it.T; j++, gt++) {
+                if (!tc::mbar_wait(&bar->s_full, gt & 1, abort, &g_attn_watchdog, 11)) { ok = false; break; }
+                if (threadIdx.x == 0 && gt < 8) TRACE(2 + 4 * gt);
+                tc::tc_fence_after();
+                float s[64];
+#pragma unroll
+                for (int half = 0; half < 2; half++) {
+                    float a[32], b[32];
+                    tc::tmem_ld32(lb + TM_S + half * 32, a);         // Q_hi K_hi + Q_lo K_hi
+                    tc::tmem_ld32(lb + TM_S + 64 + half * 32, b);    // Q_hi K_lo + Q_lo K_lo
+#pragma unroll
+                    for (int c = 0; c < 32; c++) s[half * 32 + c] = (a[c] + b[c]) * scale_log2;
+                }
+                tc::tc_fence_before();
+                tc::mbar_arrive(&bar->s_free);               // the MMA warp may overwrite S now
+                const int k0 = j * BKV;
+                if (k0 + BKV > S || (causal && k0 + BKV - 1 > it.q0)) {   // tile touches the diagonal or the end
+#pragma unroll
+                    for (int c = 0; c < 64; c++)
+                        if (k0 + c >= S || (causal && k0 + c > qi)) s[c] = -INFINITY;
+                }
+                float mx4[4] = {s[0], s[1], s[2], s[3]};      // 4 independent chains
+#pragma unroll
+                for (int c = 4; c < 64; c++) mx4[c & 3] = fmaxf(mx4[c & 3], s[c]);
+                const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
+                const bool raise = mx > m + RESCALE_THRESHOLD;
+                if (__any_sync(0xffffffffu, raise)) {
+                    const float mn = raise ? mx : m;
+                    const float f = ex2(m - mn);             // 0 on the first tile, 1 for rows that keep m
+                    if (j > 0) {   // O holds this item's P_0..P_{j-1} V: wait for it, rescale moved rows
+                        if (!tc::mbar_wait(&bar->pv_done, (gt - 1) & 1, abort, &g_attn_watchdog, 12)) { ok = false; break; }
+                        tc::tc_fence_after();
+#pragma unroll 1
+                        for (int q4 = 0; q4 < 4; q4++) {
+                            float o[32];
+                            tc::tmem_ld32(lb + TM_O + q4 * 32, o);
+#pragma unroll
+                            for (int c = 0; c < 32; c++) o[c] *= f;
+                            tc::tmem_st32(lb + TM_O + q4 * 32, o);
+                        }
+                        tc::tmem_st_wait();
+                    }
+                    l *= f;
+                    m = mn;
+                }
+                if (threadIdx.x == 0 && gt < 8) TRACE(3 + 4 * gt);
+                float rs4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int c = 0; c < 64; c++) { s[c] = ex2(s[c] - m); rs4[c & 3] += s[c]; }
+                l += (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
+                // the P columns were last read by PV of tile gt-1 (exponentials above overlap it)
+                if (j >= 1 && !tc::mbar_wait(&bar->pv_done, (gt - 1) & 1, abort, &g_attn_watchdog, 14)) { ok = false; break; }
+#pragma unroll
+                for (int half = 0; half < 2; half++) {
+                    float hi[32], lo[32];
+#pragma unroll
+                    for (int c = 0; c < 32; c++) { hi[c] = hi_part(s[half * 32 + c]); lo[c] = s[half * 32 + c] - hi[c]; }
+                    tc::tmem_st32(lb + TM_P + half * 32, hi);
+                    tc::tmem_st32(lb + TM_P + 64 + half * 32, lo);
+                }
+                if (threadIdx.x == 0 && gt < 8) TRACE(4 + 4 * gt);
+                tc::tmem_st_wait();
+                tc::tc_fence_before();
+                tc::mbar_arrive(&bar->p_ready);
+                if (threadIdx.x == 0 && gt < 8) TRACE(5 + 4 * gt);
+            }
+            if (!ok) break;
+            if (it.T > 0) {
+                if (!tc::mbar_wait(&bar->pv_done, (gt - 1) & 1, abort, &g_attn_watchdog, 13)) { ok = false; break; }
+                tc::tc_fence_after();
+                const float inv = 1.f / l;
+#pragma unroll 1
+                for (int half = 0; half < 2; half++) {
+                    float o[32], o2[32];
+                    tc::tmem_ld32(lb + TM_O + half * 32, o);         // P_hi V_hi + P_lo V_hi
+                    tc::tmem_ld32(lb + TM_O + 64 + half * 32, o2);   // P_hi V_lo + P_lo V_lo
+                    if (qi < S) {
+                        float4* dst = reinterpret_cast<float4*>(it.p.o + (size_t)qi * rs + (size_t)it.h * D + half * 32);
+#pragma unroll
+                        for (int c = 0; c < 8; c++)
+                            dst[c] = make_float4((o[4 * c] + o2[4 * c]) * inv, (o[4 * c + 1] + o2[4 * c + 1]) * inv,
+                                                 (o[4 * c + 2] + o2[4 * c + 2]) * inv, (o[4 * c + 3] + o2[4 * c + 3]) * inv);
+                    }
                 }
             }
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bar->o_free);                   // O (and Q) columns reusable
         }
     } else if (warp == 4) {
         // ======================= MMA issuer =======================
         if (lane == 0) {
             constexpr uint32_t id_s = tc::idesc_tf32(BQ, 2 * BKV, false, false);
             constexpr uint32_t id_o = tc::idesc_tf32(BQ, 2 * D, false, true);
-            bool ok = tc::mbar_wait(&bar->q_ready, 0, abort, &g_attn_watchdog, 21);
-            auto issue_s = [&](int j) -> bool {
-                const int st = j % NS;
-                if (!tc::mbar_wait(&bar->k_full[st], (j / NS) & 1, abort, &g_attn_watchdog, 22)) return false;
-                if (j >= 1 && !tc::mbar_wait(&bar->s_free, (j - 1) & 1, abort, &g_attn_watchdog, 23)) return false;
+            bool ok = true;
+            int gt = 0, ii = 0;
+            auto issue_s = [&](int g) -> bool {
+                const int st = g % NS;
+                if (!tc::mbar_wait(&bar->k_full[st], (g / NS) & 1, abort, &g_attn_watchdog, 22)) return false;
+                if (g >= 1 && !tc::mbar_wait(&bar->s_free, (g - 1) & 1, abort, &g_attn_watchdog, 23)) return false;
                 tc::tc_fence_after();
                 const uint32_t kb0 = tc::smem_u32(kst + st * STAGE);
 #pragma unroll
@@ -256,79 +276,89 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                 }
                 tc::mma_commit(&bar->s_full);
                 tc::mma_commit(&bar->k_empty[st]);
-                if (j < 8) TRACE(34 + j);
+                if (g < 8) TRACE(34 + g);
                 return true;
             };
-            if (ok && T > 0) ok = issue_s(0);
-            for (int j = 0; j < T && ok; j++) {
-                if (j + 1 < T && !(ok = issue_s(j + 1))) break;
-                const int st = j % NS;
-                if (!tc::mbar_wait(&bar->p_ready, j & 1, abort, &g_attn_watchdog, 24) ||
-                    !tc::mbar_wait(&bar->v_full[st], (j / NS) & 1, abort, &g_attn_watchdog, 25)) { ok = false; break; }
-                tc::tc_fence_after();
-                const uint32_t vb0 = tc::smem_u32(vst + st * STAGE);
-                const uint32_t pb = tm + TM_P;
+            for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ii++) {
+                const Item it = get_item(i, table, base, bstride, B, H, nqt, S, causal);
+                if (!tc::mbar_wait(&bar->q_ready, ii & 1, abort, &g_attn_watchdog, 21)) { ok = false; break; }
+                if (it.T > 0 && !(ok = issue_s(gt))) break;
+                for (int j = 0; j < it.T; j++, gt++) {
+                    if (j + 1 < it.T && !(ok = issue_s(gt + 1))) break;
+                    const int st = gt % NS;
+                    if (!tc::mbar_wait(&bar->p_ready, gt & 1, abort, &g_attn_watchdog, 24) ||
+                        !tc::mbar_wait(&bar->v_full[st], (gt / NS) & 1, abort, &g_attn_watchdog, 25)) { ok = false; break; }
+                    // the first PV of an item overwrites O: the previous item's O must have been read
+                    if (j == 0 && ii >= 1 && !tc::mbar_wait(&bar->o_free, (ii - 1) & 1, abort, &g_attn_watchdog, 26)) { ok = false; break; }
+                    tc::tc_fence_after();
+                    const uint32_t vb0 = tc::smem_u32(vst + st * STAGE);
 #pragma unroll
-                for (int kb = 0; kb < BKV / 8; kb++) {
-                    const uint64_t bv = tc::smem_desc(vb0 + kb * 1024, BKV * 128, 512, tc::SWZ_128B_BASE32B);   // [V_hi | V_lo]
-                    const uint32_t acc0 = (j | kb) ? 1u : 0u;
-                    tc::mma_tf32_ts(tm + TM_O, pb + 64 + kb * 8, bv, id_o, acc0);
-                    tc::mma_tf32_ts(tm + TM_O, pb + kb * 8, bv, id_o, 1u);
+                    for (int kb = 0; kb < BKV / 8; kb++) {
+                        const uint64_t bv = tc::smem_desc(vb0 + kb * 1024, BKV * 128, 512, tc::SWZ_128B_BASE32B);   // [V_hi | V_lo]
+                        const uint32_t acc0 = (j | kb) ? 1u : 0u;
+                        tc::mma_tf32_ts(tm + TM_O, tm + TM_P + 64 + kb * 8, bv, id_o, acc0);
+                        tc::mma_tf32_ts(tm + TM_O, tm + TM_P + kb * 8, bv, id_o, 1u);
+                    }
+                    tc::mma_commit(&bar->pv_done);
+                    tc::mma_commit(&bar->v_empty[st]);
+                    if (gt < 8) TRACE(42 + gt);
                 }
-                tc::mma_commit(&bar->pv_done);
-                if (j < 8) TRACE(42 + j);
-                tc::mma_commit(&bar->v_empty[st]);
             }
         }
     } else {
         // ======================= loaders (warps 5-8) =======================
         const int t = threadIdx.x - 160;                 // 0..127
         const int jr = t >> 1, d0 = (t & 1) * 32;        // key row within tile, d half
-        float4 kv[8], vv[8];
-        auto fetch = [&](int j) {
-            const int key = j * BKV + jr;
-            const float4* ks = reinterpret_cast<const float4*>(p.k + (size_t)key * rs + (size_t)h * D + d0);
-            const float4* vs = reinterpret_cast<const float4*>(p.v + (size_t)key * rs + (size_t)h * D + d0);
+        int gt = 0;
+        bool ok = true;
+        for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
+            const Item it = get_item(i, table, base, bstride, B, H, nqt, S, causal);
+            float4 kv[8], vv[8];
+            auto fetch = [&](int j) {
+                const int key = j * BKV + jr;
+                const float4* ks = reinterpret_cast<const float4*>(it.p.k + (size_t)key * rs + (size_t)it.h * D + d0);
+                const float4* vs = reinterpret_cast<const float4*>(it.p.v + (size_t)key * rs + (size_t)it.h * D + d0);
 #pragma unroll
-            for (int c = 0; c < 8; c++) {
-                kv[c] = key < S ? __ldg(ks + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-                vv[c] = key < S ? __ldg(vs + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int c = 0; c < 8; c++) {
+                    kv[c] = key < S ? __ldg(ks + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    vv[c] = key < S ? __ldg(vs + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            };
+            if (it.T > 0) fetch(0);
+            for (int j = 0; j < it.T; j++, gt++) {
+                const int st = gt % NS;
+                float4 kn[8], vn[8];
+#pragma unroll
+                for (int c = 0; c < 8; c++) { kn[c] = kv[c]; vn[c] = vv[c]; }
+                if (j + 1 < it.T) fetch(j + 1);              // next tile in flight while this one is stored
+                if (gt >= NS && !tc::mbar_wait(&bar->k_empty[st], ((gt / NS) - 1) & 1, abort, &g_attn_watchdog, 31)) { ok = false; break; }
+                uint8_t* kh = kst + st * STAGE;
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    float x[4] = {kn[c].x, kn[c].y, kn[c].z, kn[c].w}, hi[4], lo[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) { hi[u] = hi_part(x[u]); lo[u] = x[u] - hi[u]; }
+                    *reinterpret_cast<float4*>(kh + k_off(jr, d0 + 4 * c)) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+                    *reinterpret_cast<float4*>(kh + k_off(jr + BKV, d0 + 4 * c)) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+                }
+                tc::fence_proxy_async();
+                tc::mbar_arrive(&bar->k_full[st]);
+                if (t == 0 && gt < 7) TRACE(50 + gt);
+                if (gt >= NS && !tc::mbar_wait(&bar->v_empty[st], ((gt / NS) - 1) & 1, abort, &g_attn_watchdog, 32)) { ok = false; break; }
+                uint8_t* vh = vst + st * STAGE;
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    float x[4] = {vn[c].x, vn[c].y, vn[c].z, vn[c].w}, hi[4], lo[4];
+#pragma unroll
+                    for (int u = 0; u < 4; u++) { hi[u] = hi_part(x[u]); lo[u] = x[u] - hi[u]; }
+                    const uint32_t o = v_off(jr, d0 + 4 * c);
+                    *reinterpret_cast<float4*>(vh + o) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+                    *reinterpret_cast<float4*>(vh + KV_HALF + o) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+                }
+                tc::fence_proxy_async();
+                tc::mbar_arrive(&bar->v_full[st]);
+                if (t == 0 && gt < 6) TRACE(57 + gt);
             }
-        };
-        if (T > 0) fetch(0);
-        for (int j = 0; j < T; j++) {
-            const int st = j % NS;
-            float4 kn[8], vn[8];
-#pragma unroll
-            for (int c = 0; c < 8; c++) { kn[c] = kv[c]; vn[c] = vv[c]; }
-            if (j + 1 < T) fetch(j + 1);                 // next tile in flight while this one is stored
-            if (j >= NS && !tc::mbar_wait(&bar->k_empty[st], ((j / NS) - 1) & 1, abort, &g_attn_watchdog, 31)) break;
-            uint8_t* kh = kst + st * STAGE;
-#pragma unroll
-            for (int c = 0; c < 8; c++) {
-                float x[4] = {kn[c].x, kn[c].y, kn[c].z, kn[c].w}, hi[4], lo[4];
-#pragma unroll
-                for (int u = 0; u < 4; u++) { hi[u] = hi_part(x[u]); lo[u] = x[u] - hi[u]; }
-                *reinterpret_cast<float4*>(kh + k_off(jr, d0 + 4 * c)) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<float4*>(kh + k_off(jr + BKV, d0 + 4 * c)) = make_float4(lo[0], lo[1], lo[2], lo[3]);
-            }
-            tc::fence_proxy_async();
-            tc::mbar_arrive(&bar->k_full[st]);
-            if (t == 0 && j < 7) TRACE(50 + j);
-            if (j >= NS && !tc::mbar_wait(&bar->v_empty[st], ((j / NS) - 1) & 1, abort, &g_attn_watchdog, 32)) break;
-            uint8_t* vh = vst + st * STAGE;
-#pragma unroll
-            for (int c = 0; c < 8; c++) {
-                float x[4] = {vn[c].x, vn[c].y, vn[c].z, vn[c].w}, hi[4], lo[4];
-#pragma unroll
-                for (int u = 0; u < 4; u++) { hi[u] = hi_part(x[u]); lo[u] = x[u] - hi[u]; }
-                const uint32_t o = v_off(jr, d0 + 4 * c);
-                *reinterpret_cast<float4*>(vh + o) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-                *reinterpret_cast<float4*>(vh + KV_HALF + o) = make_float4(lo[0], lo[1], lo[2], lo[3]);
-            }
-            tc::fence_proxy_async();
-            tc::mbar_arrive(&bar->v_full[st]);
-            if (t == 0 && j < 6) TRACE(57 + j);
         }
     }
 
@@ -362,9 +392,18 @@ extern "C" lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const flo
     }
     LcuAttnGroup base{q, k, v, o};
     float scale_log2 = (float)(1.4426950408889634 / 8.0);   // log2(e) / sqrt(64)
-    dim3 grid((unsigned)((S + BQ - 1) / BQ), (unsigned)H, (unsigned)B);
-    k_attn_tc<<<grid, THREADS, SMEM_BYTES, lcu_as_stream(stream)>>>(d_table, base, S * H * D, (int)S, (int)H, causal,
-                                                                     scale_log2);
+    // persistent grid: one CTA per SM (TMEM and shared memory allow no more), each walks
+    // the heaviest-first item list with stride gridDim.x
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = LCU_SMS;
+    }
+    const size_t items = ((S + BQ - 1) / BQ) * H * B;
+    const unsigned grid = (unsigned)(items < (size_t)sms ? items : (size_t)sms);
+    k_attn_tc<<<grid, THREADS, SMEM_BYTES, lcu_as_stream(stream)>>>(d_table, base, S * H * D, (int)B, (int)S, (int)H,
+                                                                     causal, scale_log2);
     lcu_note_launch();
     return lcu_launch_status();
 }
