@@ -398,8 +398,10 @@ def main():
     roof = None
     if args.config == "attention":
         achieved = built.bytes / (sec_per_graph) / 1e9
+        # traffic: dram__bytes_read.sum + dram__bytes_write.sum of one k_attn_tc launch
+        # (profiles/attention_tcgen05_b8_s512_h8_d64.md)
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": 25256448,
                 "kernel": "attention (one grouped launch over the 8 ATTENTION nodes)",
                 "peak_src": pk["src"] + " hbm_gbs (burst copy)"}
     else:
