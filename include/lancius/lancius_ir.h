@@ -113,6 +113,11 @@ lancius_node* lancius_maxpool2d_bwd(lancius_graph* g, const lancius_node* grad, 
 
 void lancius_optimize_fusion(lancius_graph* g);
 
+/* .lancius v1 files (reference lancius_serialize.c:13-259); the loader also reads the
+ * older record layout without the is_view byte (stable/v9S files). */
+void lancius_graph_save(lancius_graph* g, const char* path);
+lancius_graph* lancius_graph_load(const char* path);
+
 lancius_node* lancius_attention(lancius_graph* g, const lancius_node* q, const lancius_node* k, const lancius_node* v);
 lancius_node* lancius_attention_noncausal(lancius_graph* g, const lancius_node* q, const lancius_node* k, const lancius_node* v);
 lancius_node* lancius_layernorm(lancius_graph* g, const lancius_node* in, const lancius_node* gamma, const lancius_node* beta);

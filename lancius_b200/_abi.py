@@ -81,6 +81,8 @@ IR_FUNCS = {
     "lancius_gelu": (NODE_P, [GRAPH_P, NODE_P]),
     "lancius_rmsnorm": (NODE_P, [GRAPH_P, NODE_P, NODE_P]),
     "lancius_optimize_fusion": (None, [GRAPH_P]),
+    "lancius_graph_load": (GRAPH_P, [C.c_char_p]),
+    "lancius_graph_save": (None, [GRAPH_P, C.c_char_p]),
     "lancius_node_bind_external": (None, [NODE_P, P]),
     "lancius_ir_schedule": (SCHED_P, [GRAPH_P]),
     "lancius_schedule_destroy": (None, [SCHED_P]),

@@ -86,6 +86,20 @@ class Schedule:
 
 
 class Graph:
+    @classmethod
+    def load(cls, path, lib=None):
+        """lancius_graph_load: weights stay in the loaded INPUT nodes (owned heap FP64)."""
+        g = cls.__new__(cls)
+        g.lib = lib if lib is not None else load()
+        g.ptr = g.lib.lancius_graph_load(path.encode())
+        if not g.ptr:
+            raise LanciusError(g.lib.lancius_get_error(), f"lancius_graph_load({path})")
+        g._keep = {}
+        return g
+
+    def save(self, path):
+        self.lib.lancius_graph_save(self.ptr, path.encode())
+
     def __init__(self, lib=None):
         self.lib = lib if lib is not None else load()
         self.ptr = self.lib.lancius_graph_create()

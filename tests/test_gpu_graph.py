@@ -112,3 +112,26 @@ def test_fused_launch_count(device):
     b = configs.mlp(L.Graph())
     run_gpu(device, b)
     assert device.last_launch_count == 3
+
+
+def test_lenet_model_file_on_gpu(device, orc):
+    """stable/v9S/pytorch_lenet.lancius loaded by lancius_graph_load and run on the GPU:
+    conv5x5(pad 2)+ReLU+maxpool x2, flatten, matmul+add+ReLU, matmul+add; vs ONNX Runtime's
+    golden output (normwise 1e-4, FP32-exact) and vs the FP64 oracle."""
+    import os
+    gold = os.path.join(os.path.dirname(__file__), "golden")
+    g = L.Graph.load(os.path.join(gold, "pytorch_lenet.lancius"))
+    nodes = g.nodes()
+    x = next(n for n in nodes if n.op == "INPUT" and len(n.shape) == 4 and n.shape[1] == 3 and not n.c.runtime_data)
+    out = [n for n in nodes if len(n.shape) == 2 and n.shape[1] == 10 and n.op != "INPUT"][-1]
+    inp = np.fromfile(os.path.join(gold, "parity_input.bin"), dtype=np.float32).astype(np.float64)
+    g.bind(x, inp)
+    s = g.schedule()
+    device.set_graph_replay(False)
+    device.bind(s)
+    device.upload_bound_inputs()           # weights came with the file; the image was bound above
+    device.execute(s)
+    y = device.download(out).ravel()
+    ort = np.fromfile(os.path.join(gold, "baseline_out.bin"), dtype=np.float32)
+    assert_close(y, ort, 1e-4)
+    assert_close(y, orc.run_graph(g, [out])[out.id].ravel(), 1e-4)
