@@ -54,7 +54,8 @@ lancius_error lcu_bind_plan(lcu_ctx* ctx, lancius_schedule* sched, lancius_graph
                             const lancius_memory_plan* plan);
 
 /* Host <-> device copies of one node's slot. host_dtype is LANCIUS_DTYPE_FP64
- * (reference-style double buffers, converted on the device) or FP32. */
+ * (reference-style double buffers, converted on the device), FP32, or INT8 for
+ * quantized weights (bytes, uploaded as they are). */
 lancius_error lcu_upload(lcu_ctx* ctx, const lancius_node* n, const void* host, lancius_dtype host_dtype);
 lancius_error lcu_download(lcu_ctx* ctx, const lancius_node* n, void* host, lancius_dtype host_dtype);
 /* Uploads every INPUT node whose runtime_data (FP64) is bound on the host. */
@@ -141,6 +142,31 @@ lancius_error lcu_gemm_colsplit(lcu_comm* comm, float* c, const float* a, const 
 lancius_error lcu_matmul_noalloc(float* out, const float* a, const float* b, size_t M, size_t K, size_t N,
                                  const float* bias, int epilogue, int mode, void* stream);
 size_t lcu_noalloc_scratch_capacity(void);
+
+/* ---- training, LLM and INT8 operators (SURVEY-ranked "next" rows) --------- */
+lancius_error lcu_sum(float* out, const float* a, size_t n, void* stream);                       /* scheduler.c:251-256 */
+lancius_error lcu_sum_axis0(float* out, const float* a, size_t rows, size_t cols, void* stream); /* :257-262 */
+lancius_error lcu_transpose(float* out, const float* a, size_t rows, size_t cols, void* stream); /* :246-250 */
+lancius_error lcu_relu_bwd(float* out, const float* grad, const float* fwd, size_t n, void* stream); /* :279-283 */
+lancius_error lcu_softmax_bwd(float* out, const float* dy, const float* y, size_t rows, size_t cols, void* stream); /* :295-304 */
+lancius_error lcu_cross_entropy(float* out, const float* logits, const float* targets, size_t rows, size_t cols,
+                                void* stream);                                                   /* :68-86 */
+lancius_error lcu_cross_entropy_bwd(float* out, const float* logits, const float* targets, const float* grad_out,
+                                    size_t rows, size_t cols, void* stream);                     /* :90-106 */
+lancius_error lcu_rmsnorm(float* out, const float* in, const float* gamma, size_t rows, size_t hidden, float eps,
+                          void* stream);                                                         /* lancius_kernels.c:381-396 */
+lancius_error lcu_swiglu(float* out, const float* gate, const float* up, size_t n, void* stream); /* :398-405 */
+lancius_error lcu_rope(float* q, float* k, size_t B, size_t S, size_t H, size_t D, int pos_offset, void* stream); /* :248-272 */
+lancius_error lcu_gqa(float* out, const float* q, const float* k, const float* v, size_t S, size_t Hq, size_t Hkv,
+                      size_t D, void* stream);                                                   /* :407-448 */
+lancius_error lcu_maxpool2d_bwd(float* out, const float* grad, const float* in, size_t N, size_t C, size_t H, size_t W,
+                                size_t K, size_t stride, void* stream);                          /* vision_ops.c:149-190 */
+lancius_error lcu_conv2d_bwd(float* out, const float* grad, const float* w, size_t N, size_t C_in, size_t H, size_t W,
+                             size_t C_out, size_t H_out, size_t W_out, size_t K_h, size_t K_w, size_t stride, size_t pad,
+                             void* stream);                                                      /* lancius_kernels.c:62-91 */
+lancius_error lcu_conv2d_bwd_w(float* out, const float* grad, const float* in, size_t N, size_t C_in, size_t H, size_t W,
+                               size_t C_out, size_t H_out, size_t W_out, size_t K_h, size_t K_w, size_t stride,
+                               size_t pad, void* stream);                                        /* :93-136 */
 
 /* Library self-description for tests: the names of this build's kernels. */
 const char* lcu_build_info(void);

@@ -80,6 +80,16 @@ IR_FUNCS = {
     "lancius_layernorm": (NODE_P, [GRAPH_P, NODE_P, NODE_P, NODE_P]),
     "lancius_gelu": (NODE_P, [GRAPH_P, NODE_P]),
     "lancius_rmsnorm": (NODE_P, [GRAPH_P, NODE_P, NODE_P]),
+    "lancius_swiglu": (NODE_P, [GRAPH_P, NODE_P, NODE_P]),
+    "lancius_gqa": (NODE_P, [GRAPH_P, NODE_P, NODE_P, NODE_P, C.c_uint32, C.c_uint32]),
+    "lancius_relu_bwd": (NODE_P, [GRAPH_P, NODE_P, NODE_P]),
+    "lancius_softmax_bwd": (NODE_P, [GRAPH_P, NODE_P, NODE_P]),
+    "lancius_cross_entropy": (NODE_P, [GRAPH_P, NODE_P, NODE_P]),
+    "lancius_cross_entropy_bwd": (NODE_P, [GRAPH_P, NODE_P, NODE_P, NODE_P]),
+    "lancius_conv2d_bwd": (NODE_P, [GRAPH_P, NODE_P, NODE_P, NODE_P, C.c_uint32, C.c_uint32]),
+    "lancius_conv2d_bwd_w": (NODE_P, [GRAPH_P, NODE_P, NODE_P, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32]),
+    "lancius_maxpool2d_bwd": (NODE_P, [GRAPH_P, NODE_P, NODE_P, C.c_uint32, C.c_uint32]),
+    "lancius_node_bind_external_int8": (None, [NODE_P, P]),
     "lancius_optimize_fusion": (None, [GRAPH_P]),
     "lancius_graph_load": (GRAPH_P, [C.c_char_p]),
     "lancius_graph_save": (None, [GRAPH_P, C.c_char_p]),
@@ -132,6 +142,17 @@ B200_FUNCS = {
     "lcu_sum_axis1": (C.c_int, [P, P, c_size, c_size, P]),
     "lcu_maxpool2d": (C.c_int, [P, P, c_size, c_size, c_size, c_size, c_size, c_size, P]),
     "lcu_build_info": (C.c_char_p, []),
+    "lcu_sum": (C.c_int, [P, P, c_size, P]),
+    "lcu_sum_axis0": (C.c_int, [P, P, c_size, c_size, P]),
+    "lcu_transpose": (C.c_int, [P, P, c_size, c_size, P]),
+    "lcu_relu_bwd": (C.c_int, [P, P, P, c_size, P]),
+    "lcu_softmax_bwd": (C.c_int, [P, P, P, c_size, c_size, P]),
+    "lcu_cross_entropy": (C.c_int, [P, P, P, c_size, c_size, P]),
+    "lcu_cross_entropy_bwd": (C.c_int, [P, P, P, P, c_size, c_size, P]),
+    "lcu_rmsnorm": (C.c_int, [P, P, P, c_size, c_size, C.c_float, P]),
+    "lcu_swiglu": (C.c_int, [P, P, P, c_size, P]),
+    "lcu_rope": (C.c_int, [P, P, c_size, c_size, c_size, c_size, C.c_int, P]),
+    "lcu_gqa": (C.c_int, [P, P, P, P, c_size, c_size, c_size, c_size, P]),
     "lcu_comm_unique_id": (C.c_int, [P, c_size]),
     "lcu_comm_create": (P, [C.c_int, C.c_int, P, C.c_int]),
     "lcu_comm_destroy": (None, [P]),

@@ -12,7 +12,8 @@ constexpr int BQ = 64, BKV = 64, THREADS = 256;
 
 template <int D>
 __global__ void __launch_bounds__(THREADS) k_attn_simt(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base,
-                                                       size_t batch_stride, int S, int H, int causal, float scale_log2) {
+                                                       size_t batch_stride, int S, int H, int causal, float scale_log2,
+                                                       int Hkv) {
     extern __shared__ float4 smem4[];
     float* smem = reinterpret_cast<float*>(smem4);
     float* Qs = smem;                 // [D][BQ]
@@ -27,8 +28,9 @@ __global__ void __launch_bounds__(THREADS) k_attn_simt(const LcuAttnGroup* __res
         p.q = base.q + off; p.k = base.k + off; p.v = base.v + off; p.o = base.o + off;
     }
     const int h = blockIdx.y, q0 = blockIdx.x * BQ;
+    const int hk = h / (H / Hkv);                      // grouped-query: kv head of this query head
     const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
-    const size_t row_stride = (size_t)H * D;
+    const size_t row_stride = (size_t)H * D, kv_stride = (size_t)Hkv * D;
     constexpr int DC = D / 16;        // output columns per thread
 
     // stage Q (transposed into [d][r])
@@ -54,7 +56,7 @@ __global__ void __launch_bounds__(THREADS) k_attn_simt(const LcuAttnGroup* __res
             int j = idx / (D / 4), d4 = (idx % (D / 4)) * 4;
             float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
             if (k0 + j < S) {
-                size_t g = (size_t)(k0 + j) * row_stride + (size_t)h * D + d4;
+                size_t g = (size_t)(k0 + j) * kv_stride + (size_t)hk * D + d4;
                 kv = __ldg(reinterpret_cast<const float4*>(p.k + g));
                 vv = __ldg(reinterpret_cast<const float4*>(p.v + g));
             }
@@ -139,16 +141,18 @@ __global__ void __launch_bounds__(THREADS) k_attn_simt(const LcuAttnGroup* __res
 
 template <int D>
 lancius_error launch(const LcuAttnGroup* table, LcuAttnGroup base, size_t bstride, int B, int S, int H, int causal,
-                     cudaStream_t st) {
+                     cudaStream_t st, int Hkv) {
     size_t smem = sizeof(float) * (size_t)(2 * D * BQ + BKV * D + BKV * BQ);
-    static bool configured = false;
-    if (!configured) {
+    static bool configured[64] = {};   // the attribute is per device
+    int dev_ = 0;
+    cudaGetDevice(&dev_);
+    if (dev_ >= 0 && dev_ < 64 && !configured[dev_]) {
         cudaFuncSetAttribute(k_attn_simt<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        configured = true;
+        configured[dev_] = true;
     }
     float scale_log2 = (float)(1.4426950408889634 / sqrt((double)D));
     dim3 grid((unsigned)((S + BQ - 1) / BQ), (unsigned)H, (unsigned)B);
-    k_attn_simt<D><<<grid, THREADS, smem, st>>>(table, base, bstride, S, H, causal, scale_log2);
+    k_attn_simt<D><<<grid, THREADS, smem, st>>>(table, base, bstride, S, H, causal, scale_log2, Hkv);
     lcu_note_launch();
     return lcu_launch_status();
 }
@@ -166,8 +170,28 @@ extern "C" lancius_error lcu_attention_simt(const LcuAttnGroup* d_table, const f
     size_t bstride = S * H * D;
     cudaStream_t st = lcu_as_stream(stream);
     switch (D) {
-        case 64: return launch<64>(d_table, base, bstride, (int)B, (int)S, (int)H, causal, st);
-        case 128: return launch<128>(d_table, base, bstride, (int)B, (int)S, (int)H, causal, st);
+        case 64: return launch<64>(d_table, base, bstride, (int)B, (int)S, (int)H, causal, st, (int)H);
+        case 128: return launch<128>(d_table, base, bstride, (int)B, (int)S, (int)H, causal, st, (int)H);
+        default: lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP;
+    }
+}
+
+// Grouped-query attention (kernel_gqa, lancius_kernels.c:407-448): causal, query head h
+// reads kv head h / (Hq / Hkv); q/out [S, Hq, D], k/v [S, Hkv, D].
+extern "C" lancius_error lcu_gqa(float* o, const float* q, const float* k, const float* v, size_t S, size_t Hq,
+                                 size_t Hkv, size_t D, void* stream) {
+    if (!o || !q || !k || !v) { lancius_set_error(LANCIUS_ERROR_NULL_PTR); return LANCIUS_ERROR_NULL_PTR; }
+    if (Hkv == 0 || Hq % Hkv) { lancius_set_error(LANCIUS_ERROR_SHAPE_MISMATCH); return LANCIUS_ERROR_SHAPE_MISMATCH; }
+    if ((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)o) & 15u)) {
+        lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+        return LANCIUS_ERROR_UNSUPPORTED_DTYPE;
+    }
+    if (S == 0) return LANCIUS_ERROR_OK;
+    LcuAttnGroup base{q, k, v, o};
+    cudaStream_t st = lcu_as_stream(stream);
+    switch (D) {
+        case 64: return launch<64>(nullptr, base, 0, 1, (int)S, (int)Hq, 1, st, (int)Hkv);
+        case 128: return launch<128>(nullptr, base, 0, 1, (int)S, (int)Hq, 1, st, (int)Hkv);
         default: lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP;
     }
 }

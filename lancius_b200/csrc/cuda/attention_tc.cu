@@ -384,11 +384,13 @@ extern "C" int lcu_attention_tc_supported(size_t D_) { return D_ == (size_t)D; }
 extern "C" lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, const float* k, const float* v,
                                           float* o, size_t B, size_t S, size_t H, int causal, void* stream) {
     if (B == 0 || S == 0 || H == 0) return LANCIUS_ERROR_OK;
-    static bool configured = false;
-    if (!configured) {
+    static bool configured[64] = {};   // the attribute is per device
+    int dev_ = 0;
+    cudaGetDevice(&dev_);
+    if (dev_ >= 0 && dev_ < 64 && !configured[dev_]) {
         if (cudaFuncSetAttribute(k_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
             return lcu_launch_status();
-        configured = true;
+        configured[dev_] = true;
     }
     LcuAttnGroup base{q, k, v, o};
     float scale_log2 = (float)(1.4426950408889634 / 8.0);   // log2(e) / sqrt(64)

@@ -26,7 +26,7 @@ namespace {
 constexpr size_t NPOS = (size_t)-1;
 constexpr size_t SLOT_ALIGN = 256;
 
-enum StepKind { S_GEMM, S_ATTN, S_CONV, S_LN, S_SOFTMAX, S_SUMAX1, S_ELT, S_BCAST, S_MAXPOOL };
+enum StepKind { S_GEMM, S_ATTN, S_CONV, S_LN, S_SOFTMAX, S_SUMAX1, S_ELT, S_BCAST, S_MAXPOOL, S_MISC };
 
 struct Step {
     StepKind kind;
@@ -40,6 +40,9 @@ struct Step {
     size_t cn = 0, ci = 0, h = 0, w = 0, co = 0, kh = 0, kw = 0, stride = 0, pad = 0;
     size_t out = 0, in0 = 0, in1 = 0;   // node offsets for single-instance steps
     size_t rows = 0, cols = 0, n = 0, in_elems = 0;
+    size_t in2 = 0;            // third input (S_MISC)
+    int lop = 0;               // lancius opcode (S_MISC); LANCIUS_OP_MATMUL / CONV2D* mean the INT8-weight forms
+    double dscale = 1.0;       // INT8 weight scale
     float eps = 1e-5f;
 };
 
@@ -184,6 +187,7 @@ struct Builder {
         for (uint32_t i = 0; i < g->node_count; i++) {
             const lancius_node* m = g->nodes[i];
             if (m->op != LANCIUS_OP_MATMUL || m->ndim != 2) continue;
+            if (m->inputs[1]->dtype == LANCIUS_DTYPE_INT8 && m->inputs[1]->runtime_data_int8) continue;   // INT8 path
             size_t M = m->shape[0], N = m->shape[1];
             Chain ch;
             const lancius_node* tail = m;
@@ -263,7 +267,10 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
             for (uint32_t j = 0; j < n->input_count; j++) {
                 const lancius_node* in = n->inputs[j];
                 if (!in || off[in->id] == NPOS) return fail(LANCIUS_ERROR_NULL_PTR);
-                if (in->runtime_data_int8 || in->dtype == LANCIUS_DTYPE_INT8) return fail(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+                const bool int8_weight_ok = j == 1 && (n->op == LANCIUS_OP_MATMUL || n->op == LANCIUS_OP_CONV2D ||
+                                                       n->op == LANCIUS_OP_CONV2D_RELU_FUSED);
+                if ((in->runtime_data_int8 || in->dtype == LANCIUS_DTYPE_INT8) && !int8_weight_ok)
+                    return fail(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
             }
             size_t E = lancius_node_elements(n);
             switch (n->op) {
@@ -299,6 +306,10 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                     break;
                 case LANCIUS_OP_SOFTMAX: case LANCIUS_OP_SUM_AXIS1: case LANCIUS_OP_BROADCAST:
                 case LANCIUS_OP_CONV2D: case LANCIUS_OP_CONV2D_RELU_FUSED: case LANCIUS_OP_MAXPOOL2D:
+                case LANCIUS_OP_SUM: case LANCIUS_OP_SUM_AXIS0: case LANCIUS_OP_TRANSPOSE: case LANCIUS_OP_RELU_BWD:
+                case LANCIUS_OP_SOFTMAX_BWD: case LANCIUS_OP_CROSS_ENTROPY: case LANCIUS_OP_CROSS_ENTROPY_BWD:
+                case LANCIUS_OP_RMSNORM: case LANCIUS_OP_SWIGLU: case LANCIUS_OP_GQA: case LANCIUS_OP_MAXPOOL2D_BWD:
+                case LANCIUS_OP_CONV2D_BWD: case LANCIUS_OP_CONV2D_BWD_W:
                     snprintf(key, sizeof key, "U:%u", n->id);      // one launch per node
                     break;
                 default:
@@ -319,7 +330,8 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                     st.kind = S_GEMM;
                     st.M = n->shape[0]; st.N = n->shape[1]; st.K = n->inputs[0]->shape[n->inputs[0]->ndim - 1];
                     st.epi = b.chain[n->id].epi;
-                    st.tc = lcu_use_tensor_cores(st.M, st.N, st.K);
+                    st.tc = lcu_use_tensor_cores(st.M, st.N, st.K) &&
+                            !(n->inputs[1]->dtype == LANCIUS_DTYPE_INT8 && n->inputs[1]->runtime_data_int8);
                     st.gb = ns.size();
                     {
                         bool shared_b = true;
@@ -331,6 +343,15 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                         if (need > c->scratch_bytes) c->scratch_bytes = need;
                         st.plan_idx = (int)c->tc_plans.size();
                         c->tc_plans.push_back(LcuTcGemmPlan());
+                    }
+                    if (n->inputs[1]->dtype == LANCIUS_DTYPE_INT8 && n->inputs[1]->runtime_data_int8) {
+                        // INT8 weights: dynamic per-tensor quantisation of A (scheduler.c:195-220)
+                        st.kind = S_MISC; st.lop = LANCIUS_OP_MATMUL; st.count = 1;
+                        st.out = O(n); st.in0 = O(n->inputs[0]); st.in1 = O(n->inputs[1]); st.dscale = n->inputs[1]->scale;
+                        st.table_off = b.add_table(std::vector<float>(64, 0.f));     // one float of scratch (max |a|)
+                        st.tc = 0;
+                        if (ns.size() > 1) return fail(LANCIUS_ERROR_UNSUPPORTED_OP);
+                        break;
                     }
                     std::vector<LcuGemmGroup> t;
                     for (const lancius_node* x : ns) {
@@ -396,6 +417,12 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                     st.co = wt->shape[0]; st.kh = wt->shape[2]; st.kw = wt->shape[3]; st.stride = n->stride; st.pad = n->pad;
                     if (in->ndim != 4 || wt->ndim != 4 || wt->shape[1] != st.ci || st.stride == 0) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
                     st.out = O(n); st.in0 = O(in); st.in1 = O(wt);
+                    if (wt->dtype == LANCIUS_DTYPE_INT8 && wt->runtime_data_int8) {
+                        // INT8 weights: dynamic quantisation of the input (vision_ops.c:16-57)
+                        st.kind = S_MISC; st.lop = n->op; st.dscale = wt->scale;
+                        st.table_off = b.add_table(std::vector<float>(64, 0.f));
+                        break;
+                    }
                     size_t ho = (st.h + 2 * st.pad - st.kh) / st.stride + 1, wo = (st.w + 2 * st.pad - st.kw) / st.stride + 1;
                     st.M = st.co; st.N = st.cn * ho * wo; st.K = st.ci * st.kh * st.kw;
                     st.tc = st.cn && st.ci && lcu_use_tensor_cores(st.M, st.N, st.K);
@@ -408,6 +435,51 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                                                                  nullptr, nullptr}};
                         st.table_off = b.add_table(t);
                     }
+                } break;
+                case LANCIUS_OP_SUM: case LANCIUS_OP_SUM_AXIS0: case LANCIUS_OP_TRANSPOSE: case LANCIUS_OP_RELU_BWD:
+                case LANCIUS_OP_SOFTMAX_BWD: case LANCIUS_OP_CROSS_ENTROPY: case LANCIUS_OP_CROSS_ENTROPY_BWD:
+                case LANCIUS_OP_RMSNORM: case LANCIUS_OP_SWIGLU: case LANCIUS_OP_GQA: case LANCIUS_OP_MAXPOOL2D_BWD:
+                case LANCIUS_OP_CONV2D_BWD: case LANCIUS_OP_CONV2D_BWD_W: {
+                    const lancius_node* i0 = n->inputs[0];
+                    const lancius_node* i1 = n->input_count > 1 ? n->inputs[1] : nullptr;
+                    const lancius_node* i2 = n->input_count > 2 ? n->inputs[2] : nullptr;
+                    st.kind = S_MISC; st.lop = n->op; st.out = O(n); st.in0 = O(i0);
+                    st.in1 = i1 ? O(i1) : 0; st.in2 = i2 ? O(i2) : 0;
+                    st.n = lancius_node_elements(n);
+                    size_t E0 = lancius_node_elements(i0), E1 = i1 ? lancius_node_elements(i1) : 0;
+                    bool okshape = true;
+                    switch (n->op) {
+                        case LANCIUS_OP_SUM: st.n = E0; break;
+                        case LANCIUS_OP_SUM_AXIS0: case LANCIUS_OP_TRANSPOSE:
+                            okshape = i0->ndim == 2; st.rows = i0->shape[0]; st.cols = i0->shape[1]; break;
+                        case LANCIUS_OP_RELU_BWD: case LANCIUS_OP_SWIGLU: okshape = E0 >= st.n && E1 >= st.n; break;
+                        case LANCIUS_OP_SOFTMAX_BWD: case LANCIUS_OP_CROSS_ENTROPY_BWD:
+                            okshape = n->ndim == 2 && E0 >= st.n && E1 >= st.n; st.rows = n->shape[0]; st.cols = n->shape[1]; break;
+                        case LANCIUS_OP_CROSS_ENTROPY:
+                            okshape = i0->ndim == 2; st.rows = i0->shape[0]; st.cols = i0->shape[1]; break;
+                        case LANCIUS_OP_RMSNORM:
+                            okshape = n->ndim >= 2 && E1 >= n->shape[1]; st.rows = n->shape[0]; st.cols = n->shape[1]; break;
+                        case LANCIUS_OP_GQA:
+                            okshape = n->ndim == 3 && n->kernel_w && n->kernel_h % n->kernel_w == 0 &&
+                                      (n->shape[2] == 64 || n->shape[2] == 128) && n->shape[1] == n->kernel_h;
+                            st.S = n->shape[0]; st.H = n->kernel_h; st.co = n->kernel_w; st.D = n->shape[2]; break;
+                        case LANCIUS_OP_MAXPOOL2D_BWD:
+                            okshape = i1 && i1->ndim == 4; if (!okshape) break;
+                            st.cn = i1->shape[0]; st.ci = i1->shape[1]; st.h = i1->shape[2]; st.w = i1->shape[3];
+                            st.kh = n->kernel_h; st.stride = n->stride; break;
+                        case LANCIUS_OP_CONV2D_BWD:     // (grad, fwd_in, fwd_w)
+                            okshape = i1 && i2 && i1->ndim == 4 && i2->ndim == 4 && i0->ndim == 4; if (!okshape) break;
+                            st.cn = i1->shape[0]; st.ci = i1->shape[1]; st.h = i1->shape[2]; st.w = i1->shape[3];
+                            st.co = i2->shape[0]; st.kh = i2->shape[2]; st.kw = i2->shape[3]; st.M = i0->shape[2]; st.N = i0->shape[3];
+                            st.stride = n->stride; st.pad = n->pad; break;
+                        case LANCIUS_OP_CONV2D_BWD_W:   // (grad, fwd_in)
+                            okshape = i1 && i1->ndim == 4 && i0->ndim == 4; if (!okshape) break;
+                            st.cn = i1->shape[0]; st.ci = i1->shape[1]; st.h = i1->shape[2]; st.w = i1->shape[3];
+                            st.co = n->shape[0]; st.kh = n->shape[2]; st.kw = n->shape[3]; st.M = i0->shape[2]; st.N = i0->shape[3];
+                            st.stride = n->stride; st.pad = n->pad; break;
+                        default: break;
+                    }
+                    if (!okshape) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
                 } break;
                 case LANCIUS_OP_MAXPOOL2D: {
                     const lancius_node* in = n->inputs[0];
@@ -554,6 +626,8 @@ extern "C" lancius_error lcu_upload(lcu_ctx* c, const lancius_node* n, const voi
     cudaSetDevice(c->device);
     if (dt == LANCIUS_DTYPE_FP32)
         return cuda_fail(cudaMemcpyAsync(d, host, E * 4, cudaMemcpyHostToDevice, c->stream));
+    if (dt == LANCIUS_DTYPE_INT8)       // INT8 weights are stored as bytes in the node's slot
+        return cuda_fail(cudaMemcpyAsync(d, host, E, cudaMemcpyHostToDevice, c->stream));
     if (dt != LANCIUS_DTYPE_FP64) return fail(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
     if (E > c->staging_elems) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
     cudaError_t ce = cudaMemcpyAsync(c->staging, host, E * 8, cudaMemcpyHostToDevice, c->stream);
@@ -585,7 +659,10 @@ extern "C" lancius_error lcu_upload_bound_inputs(lcu_ctx* c) {
     if (!c || !c->g) return fail(LANCIUS_ERROR_NULL_PTR);
     for (uint32_t i = 0; i < c->g->node_count; i++) {
         const lancius_node* n = c->g->nodes[i];
-        if (n->op == LANCIUS_OP_INPUT && n->runtime_data) {
+        if (n->op == LANCIUS_OP_INPUT && n->dtype == LANCIUS_DTYPE_INT8 && n->runtime_data_int8) {
+            lancius_error e = lcu_upload(c, n, n->runtime_data_int8, LANCIUS_DTYPE_INT8);
+            if (e != LANCIUS_ERROR_OK) return e;
+        } else if (n->op == LANCIUS_OP_INPUT && n->runtime_data) {
             lancius_error e = lcu_upload(c, n, n->runtime_data, LANCIUS_DTYPE_FP64);
             if (e != LANCIUS_ERROR_OK) return e;
         }
@@ -602,6 +679,39 @@ extern "C" void lcu_host_free(void* p) { if (p) cudaFreeHost(p); }
 
 // ---------------------------------------------------------------------------
 // execution
+
+static lancius_error run_misc(const Step& s, char* base, void* st) {
+    auto F = [&](size_t off) { return reinterpret_cast<float*>(base + off); };
+    switch (s.lop) {
+        case LANCIUS_OP_MATMUL:
+            return lcu_matmul_int8(F(s.out), F(s.in0), reinterpret_cast<const int8_t*>(base + s.in1), s.dscale, s.M, s.K, s.N,
+                                   F(s.table_off), st);
+        case LANCIUS_OP_CONV2D: case LANCIUS_OP_CONV2D_RELU_FUSED:
+            return lcu_conv2d_int8(F(s.out), F(s.in0), reinterpret_cast<const int8_t*>(base + s.in1), s.dscale, s.cn, s.ci, s.h,
+                                   s.w, s.co, s.kh, s.kw, s.stride, s.pad, s.lop == LANCIUS_OP_CONV2D_RELU_FUSED,
+                                   F(s.table_off), st);
+        case LANCIUS_OP_SUM: return lcu_sum(F(s.out), F(s.in0), s.n, st);
+        case LANCIUS_OP_SUM_AXIS0: return lcu_sum_axis0(F(s.out), F(s.in0), s.rows, s.cols, st);
+        case LANCIUS_OP_TRANSPOSE: return lcu_transpose(F(s.out), F(s.in0), s.rows, s.cols, st);
+        case LANCIUS_OP_RELU_BWD: return lcu_relu_bwd(F(s.out), F(s.in0), F(s.in1), s.n, st);
+        case LANCIUS_OP_SOFTMAX_BWD: return lcu_softmax_bwd(F(s.out), F(s.in0), F(s.in1), s.rows, s.cols, st);
+        case LANCIUS_OP_CROSS_ENTROPY: return lcu_cross_entropy(F(s.out), F(s.in0), F(s.in1), s.rows, s.cols, st);
+        case LANCIUS_OP_CROSS_ENTROPY_BWD:
+            return lcu_cross_entropy_bwd(F(s.out), F(s.in0), F(s.in1), F(s.in2), s.rows, s.cols, st);
+        case LANCIUS_OP_RMSNORM: return lcu_rmsnorm(F(s.out), F(s.in0), F(s.in1), s.rows, s.cols, 1e-5f, st);
+        case LANCIUS_OP_SWIGLU: return lcu_swiglu(F(s.out), F(s.in0), F(s.in1), s.n, st);
+        case LANCIUS_OP_GQA: return lcu_gqa(F(s.out), F(s.in0), F(s.in1), F(s.in2), s.S, s.H, s.co, s.D, st);
+        case LANCIUS_OP_MAXPOOL2D_BWD:
+            return lcu_maxpool2d_bwd(F(s.out), F(s.in0), F(s.in1), s.cn, s.ci, s.h, s.w, s.kh, s.stride, st);
+        case LANCIUS_OP_CONV2D_BWD:
+            return lcu_conv2d_bwd(F(s.out), F(s.in0), F(s.in2), s.cn, s.ci, s.h, s.w, s.co, s.M, s.N, s.kh, s.kw, s.stride, s.pad, st);
+        case LANCIUS_OP_CONV2D_BWD_W:
+            return lcu_conv2d_bwd_w(F(s.out), F(s.in0), F(s.in1), s.cn, s.ci, s.h, s.w, s.co, s.M, s.N, s.kh, s.kw, s.stride, s.pad, st);
+        default:
+            lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP);
+            return LANCIUS_ERROR_UNSUPPORTED_OP;
+    }
+}
 
 static lancius_error run_steps(lcu_ctx* c) {
     char* base = c->dmem;
@@ -659,6 +769,7 @@ static lancius_error run_steps(lcu_ctx* c) {
                                s.relu, c->mode, st);
                 break;
             case S_MAXPOOL: e = lcu_maxpool2d(F(s.out), F(s.in0), s.cn, s.ci, s.h, s.w, s.kh, s.stride, st); break;
+            case S_MISC: e = run_misc(s, base, st); break;
         }
         if (e != LANCIUS_ERROR_OK) return e;
     }

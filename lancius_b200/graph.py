@@ -136,6 +136,15 @@ class Graph:
     def gelu(self, a): return self._mk("lancius_gelu", a)
     def rmsnorm(self, x, g): return self._mk("lancius_rmsnorm", x, g)
     def attention(self, q, k, v): return self._mk("lancius_attention", q, k, v)
+    def swiglu(self, gate, up): return self._mk("lancius_swiglu", gate, up)
+    def gqa(self, q, k, v, hq, hkv): return self._mk("lancius_gqa", q, k, v, hq, hkv)
+    def relu_bwd(self, grad, fwd): return self._mk("lancius_relu_bwd", grad, fwd)
+    def softmax_bwd(self, grad, y): return self._mk("lancius_softmax_bwd", grad, y)
+    def cross_entropy(self, logits, targets): return self._mk("lancius_cross_entropy", logits, targets)
+    def cross_entropy_bwd(self, logits, targets, g): return self._mk("lancius_cross_entropy_bwd", logits, targets, g)
+    def conv2d_bwd(self, grad, x, w, stride, pad): return self._mk("lancius_conv2d_bwd", grad, x, w, stride, pad)
+    def conv2d_bwd_w(self, grad, x, kh, kw, stride, pad): return self._mk("lancius_conv2d_bwd_w", grad, x, kh, kw, stride, pad)
+    def maxpool2d_bwd(self, grad, x, k, stride): return self._mk("lancius_maxpool2d_bwd", grad, x, k, stride)
     def attention_noncausal(self, q, k, v): return self._mk("lancius_attention_noncausal", q, k, v)
     def tanh(self, a): return self._mk("lancius_tanh", a)
 
@@ -153,6 +162,16 @@ class Graph:
             raise ValueError(f"bind {node}: {a.size} values for {node.size} elements")
         self._keep[node.id] = a
         self.lib.lancius_node_bind_external(node.ptr, a.ctypes.data_as(C.c_void_p))
+        return a
+
+    def bind_int8(self, node, array, scale):
+        """INT8 weights as the reference's quantizer leaves them (lancius_quantize.c:19-28):
+        dtype INT8, per-tensor scale, data in runtime_data_int8."""
+        a = np.ascontiguousarray(array, dtype=np.int8)
+        self._keep[(node.id, "i8")] = a
+        node.c.dtype = _abi.DTYPE_INT8
+        node.c.scale = float(scale)
+        self.lib.lancius_node_bind_external_int8(node.ptr, a.ctypes.data_as(C.c_void_p))
         return a
 
     def nodes(self):

@@ -176,6 +176,121 @@ void orc_rmsnorm(double* out, const double* in, const double* gamma, size_t rows
     }
 }
 
+
+/* lancius_kernels.c:398-405 */
+void orc_swiglu(double* out, const double* gate, const double* up, size_t n) {
+    for (size_t i = 0; i < n; i++) { double g = gate[i]; out[i] = g / (1.0 + exp(-g)) * up[i]; }
+}
+
+/* lancius_kernels.c:407-448: causal attention, query head hq reads kv head hq / (Hq / Hkv) */
+void orc_gqa(double* out, const double* q, const double* k, const double* v, size_t S, size_t Hq, size_t Hkv, size_t D) {
+    size_t grp = Hq / Hkv;
+    double scale = 1.0 / sqrt((double)D);
+    for (size_t i = 0; i < S; i++)
+        for (size_t hq = 0; hq < Hq; hq++) {
+            double acc[1024], m = -1e9, l = 0.0;
+            size_t hk = hq / grp;
+            for (size_t d = 0; d < D; d++) acc[d] = 0.0;
+            for (size_t j = 0; j < S; j++) {
+                double s = 0.0;
+                for (size_t d = 0; d < D; d++) s += q[(i * Hq + hq) * D + d] * k[(j * Hkv + hk) * D + d];
+                s *= scale;
+                if (j > i) s = -1e9;
+                double mn = s > m ? s : m, corr = exp(m - mn), p = exp(s - mn);
+                l = l * corr + p;
+                for (size_t d = 0; d < D; d++) acc[d] = acc[d] * corr + p * v[(j * Hkv + hk) * D + d];
+                m = mn;
+            }
+            for (size_t d = 0; d < D; d++) out[(i * Hq + hq) * D + d] = acc[d] / l;
+        }
+}
+
+/* lancius_kernels.c:248-272: rotary embedding on interleaved pairs, in place */
+void orc_rope(double* q, double* k, size_t B, size_t S, size_t H, size_t D, int pos_offset) {
+    for (size_t b = 0; b < B; b++)
+        for (size_t s = 0; s < S; s++)
+            for (size_t h = 0; h < H; h++)
+                for (size_t d = 0; d < D; d += 2) {
+                    double freq = 1.0 / pow(10000.0, (double)d / (double)D), ang = (double)((long)s + pos_offset) * freq;
+                    double c = cos(ang), sn = sin(ang);
+                    size_t i = ((b * S + s) * H + h) * D + d;
+                    double q0 = q[i], q1 = q[i + 1], k0 = k[i], k1 = k[i + 1];
+                    q[i] = q0 * c - q1 * sn; q[i + 1] = q0 * sn + q1 * c;
+                    k[i] = k0 * c - k1 * sn; k[i + 1] = k0 * sn + k1 * c;
+                }
+}
+
+/* lancius_kernels.c:62-91 */
+void orc_conv2d_bwd_in(double* out, const double* grad, const double* w, size_t N, size_t Ci, size_t H, size_t W,
+                       size_t Co, size_t Ho, size_t Wo, size_t Kh, size_t Kw, size_t stride, size_t pad) {
+    memset(out, 0, N * Ci * H * W * sizeof(double));
+    for (size_t n = 0; n < N; n++)
+        for (size_t co = 0; co < Co; co++)
+            for (size_t ho = 0; ho < Ho; ho++)
+                for (size_t wo = 0; wo < Wo; wo++) {
+                    double g = grad[((n * Co + co) * Ho + ho) * Wo + wo];
+                    for (size_t ci = 0; ci < Ci; ci++)
+                        for (size_t kh = 0; kh < Kh; kh++)
+                            for (size_t kw = 0; kw < Kw; kw++) {
+                                long ih = (long)(ho * stride) - (long)pad + (long)kh, iw = (long)(wo * stride) - (long)pad + (long)kw;
+                                if (ih < 0 || iw < 0 || ih >= (long)H || iw >= (long)W) continue;
+                                out[((n * Ci + ci) * H + (size_t)ih) * W + (size_t)iw] += g * w[((co * Ci + ci) * Kh + kh) * Kw + kw];
+                            }
+                }
+}
+
+/* lancius_kernels.c:93-136 (the per-thread accumulators there only change summation order) */
+void orc_conv2d_bwd_w(double* out, const double* grad, const double* in, size_t N, size_t Ci, size_t H, size_t W,
+                      size_t Co, size_t Ho, size_t Wo, size_t Kh, size_t Kw, size_t stride, size_t pad) {
+    memset(out, 0, Co * Ci * Kh * Kw * sizeof(double));
+    for (size_t n = 0; n < N; n++)
+        for (size_t co = 0; co < Co; co++)
+            for (size_t ho = 0; ho < Ho; ho++)
+                for (size_t wo = 0; wo < Wo; wo++) {
+                    double g = grad[((n * Co + co) * Ho + ho) * Wo + wo];
+                    for (size_t ci = 0; ci < Ci; ci++)
+                        for (size_t kh = 0; kh < Kh; kh++)
+                            for (size_t kw = 0; kw < Kw; kw++) {
+                                long ih = (long)(ho * stride) - (long)pad + (long)kh, iw = (long)(wo * stride) - (long)pad + (long)kw;
+                                if (ih < 0 || iw < 0 || ih >= (long)H || iw >= (long)W) continue;
+                                out[((co * Ci + ci) * Kh + kh) * Kw + kw] += g * in[((n * Ci + ci) * H + (size_t)ih) * W + (size_t)iw];
+                            }
+                }
+}
+
+/* lancius_vision_ops.c:149-190: gradient routed to the first maximum of each window */
+void orc_maxpool2d_bwd(double* out, const double* grad, const double* in, size_t N, size_t C, size_t H, size_t W,
+                       size_t Ho, size_t Wo, size_t K, size_t stride) {
+    memset(out, 0, N * C * H * W * sizeof(double));
+    for (size_t p = 0; p < N * C; p++)
+        for (size_t ho = 0; ho < Ho; ho++)
+            for (size_t wo = 0; wo < Wo; wo++) {
+                double m = -1e9;
+                size_t bi = 0, bj = 0;
+                for (size_t kh = 0; kh < K; kh++)
+                    for (size_t kw = 0; kw < K; kw++) {
+                        size_t ih = ho * stride + kh, iw = wo * stride + kw;
+                        double v = in[(p * H + ih) * W + iw];
+                        if (v > m) { m = v; bi = ih; bj = iw; }
+                    }
+                out[(p * H + bi) * W + bj] += grad[(p * Ho + ho) * Wo + wo];
+            }
+}
+
+/* lancius_scheduler.c:195-220: dynamic symmetric INT8 quantisation of A (scale max|a|/127,
+ * round half away from zero), int8 x int8 -> int32 products, result * scale_a * scale_b */
+void orc_matmul_int8(double* out, const double* a, const int8_t* b, double scale_b, size_t M, size_t K, size_t N) {
+    double mx = 0.0;
+    for (size_t i = 0; i < M * K; i++) { double v = fabs(a[i]); if (v > mx) mx = v; }
+    double sa = mx > 0.0 ? mx / 127.0 : 1e-8;
+    for (size_t r = 0; r < M; r++)
+        for (size_t c = 0; c < N; c++) {
+            int32_t acc = 0;
+            for (size_t k = 0; k < K; k++) acc += (int32_t)(int8_t)round(a[r * K + k] / sa) * (int32_t)b[k * N + c];
+            out[r * N + c] = (double)acc * (sa * scale_b);
+        }
+}
+
 /* ---- arena-mode graph executor: src/runtime/lancius_scheduler.c:61-362 ----- */
 
 static size_t elems(const lancius_node* n) { return lancius_node_elements(n); }
@@ -194,7 +309,12 @@ static void run_node(const lancius_node* n, double* o, double** R) {
     case LANCIUS_OP_MUL: for (size_t e = 0; e < E; e++) o[e] = a[e] * b[e]; break;       /* :236-240 */
     case LANCIUS_OP_RELU: for (size_t e = 0; e < E; e++) o[e] = a[e] > 0.0 ? a[e] : 0.0; break; /* :305-308 */
     case LANCIUS_OP_TANH: for (size_t e = 0; e < E; e++) o[e] = tanh(a[e]); break;
-    case LANCIUS_OP_MATMUL: orc_matmul(o, a, b, i0->shape[0], i0->shape[1], i1->shape[1]); break;
+    case LANCIUS_OP_MATMUL:
+        if (i1->runtime_data_int8 && i1->dtype == LANCIUS_DTYPE_INT8)
+            orc_matmul_int8(o, a, i1->runtime_data_int8, i1->scale, i0->shape[0], i0->shape[1], i1->shape[1]);
+        else
+            orc_matmul(o, a, b, i0->shape[0], i0->shape[1], i1->shape[1]);
+        break;
     case LANCIUS_OP_SOFTMAX: orc_softmax(o, a, n->shape[0], n->shape[1]); break;
     case LANCIUS_OP_SUM: { double s = 0.0; for (size_t e = 0; e < elems(i0); e++) s += a[e]; o[0] = s; } break;
     case LANCIUS_OP_SUM_AXIS0: {                                                          /* :257-262 */
@@ -214,6 +334,55 @@ static void run_node(const lancius_node* n, double* o, double** R) {
     case LANCIUS_OP_LAYERNORM: orc_layernorm(o, a, b, c, n->shape[0], n->shape[1], 1e-5); break; /* :109-115 */
     case LANCIUS_OP_GELU: orc_gelu(o, a, E); break;
     case LANCIUS_OP_RMSNORM: orc_rmsnorm(o, a, b, n->shape[0], n->shape[1], 1e-5); break;
+    case LANCIUS_OP_SWIGLU: orc_swiglu(o, a, b, E); break;
+    case LANCIUS_OP_GQA: orc_gqa(o, a, b, c, n->shape[0], n->kernel_h, n->kernel_w, n->shape[2]); break;
+    case LANCIUS_OP_RELU_BWD: for (size_t e = 0; e < E; e++) o[e] = b[e] > 0.0 ? a[e] : 0.0; break;   /* :279-283 */
+    case LANCIUS_OP_SOFTMAX_BWD: {                                                                    /* :295-304 */
+        size_t Rr = n->shape[0], Cc = n->shape[1];
+        for (size_t r = 0; r < Rr; r++) {
+            double dot = 0.0;
+            for (size_t cc = 0; cc < Cc; cc++) dot += a[r * Cc + cc] * b[r * Cc + cc];
+            for (size_t cc = 0; cc < Cc; cc++) o[r * Cc + cc] = b[r * Cc + cc] * (a[r * Cc + cc] - dot);
+        }
+    } break;
+    case LANCIUS_OP_CROSS_ENTROPY: {                                                                  /* :68-86 */
+        size_t Rr = i0->shape[0], Cc = i0->shape[1];
+        double tot = 0.0;
+        for (size_t r = 0; r < Rr; r++) {
+            double mx = a[r * Cc];
+            for (size_t cc = 1; cc < Cc; cc++) if (a[r * Cc + cc] > mx) mx = a[r * Cc + cc];
+            double se = 0.0;
+            for (size_t cc = 0; cc < Cc; cc++) se += exp(a[r * Cc + cc] - mx);
+            double lse = log(se) + mx;
+            for (size_t cc = 0; cc < Cc; cc++) if (b[r * Cc + cc] == 1.0) tot -= a[r * Cc + cc] - lse;
+        }
+        o[0] = fabs(tot / (double)Rr);
+    } break;
+    case LANCIUS_OP_CROSS_ENTROPY_BWD: {                                                              /* :90-106 */
+        size_t Rr = n->shape[0], Cc = n->shape[1];
+        double sc = c[0] / (double)Rr;
+        for (size_t r = 0; r < Rr; r++) {
+            double mx = a[r * Cc];
+            for (size_t cc = 1; cc < Cc; cc++) if (a[r * Cc + cc] > mx) mx = a[r * Cc + cc];
+            double se = 0.0;
+            for (size_t cc = 0; cc < Cc; cc++) se += exp(a[r * Cc + cc] - mx);
+            for (size_t cc = 0; cc < Cc; cc++) o[r * Cc + cc] = (exp(a[r * Cc + cc] - mx) / se - b[r * Cc + cc]) * sc;
+        }
+    } break;
+    case LANCIUS_OP_MAXPOOL2D_BWD: {
+        const lancius_node* g0 = n->inputs[0];
+        orc_maxpool2d_bwd(o, a, b, i1->shape[0], i1->shape[1], i1->shape[2], i1->shape[3], g0->shape[2], g0->shape[3],
+                          n->kernel_h, n->stride);
+    } break;
+    case LANCIUS_OP_CONV2D_BWD: {                                                                      /* vision_ops.c:126-137 */
+        const lancius_node* wn = n->inputs[2];
+        orc_conv2d_bwd_in(o, a, c, i1->shape[0], i1->shape[1], i1->shape[2], i1->shape[3], wn->shape[0], i0->shape[2],
+                          i0->shape[3], wn->shape[2], wn->shape[3], n->stride, n->pad);
+    } break;
+    case LANCIUS_OP_CONV2D_BWD_W:                                                                      /* vision_ops.c:138-148 */
+        orc_conv2d_bwd_w(o, a, b, i1->shape[0], i1->shape[1], i1->shape[2], i1->shape[3], n->shape[0], i0->shape[2],
+                         i0->shape[3], n->shape[2], n->shape[3], n->stride, n->pad);
+        break;
     case LANCIUS_OP_ATTENTION: orc_attention(o, a, b, c, n->shape[0], n->shape[1], n->shape[2], n->attr_val != 1.0); break;
     case LANCIUS_OP_CONV2D: case LANCIUS_OP_CONV2D_RELU_FUSED:                           /* vision_ops.c:60-81 */
         orc_conv2d(o, a, b, i0->shape[0], i0->shape[1], i0->shape[2], i0->shape[3], i1->shape[0],

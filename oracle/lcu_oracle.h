@@ -21,6 +21,16 @@ void orc_softmax(double* out, const double* in, size_t rows, size_t cols);
 void orc_attention(double* out, const double* q, const double* k, const double* v, size_t S, size_t H, size_t D, int causal);
 void orc_naive_attention(double* out, const double* q, const double* k, const double* v, size_t S, size_t H, size_t D);
 void orc_sum_axis1(double* out, const double* in, size_t rows, size_t cols);
+void orc_swiglu(double* out, const double* gate, const double* up, size_t n);
+void orc_gqa(double* out, const double* q, const double* k, const double* v, size_t S, size_t Hq, size_t Hkv, size_t D);
+void orc_rope(double* q, double* k, size_t B, size_t S, size_t H, size_t D, int pos_offset);
+void orc_conv2d_bwd_in(double* out, const double* grad, const double* w, size_t N, size_t Ci, size_t H, size_t W,
+                       size_t Co, size_t Ho, size_t Wo, size_t Kh, size_t Kw, size_t stride, size_t pad);
+void orc_conv2d_bwd_w(double* out, const double* grad, const double* in, size_t N, size_t Ci, size_t H, size_t W,
+                      size_t Co, size_t Ho, size_t Wo, size_t Kh, size_t Kw, size_t stride, size_t pad);
+void orc_maxpool2d_bwd(double* out, const double* grad, const double* in, size_t N, size_t C, size_t H, size_t W,
+                       size_t Ho, size_t Wo, size_t K, size_t stride);
+void orc_matmul_int8(double* out, const double* a, const int8_t* b, double scale_b, size_t M, size_t K, size_t N);
 void orc_rmsnorm(double* out, const double* in, const double* gamma, size_t rows, size_t hidden, double eps);
 
 /* Executes the graph on the CPU in arena mode (every node its own buffer).

@@ -1,0 +1,57 @@
+"""GPU parity of the training, LLM and INT8 operators (executor path) against the
+FP64 oracle; the oracle itself is pinned to the reference executor on these graphs
+(test_oracle_extra_ops.py). FP32 storage: normwise 1e-4."""
+import numpy as np
+import pytest
+
+from conftest import assert_close
+import lancius_b200 as L
+from lancius_b200 import opgraphs
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+
+@pytest.fixture(scope="module")
+def device():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    d = L.Device(0)
+    yield d
+    d.close()
+
+
+@pytest.mark.parametrize("build", [opgraphs.training_ops, opgraphs.llm_ops, opgraphs.int8_matmul])
+def test_extra_ops_on_gpu(device, orc, build):
+    g = L.Graph()
+    r = build(g)
+    inputs, outputs = r[0], r[-1]
+    for n, arr in inputs.items():
+        g.bind(n, np.asarray(arr, np.float32).astype(np.float64))   # FP32-exact inputs: same quantisation
+    if len(r) == 3:
+        for n, (q, scale) in r[1].items():
+            g.bind_int8(n, q, scale)
+    s = g.schedule()
+    device.set_graph_replay(False)
+    device.bind(s)
+    device.upload_bound_inputs()
+    device.execute(s)
+    want = orc.run_graph(g, outputs)
+    for o in outputs:
+        assert_close(device.download(o), want[o.id], 1e-4)
+
+
+def test_rope_and_gqa_per_op(orc):
+    import ctypes as C
+    from lancius_b200 import data, load
+    lib = load()
+    B, S, H, D = 1, 40, 4, 64
+    q = data.normal(1, (B, S, H, D)); k = data.normal(2, (B, S, H, D))
+    qd = torch.tensor(q.astype(np.float32), device="cuda"); kd = torch.tensor(k.astype(np.float32), device="cuda")
+    assert lib.lcu_rope(C.c_void_p(qd.data_ptr()), C.c_void_p(kd.data_ptr()), B, S, H, D, 3, None) == 0
+    torch.cuda.synchronize()
+    qr, kr = q.copy(), k.copy()
+    dp = lambda a: a.ctypes.data_as(C.POINTER(C.c_double))
+    orc.lib.orc_rope(dp(qr), dp(kr), C.c_size_t(B), C.c_size_t(S), C.c_size_t(H), C.c_size_t(D), C.c_int(3))
+    assert_close(qd.cpu().numpy(), qr, 1e-5)
+    assert_close(kd.cpu().numpy(), kr, 1e-5)
