@@ -34,7 +34,7 @@ struct Step {
     size_t table_off = 0;      // byte offset of the group table inside the allocation
     size_t M = 0, N = 0, K = 0;
     int epi = 0, op = 0, vec = 0, causal = 0, relu = 0;
-    int tc = 0, gb = 1;        // tensor-core GEMM; distinct B operands in the group
+    int tc = 0, ga = 1, gb = 1;   // tensor-core GEMM; distinct A / B operands in the group
     int plan_idx = -1, plan_mode = -1;
     size_t S = 0, H = 0, D = 0;
     size_t cn = 0, ci = 0, h = 0, w = 0, co = 0, kh = 0, kw = 0, stride = 0, pad = 0;
@@ -332,14 +332,23 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                     st.epi = b.chain[n->id].epi;
                     st.tc = lcu_use_tensor_cores(st.M, st.N, st.K) &&
                             !(n->inputs[1]->dtype == LANCIUS_DTYPE_INT8 && n->inputs[1]->runtime_data_int8);
-                    st.gb = ns.size();
+                    // distinct operands: same-shaped products of a wave often share A (Q/K/V of one
+                    // LayerNorm output) or B (the weight shared by all batch elements)
+                    std::vector<int> aidx(ns.size()), bidx(ns.size()), adup(ns.size(), 0), bdup(ns.size(), 0);
                     {
-                        bool shared_b = true;
-                        for (const lancius_node* x : ns) shared_b &= x->inputs[1] == n->inputs[1];
-                        if (shared_b) st.gb = 1;
+                        std::map<const lancius_node*, int> am, bm;
+                        for (size_t i = 0; i < ns.size(); i++) {
+                            auto ia = am.find(ns[i]->inputs[0]);
+                            if (ia == am.end()) { aidx[i] = (int)am.size(); am[ns[i]->inputs[0]] = aidx[i]; }
+                            else { aidx[i] = ia->second; adup[i] = 1; }
+                            auto ib = bm.find(ns[i]->inputs[1]);
+                            if (ib == bm.end()) { bidx[i] = (int)bm.size(); bm[ns[i]->inputs[1]] = bidx[i]; }
+                            else { bidx[i] = ib->second; bdup[i] = 1; }
+                        }
+                        st.ga = (int)am.size(); st.gb = (int)bm.size();
                     }
                     if (st.tc) {
-                        size_t need = lcu_gemm_tc_scratch_bytes(st.M, st.N, st.K, st.count, st.gb, 3);
+                        size_t need = lcu_gemm_tc_scratch_bytes(st.M, st.N, st.K, st.count, st.ga, st.gb, 3);
                         if (need > c->scratch_bytes) c->scratch_bytes = need;
                         st.plan_idx = (int)c->tc_plans.size();
                         c->tc_plans.push_back(LcuTcGemmPlan());
@@ -354,12 +363,14 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                         break;
                     }
                     std::vector<LcuGemmGroup> t;
-                    for (const lancius_node* x : ns) {
+                    for (size_t i = 0; i < ns.size(); i++) {
+                        const lancius_node* x = ns[i];
                         const Chain& ch = b.chain[x->id];
                         t.push_back(LcuGemmGroup{ptr_token(O(x->inputs[0])), ptr_token(O(x->inputs[1])),
                                                  (float*)ptr_token(O(x)),
                                                  ch.bias_src ? ptr_token(O(ch.bias_src)) : nullptr,
-                                                 ch.resid ? ptr_token(O(ch.resid)) : nullptr});
+                                                 ch.resid ? ptr_token(O(ch.resid)) : nullptr,
+                                                 aidx[i], bidx[i], adup[i], bdup[i]});
                     }
                     st.table_off = b.add_table(t);
                 } break;
@@ -427,7 +438,7 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                     st.M = st.co; st.N = st.cn * ho * wo; st.K = st.ci * st.kh * st.kw;
                     st.tc = st.cn && st.ci && lcu_use_tensor_cores(st.M, st.N, st.K);
                     if (st.tc) {
-                        size_t need = lcu_gemm_tc_scratch_bytes(st.M, st.N, st.K, 1, 1, 3);
+                        size_t need = lcu_gemm_tc_scratch_bytes(st.M, st.N, st.K, 1, 1, 1, 3);
                         if (need > c->scratch_bytes) c->scratch_bytes = need;
                         st.plan_idx = (int)c->tc_plans.size();
                         c->tc_plans.push_back(LcuTcGemmPlan());
@@ -725,7 +736,7 @@ static lancius_error run_steps(lcu_ctx* c) {
                     LcuTcGemmPlan& p = c->tc_plans[s.plan_idx];
                     int passes = c->mode == LCU_MODE_TF32 ? 1 : 3;
                     if (p.passes != passes || p.M != s.M) {
-                        e = lcu_gemm_tc_prepare(&p, c->scratch, s.M, s.N, s.K, s.count, s.gb, passes);
+                        e = lcu_gemm_tc_prepare(&p, c->scratch, s.M, s.N, s.K, s.count, s.ga, s.gb, passes);
                         if (e != LANCIUS_ERROR_OK) break;
                     }
                     e = lcu_gemm_tc_run(&p, (const LcuGemmGroup*)(base + s.table_off), s.epi, st);
@@ -756,7 +767,7 @@ static lancius_error run_steps(lcu_ctx* c) {
                     LcuTcGemmPlan& p = c->tc_plans[s.plan_idx];
                     int passes = c->mode == LCU_MODE_TF32 ? 1 : 3;
                     if (p.passes != passes || p.M != s.M) {
-                        e = lcu_gemm_tc_prepare(&p, c->scratch, s.M, s.N, s.K, 1, 1, passes);
+                        e = lcu_gemm_tc_prepare(&p, c->scratch, s.M, s.N, s.K, 1, 1, 1, passes);
                         if (e != LANCIUS_ERROR_OK) break;
                         size_t ho = (s.h + 2 * s.pad - s.kh) / s.stride + 1, wo = (s.w + 2 * s.pad - s.kw) / s.stride + 1;
                         p.conv = LcuConvShape{(int)s.cn, (int)s.ci, (int)s.h, (int)s.w, (int)s.co, (int)s.kh, (int)s.kw,

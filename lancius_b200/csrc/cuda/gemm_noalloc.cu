@@ -62,7 +62,7 @@ extern "C" lancius_error lcu_matmul_noalloc(float* out, const float* a, const fl
     if (M == 0 || N == 0 || K == 0) { lancius_set_error(LANCIUS_ERROR_SHAPE_MISMATCH); return LANCIUS_ERROR_SHAPE_MISMATCH; }
     if (M > (1u << 30) || N > (1u << 30) || K > (1u << 30)) { lancius_set_error(LANCIUS_ERROR_OVERFLOW); return LANCIUS_ERROR_OVERFLOW; }
     const int passes = mode == LCU_MODE_TF32 ? 1 : 3;
-    const size_t need = lcu_gemm_tc_scratch_bytes(M, N, K, 1, 1, passes) + 256;
+    const size_t need = lcu_gemm_tc_scratch_bytes(M, N, K, 1, 1, 1, passes) + 256;
     if (need > LCU_NOALLOC_SCRATCH_BYTES) {
         fprintf(stderr, "[LANCIUS CUDA] lcu_matmul_noalloc: %zux%zux%zu needs %zu scratch bytes, the fixed array holds %u\n",
                 M, K, N, need, LCU_NOALLOC_SCRATCH_BYTES);
@@ -84,7 +84,7 @@ extern "C" lancius_error lcu_matmul_noalloc(float* out, const float* a, const fl
     cudaError_t ce = cudaMemcpyAsync(d_group, &h, sizeof(h), cudaMemcpyHostToDevice, st);
     if (ce != cudaSuccess) return lcu_check_cuda(ce);
     LcuTcGemmPlan p;
-    lancius_error e = lcu_gemm_tc_prepare(&p, scratch, M, N, K, 1, 1, passes);
+    lancius_error e = lcu_gemm_tc_prepare(&p, scratch, M, N, K, 1, 1, 1, passes);
     if (e == LANCIUS_ERROR_OK) e = lcu_gemm_tc_run(&p, d_group, epilogue, stream);
     // `h` lives on this stack frame: wait until the copy (and the GEMM) ran
     lancius_error se = lcu_check_cuda(cudaStreamSynchronize(st));

@@ -47,7 +47,7 @@ struct Smem {
 __global__ void __launch_bounds__(THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
           const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
-          const LcuGemmGroup* __restrict__ groups, int M, int N, int K, int epi, int passes, int b_shared,
+          const LcuGemmGroup* __restrict__ groups, int M, int N, int K, int epi, int passes,
           int splits, int kchunk, float* __restrict__ partial, int conv_hw) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -55,7 +55,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     // blockIdx.z = group * splits + split; a split covers k in [k_begin, k_begin + kchunk)
-    const int g = blockIdx.z / splits, split = blockIdx.z % splits, gb = b_shared ? 0 : g;
+    const int g = blockIdx.z / splits, split = blockIdx.z % splits;
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
     const int k_begin = split * kchunk;
     const int k_end = min(K, k_begin + kchunk);
@@ -82,17 +82,18 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer ----------------
         const uint32_t tx = passes > 1 ? STAGE_BYTES : A_TILE + B_TILE;
+        const int ga = groups[g].aidx, gb = groups[g].bidx;      // scratch slots of this group's operands
         for (int kt = 0; kt < KT; kt++) {
             int s = kt % STAGES;
             if (kt >= STAGES && !tc::mbar_wait(&sm->empty[s], ((kt / STAGES) - 1) & 1, abort, &g_gemm_watchdog, 1)) break;
             uint8_t* st = tiles + s * STAGE_BYTES;
             tc::mbar_expect_tx(&sm->full[s], tx);
             int k0 = k_begin + kt * BK;
-            tc::tma_load_3d(st, &ta_hi, &sm->full[s], k0, m0, g);
+            tc::tma_load_3d(st, &ta_hi, &sm->full[s], k0, m0, ga);
             for (int j = 0; j < BN / 32; j++)
                 tc::tma_load_3d(st + 2 * A_TILE + j * B_CHUNK, &tb_hi, &sm->full[s], n0 + 32 * j, k0, gb);
             if (passes > 1) {
-                tc::tma_load_3d(st + A_TILE, &ta_lo, &sm->full[s], k0, m0, g);
+                tc::tma_load_3d(st + A_TILE, &ta_lo, &sm->full[s], k0, m0, ga);
                 for (int j = 0; j < BN / 32; j++)
                     tc::tma_load_3d(st + 2 * A_TILE + B_TILE + j * B_CHUNK, &tb_lo, &sm->full[s], n0 + 32 * j, k0, gb);
             }
@@ -227,8 +228,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
 // hi/lo split of `count` row-major [rows, cols] operands into pitched scratch
 __global__ void k_split(const LcuGemmGroup* __restrict__ groups, int which, size_t rows, size_t cols, size_t pitch,
                         float* __restrict__ hi, float* __restrict__ lo) {
-    const float* src = which == 0 ? groups[blockIdx.y].a : groups[blockIdx.y].b;
-    size_t base = (size_t)blockIdx.y * rows * pitch;
+    const LcuGemmGroup& gr = groups[blockIdx.y];
+    if (which == 0 ? gr.adup : gr.bdup) return;          // an earlier group already split this operand
+    const float* src = which == 0 ? gr.a : gr.b;
+    size_t base = (size_t)(which == 0 ? gr.aidx : gr.bidx) * rows * pitch;
     size_t n = rows * cols;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
         size_t r = i / cols, c = i % cols;
@@ -331,18 +334,18 @@ size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
 constexpr int kMaxChunk = 8192;
 int split_count(size_t K) { return K > (size_t)kMaxChunk ? (int)((K + kMaxChunk - 1) / kMaxChunk) : 1; }
 
-extern "C" size_t lcu_gemm_tc_scratch_bytes(size_t M, size_t N, size_t K, int G, int Gb, int passes) {
-    size_t a = al256((size_t)G * M * pad4(K) * 4), b = al256((size_t)Gb * K * pad4(N) * 4);
+extern "C" size_t lcu_gemm_tc_scratch_bytes(size_t M, size_t N, size_t K, int G, int Ga, int Gb, int passes) {
+    size_t a = al256((size_t)Ga * M * pad4(K) * 4), b = al256((size_t)Gb * K * pad4(N) * 4);
     int sp = split_count(K);
     size_t part = sp > 1 ? al256((size_t)G * sp * M * N * 4) : 0;
     return (passes > 1 ? 2 * (a + b) : a + b) + part;
 }
 
 extern "C" lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, size_t M, size_t N, size_t K, int G,
-                                             int Gb, int passes) {
-    p->M = M; p->N = N; p->K = K; p->Kp = pad4(K); p->Np = pad4(N); p->G = G; p->Gb = Gb; p->passes = passes;
+                                             int Ga, int Gb, int passes) {
+    p->M = M; p->N = N; p->K = K; p->Kp = pad4(K); p->Np = pad4(N); p->G = G; p->Ga = Ga; p->Gb = Gb; p->passes = passes;
     p->conv = LcuConvShape{};
-    size_t a = al256((size_t)G * M * p->Kp * 4), b = al256((size_t)Gb * K * p->Np * 4);
+    size_t a = al256((size_t)Ga * M * p->Kp * 4), b = al256((size_t)Gb * K * p->Np * 4);
     char* s = static_cast<char*>(scratch);
     p->s_ahi = (float*)s; s += a;
     p->s_bhi = (float*)s; s += b;
@@ -351,10 +354,10 @@ extern "C" lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, si
     p->splits = split_count(K);
     p->kchunk = p->splits > 1 ? (int)(((K + p->splits - 1) / p->splits + BK - 1) / BK * BK) : (int)(K ? K : 1);
     p->partial = p->splits > 1 ? (float*)s : nullptr;
-    bool ok = make_map(&p->a_hi, p->s_ahi, K, M, G, p->Kp, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B) &&
+    bool ok = make_map(&p->a_hi, p->s_ahi, K, M, Ga, p->Kp, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B) &&
               make_map(&p->b_hi, p->s_bhi, N, K, Gb, p->Np, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     if (ok && passes > 1)
-        ok = make_map(&p->a_lo, p->s_alo, K, M, G, p->Kp, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B) &&
+        ok = make_map(&p->a_lo, p->s_alo, K, M, Ga, p->Kp, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B) &&
              make_map(&p->b_lo, p->s_blo, N, K, Gb, p->Np, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     else if (ok) { p->a_lo = p->a_hi; p->b_lo = p->b_hi; }
     if (!ok) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
@@ -381,12 +384,12 @@ extern "C" lancius_error lcu_gemm_tc_run(const LcuTcGemmPlan* p, const LcuGemmGr
             k_im2col_split<<<dim3((unsigned)((p->N + 1023) / 1024 < 64 ? (p->N + 1023) / 1024 : 64), (unsigned)p->K), 256, 0, st>>>(
                 d_groups, p->conv, p->Np, p->s_bhi, lo_b);
         else
-            k_split<<<dim3(lcu_blocks(p->K * p->N, 256 * 8, 148 * 4), p->Gb), 256, 0, st>>>(d_groups, 1, p->K, p->N, p->Np, p->s_bhi, lo_b);
+            k_split<<<dim3(lcu_blocks(p->K * p->N, 256 * 8, 148 * 4), p->G), 256, 0, st>>>(d_groups, 1, p->K, p->N, p->Np, p->s_bhi, lo_b);
         lcu_note_launch();
     }
     dim3 grid((unsigned)((p->N + BN - 1) / BN), (unsigned)((p->M + BM - 1) / BM), (unsigned)(p->G * p->splits));
     k_gemm_tc<<<grid, THREADS, SMEM_BYTES, st>>>(p->a_hi, p->a_lo, p->b_hi, p->b_lo, d_groups, (int)p->M, (int)p->N,
-                                                 (int)p->K, epi, p->passes, p->Gb == 1 && p->G > 1 ? 1 : 0,
+                                                 (int)p->K, epi, p->passes,
                                                  p->splits, p->kchunk, p->partial, p->conv.n ? p->conv.ho * p->conv.wo : 0);
     lcu_note_launch();
     if (p->splits > 1) {
@@ -438,7 +441,7 @@ extern "C" void* lcu_scratch_acquire_gather(size_t bytes) { return acquire_from(
 extern "C" lancius_error lcu_gemm_tc(float* c, const float* a, const float* b, size_t M, size_t K, size_t N,
                                      const float* bias, int epi, int mode, void* stream) {
     int passes = mode == LCU_MODE_TF32 ? 1 : 3;
-    size_t need = lcu_gemm_tc_scratch_bytes(M, N, K, 1, 1, passes) + 256;
+    size_t need = lcu_gemm_tc_scratch_bytes(M, N, K, 1, 1, 1, passes) + 256;
     char* scratch = static_cast<char*>(lcu_scratch_acquire(need));
     if (!scratch) { lancius_set_error(LANCIUS_ERROR_OOM); return LANCIUS_ERROR_OOM; }
     // the one-entry group table lives at the end of the scratch region
@@ -448,7 +451,7 @@ extern "C" lancius_error lcu_gemm_tc(float* c, const float* a, const float* b, s
     cudaError_t ce = cudaMemcpyAsync(d_group, &h, sizeof(h), cudaMemcpyHostToDevice, st);
     if (ce != cudaSuccess) return lcu_check_cuda(ce);
     LcuTcGemmPlan p;
-    lancius_error e = lcu_gemm_tc_prepare(&p, scratch, M, N, K, 1, 1, passes);
+    lancius_error e = lcu_gemm_tc_prepare(&p, scratch, M, N, K, 1, 1, 1, passes);
     if (e != LANCIUS_ERROR_OK) return e;
     e = lcu_gemm_tc_run(&p, d_group, epi, stream);
     // the host-side group record must stay valid until the copy ran
@@ -462,7 +465,7 @@ extern "C" lancius_error lcu_conv2d_tc(float* out, const float* in, const float*
                                        void* stream) {
     const int passes = mode == LCU_MODE_TF32 ? 1 : 3;
     const size_t M = cs.co, K = (size_t)cs.ci * cs.kh * cs.kw, N = (size_t)cs.n * cs.ho * cs.wo;
-    const size_t need = lcu_gemm_tc_scratch_bytes(M, N, K, 1, 1, passes) + 256;
+    const size_t need = lcu_gemm_tc_scratch_bytes(M, N, K, 1, 1, 1, passes) + 256;
     char* scratch = static_cast<char*>(lcu_scratch_acquire(need));
     if (!scratch) { lancius_set_error(LANCIUS_ERROR_OOM); return LANCIUS_ERROR_OOM; }
     LcuGemmGroup* d_group = reinterpret_cast<LcuGemmGroup*>(scratch + need - 256);
@@ -471,7 +474,7 @@ extern "C" lancius_error lcu_conv2d_tc(float* out, const float* in, const float*
     cudaError_t ce = cudaMemcpyAsync(d_group, &h, sizeof(h), cudaMemcpyHostToDevice, st);
     if (ce != cudaSuccess) return lcu_check_cuda(ce);
     LcuTcGemmPlan p;
-    lancius_error e = lcu_gemm_tc_prepare(&p, scratch, M, N, K, 1, 1, passes);
+    lancius_error e = lcu_gemm_tc_prepare(&p, scratch, M, N, K, 1, 1, 1, passes);
     if (e != LANCIUS_ERROR_OK) return e;
     p.conv = cs;
     e = lcu_gemm_tc_run(&p, d_group, relu ? LCU_EPI_RELU : LCU_EPI_NONE, stream);

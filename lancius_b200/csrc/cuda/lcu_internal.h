@@ -11,6 +11,9 @@ struct LcuGemmGroup {        // one independent product C = act(A*B + bias) + re
     float* c;
     const float* bias;   // [N] row vector added to every row, or NULL
     const float* resid;  // [M,N] added after the activation, or NULL
+    // tensor-core path: scratch slot of this group's hi/lo A and B copies; a group whose
+    // operand equals an earlier group's (adup/bdup = 1) reuses that slot and skips the split
+    int aidx, bidx, adup, bdup;
 };
 struct LcuAttnGroup { const float* q; const float* k; const float* v; float* o; };
 struct LcuEltGroup { float* out; const float* a; const float* b; };
@@ -23,15 +26,16 @@ struct LcuTcGemmPlan {
     CUtensorMap a_hi, a_lo, b_hi, b_lo;
     float *s_ahi, *s_alo, *s_bhi, *s_blo;
     size_t M, N, K, Kp, Np;
-    int G, Gb, passes;
+    int G, Ga, Gb, passes;       // groups, distinct A operands, distinct B operands
     int splits, kchunk;          // K cut into `splits` chunks of kchunk (multiple of 16)
     float* partial;              // [G][splits][M][N] partial sums when splits > 1
     LcuConvShape conv;           // conv.n > 0: B is the im2col of groups[0].b, C is stored NCHW
 };
 
 extern "C" {
-size_t lcu_gemm_tc_scratch_bytes(size_t M, size_t N, size_t K, int G, int Gb, int passes);
-lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, size_t M, size_t N, size_t K, int G, int Gb, int passes);
+size_t lcu_gemm_tc_scratch_bytes(size_t M, size_t N, size_t K, int G, int Ga, int Gb, int passes);
+lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, size_t M, size_t N, size_t K, int G, int Ga, int Gb,
+                                  int passes);
 lancius_error lcu_gemm_tc_run(const LcuTcGemmPlan* p, const LcuGemmGroup* d_groups, int epi, void* stream);
 lancius_error lcu_gemm_simt_grouped(const LcuGemmGroup* d_groups, int count, size_t M, size_t N, size_t K, int epi,
                                     void* stream);
