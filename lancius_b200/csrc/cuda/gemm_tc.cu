@@ -24,13 +24,13 @@
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4, THREADS = 192;
-constexpr int A_TILE = BM * BK * 4;                  // 8 KB
+constexpr int BM = 256, BN = 256, BK = 16, STAGES = 3, THREADS = 192;
+constexpr int A_TILE = BM * BK * 4;                  // 16 KB (two 128-row halves)
 constexpr int B_CHUNK = BK * 32 * 4;                 // 2 KB: 16 k-rows x 32 n
 constexpr int B_TILE = BN * BK * 4;                  // 16 KB
-constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE; // 48 KB
+constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE; // 64 KB
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
-constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t TMEM_COLS = 512;   // two 128x256 FP32 accumulators (rows 0-127, 128-255)
 
 __device__ int g_gemm_watchdog = 0;
 
@@ -101,7 +101,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
         }
     } else if (warp == 1 && lane == 0) {
         // ---------------- MMA issuer ----------------
-        constexpr uint32_t idesc = tc::idesc_tf32(BM, BN, false, true);
+        constexpr uint32_t idesc = tc::idesc_tf32(128, BN, false, true);
         bool ok = true;
         for (int kt = 0; kt < KT && ok; kt++) {
             int s = kt % STAGES;
@@ -117,17 +117,21 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
             uint32_t a_hi = st, a_lo = st + A_TILE, b_hi = st + 2 * A_TILE, b_lo = st + 2 * A_TILE + B_TILE;
 #pragma unroll
             for (int kb = 0; kb < BK / 8; kb++) {
-                uint64_t dah = tc::smem_desc(a_hi + kb * 32, 16, 512, tc::SWZ_64B);
                 uint64_t dbh = tc::smem_desc(b_hi + kb * 1024, B_CHUNK, 512, tc::SWZ_128B_BASE32B);
-                uint32_t acc = (kt | kb) ? 1u : 0u;
-                if (passes > 1) {
-                    uint64_t dal = tc::smem_desc(a_lo + kb * 32, 16, 512, tc::SWZ_64B);
-                    uint64_t dbl = tc::smem_desc(b_lo + kb * 1024, B_CHUNK, 512, tc::SWZ_128B_BASE32B);
-                    tc::mma_tf32(tmem, dal, dbh, idesc, acc);      // small terms first
-                    tc::mma_tf32(tmem, dah, dbl, idesc, 1u);
-                    tc::mma_tf32(tmem, dah, dbh, idesc, 1u);
-                } else {
-                    tc::mma_tf32(tmem, dah, dbh, idesc, acc);
+                uint64_t dbl = tc::smem_desc(b_lo + kb * 1024, B_CHUNK, 512, tc::SWZ_128B_BASE32B);
+#pragma unroll
+                for (int half = 0; half < 2; half++) {       // rows 0-127 and 128-255 share the B tile
+                    const uint32_t hoff = (uint32_t)half * (128 * BK * 4), d = tmem + (uint32_t)half * BN;
+                    uint64_t dah = tc::smem_desc(a_hi + hoff + kb * 32, 16, 512, tc::SWZ_64B);
+                    uint32_t acc = (kt | kb) ? 1u : 0u;
+                    if (passes > 1) {
+                        uint64_t dal = tc::smem_desc(a_lo + hoff + kb * 32, 16, 512, tc::SWZ_64B);
+                        tc::mma_tf32(d, dal, dbh, idesc, acc);      // small terms first
+                        tc::mma_tf32(d, dah, dbl, idesc, 1u);
+                        tc::mma_tf32(d, dah, dbh, idesc, 1u);
+                    } else {
+                        tc::mma_tf32(d, dah, dbh, idesc, acc);
+                    }
                 }
             }
             tc::mma_commit(&sm->empty[s]);          // stage s is free once these MMAs retire
@@ -145,13 +149,15 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
             }
             const int epi_here = splits > 1 ? LCU_EPI_NONE : epi;
             const int q = warp & 3;                    // TMEM lane quadrant of this warp
-            const int row = m0 + 32 * q + lane;
+            for (int half = 0; half < 2; half++) {
+            const int row = m0 + half * 128 + 32 * q + lane;
+            if (m0 + half * 128 >= M) break;           // warp-uniform
             const bool vec = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(gr.c) & 15) == 0) &&
                              (!gr.resid || (reinterpret_cast<uintptr_t>(gr.resid) & 15) == 0);
             for (int c = 0; c < BN; c += 32) {
                 if (n0 + c >= N) break;                // warp-uniform
                 float v[32];
-                tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)c, v);
+                tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * BN + c), v);
                 if (LCU_GEMM_DEBUG && blockIdx.x == 0 && blockIdx.y == 0 && c == 0 && (lane == 0 || lane == 1) && q == 0)
                     printf("row %d v=%g %g %g %g %g %g\n", row, v[0], v[1], v[2], v[3], v[4], v[5]);
                 if (row >= M) continue;
@@ -201,6 +207,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
                     }
                 }
             }
+            }   // half
         }
     }
 
