@@ -14,9 +14,10 @@
 //                S_0, S_1, PV_0, S_2, PV_1, ...
 //              S_j = Q K_j^T (A = Q from TMEM), O += P_j V_j (A = P_j from TMEM).
 //              tcgen05 costs about the same per instruction whatever its N, so the
-//              hi/lo halves of B are concatenated along N: Q_hi*[K_hi|K_lo] and
-//              Q_lo*[K_hi|K_lo] (N = 128) accumulate hh+lh in the left and hl+ll in
-//              the right half of S, and S = left + right; same for P*[V_hi|V_lo] into O
+//              hi/lo halves of B are concatenated along N: Q_hi*[K_hi|K_lo] (N = 128)
+//              and Q_lo*K_hi (N = 64) accumulate Q_hi K_hi + Q_lo K_hi in the left and
+//              Q_hi K_lo in the right half of S, and S = left + right; same for
+//              P_hi*[V_hi|V_lo] and P_lo*V_hi into O
 //   warps 5-8  loaders: K_j, V_j from global (coalesced float4, next tile prefetched
 //              into registers), split hi/lo, stored in the swizzled layouts tcgen05
 //              reads (K: K-major 128B swizzle; V: N-major 128B swizzle, 32B atoms)
@@ -76,15 +77,22 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-struct Item { LcuAttnGroup p; int h, q0, T; };
+struct Item { LcuAttnGroup p; int h, q0, T; bool valid; };
 
-// Work item i of the persistent grid: heaviest query tiles first (causal cost grows
-// with the tile index), then batch element, then head.
-__device__ __forceinline__ Item get_item(int i, const LcuAttnGroup* table, const LcuAttnGroup& base, size_t bstride,
+// Work slots of the persistent grid. Causal cost grows with the query tile index, so
+// tile qt is paired with tile nqt-1-qt: slot 2p is the heavy member of pair p, slot
+// 2p+1 the light one (empty for the middle tile of an odd nqt), and every pair costs
+// the same number of key tiles. A CTA takes both slots of a pair, then strides by the
+// grid over pairs; pairs are ordered so the light (unpaired) ones come last.
+__device__ __forceinline__ int next_slot(int x) { return (x & 1) ? x - 1 + 2 * (int)gridDim.x : x + 1; }
+
+__device__ __forceinline__ Item get_item(int x, const LcuAttnGroup* table, const LcuAttnGroup& base, size_t bstride,
                                          int B, int H, int nqt, int S, int causal) {
     Item it;
     const int per = B * H;
-    const int qt = nqt - 1 - i / per, r = i % per, b = r / H;
+    const int pair = x >> 1, qp = pair / per, r = pair % per, b = r / H;
+    const int qt = (x & 1) ? qp : nqt - 1 - qp;
+    it.valid = !((x & 1) && qt == nqt - 1 - qp);
     it.h = r % H;
     if (table) it.p = table[b];
     else {
@@ -108,7 +116,7 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nqt = (S + BQ - 1) / BQ;
-    const int n_items = nqt * B * H;
+    const int n_slots = 2 * ((nqt + 1) / 2) * B * H;
     const size_t rs = (size_t)H * D;                // row stride of [S, H, D]
     volatile int* abort = &bar->abort;
 
@@ -142,8 +150,9 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
         const uint32_t lb = tm + ((uint32_t)(32 * warp) << 16);
         int gt = 0;
         bool ok = true;
-        for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
-            const Item it = get_item(i, table, base, bstride, B, H, nqt, S, causal);
+        for (int x = 2 * (int)blockIdx.x; x < n_slots && ok; x = next_slot(x)) {
+            const Item it = get_item(x, table, base, bstride, B, H, nqt, S, causal);
+            if (!it.valid) continue;
             const int qi = it.q0 + row;
             {   // Q row -> TMEM hi/lo (the previous item is fully read out at this point)
                 float hi[32], lo[32];
@@ -175,7 +184,7 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                 for (int half = 0; half < 2; half++) {
                     float a[32], b[32];
                     tc::tmem_ld32(lb + TM_S + half * 32, a);         // Q_hi K_hi + Q_lo K_hi
-                    tc::tmem_ld32(lb + TM_S + 64 + half * 32, b);    // Q_hi K_lo + Q_lo K_lo
+                    tc::tmem_ld32(lb + TM_S + 64 + half * 32, b);    // Q_hi K_lo
 #pragma unroll
                     for (int c = 0; c < 32; c++) s[half * 32 + c] = (a[c] + b[c]) * scale_log2;
                 }
@@ -241,7 +250,7 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                 for (int half = 0; half < 2; half++) {
                     float o[32], o2[32];
                     tc::tmem_ld32(lb + TM_O + half * 32, o);         // P_hi V_hi + P_lo V_hi
-                    tc::tmem_ld32(lb + TM_O + 64 + half * 32, o2);   // P_hi V_lo + P_lo V_lo
+                    tc::tmem_ld32(lb + TM_O + 64 + half * 32, o2);   // P_hi V_lo
                     if (qi < S) {
                         float4* dst = reinterpret_cast<float4*>(it.p.o + (size_t)qi * rs + (size_t)it.h * D + half * 32);
 #pragma unroll
@@ -259,6 +268,10 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
         if (lane == 0) {
             constexpr uint32_t id_s = tc::idesc_tf32(BQ, 2 * BKV, false, false);
             constexpr uint32_t id_o = tc::idesc_tf32(BQ, 2 * D, false, true);
+            // the lo x lo product is below FP32 resolution: the lo operand multiplies only
+            // the hi half of B (N = 64)
+            constexpr uint32_t id_s_lo = tc::idesc_tf32(BQ, BKV, false, false);
+            constexpr uint32_t id_o_lo = tc::idesc_tf32(BQ, D, false, true);
             bool ok = true;
             int gt = 0, ii = 0;
             auto issue_s = [&](int g) -> bool {
@@ -271,16 +284,17 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                 for (int kb = 0; kb < D / 8; kb++) {
                     const uint32_t off = (uint32_t)((kb >> 2) * (2 * BKV * 128) + (kb & 3) * 32);
                     const uint64_t bk = tc::smem_desc(kb0 + off, 16, 1024, tc::SWZ_128B);   // [K_hi | K_lo]
-                    tc::mma_tf32_ts(tm + TM_S, tm + TM_QLO + kb * 8, bk, id_s, kb ? 1u : 0u);
-                    tc::mma_tf32_ts(tm + TM_S, tm + TM_QHI + kb * 8, bk, id_s, 1u);
+                    tc::mma_tf32_ts(tm + TM_S, tm + TM_QHI + kb * 8, bk, id_s, kb ? 1u : 0u);
+                    tc::mma_tf32_ts(tm + TM_S, tm + TM_QLO + kb * 8, bk, id_s_lo, 1u);
                 }
                 tc::mma_commit(&bar->s_full);
                 tc::mma_commit(&bar->k_empty[st]);
                 if (g < 8) TRACE(34 + g);
                 return true;
             };
-            for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ii++) {
-                const Item it = get_item(i, table, base, bstride, B, H, nqt, S, causal);
+            for (int x = 2 * (int)blockIdx.x; x < n_slots && ok; x = next_slot(x)) {
+                const Item it = get_item(x, table, base, bstride, B, H, nqt, S, causal);
+                if (!it.valid) continue;
                 if (!tc::mbar_wait(&bar->q_ready, ii & 1, abort, &g_attn_watchdog, 21)) { ok = false; break; }
                 if (it.T > 0 && !(ok = issue_s(gt))) break;
                 for (int j = 0; j < it.T; j++, gt++) {
@@ -296,13 +310,14 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                     for (int kb = 0; kb < BKV / 8; kb++) {
                         const uint64_t bv = tc::smem_desc(vb0 + kb * 1024, BKV * 128, 512, tc::SWZ_128B_BASE32B);   // [V_hi | V_lo]
                         const uint32_t acc0 = (j | kb) ? 1u : 0u;
-                        tc::mma_tf32_ts(tm + TM_O, tm + TM_P + 64 + kb * 8, bv, id_o, acc0);
-                        tc::mma_tf32_ts(tm + TM_O, tm + TM_P + kb * 8, bv, id_o, 1u);
+                        tc::mma_tf32_ts(tm + TM_O, tm + TM_P + kb * 8, bv, id_o, acc0);
+                        tc::mma_tf32_ts(tm + TM_O, tm + TM_P + 64 + kb * 8, bv, id_o_lo, 1u);
                     }
                     tc::mma_commit(&bar->pv_done);
                     tc::mma_commit(&bar->v_empty[st]);
                     if (gt < 8) TRACE(42 + gt);
                 }
+                ii++;
             }
         }
     } else {
@@ -311,8 +326,9 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
         const int jr = t >> 1, d0 = (t & 1) * 32;        // key row within tile, d half
         int gt = 0;
         bool ok = true;
-        for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
-            const Item it = get_item(i, table, base, bstride, B, H, nqt, S, causal);
+        for (int x = 2 * (int)blockIdx.x; x < n_slots && ok; x = next_slot(x)) {
+            const Item it = get_item(x, table, base, bstride, B, H, nqt, S, causal);
+            if (!it.valid) continue;
             float4 kv[8], vv[8];
             auto fetch = [&](int j) {
                 const int key = j * BKV + jr;
@@ -395,15 +411,15 @@ extern "C" lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const flo
     LcuAttnGroup base{q, k, v, o};
     float scale_log2 = (float)(1.4426950408889634 / 8.0);   // log2(e) / sqrt(64)
     // persistent grid: one CTA per SM (TMEM and shared memory allow no more), each walks
-    // the heaviest-first item list with stride gridDim.x
+    // pairs of query tiles of equal total cost with stride gridDim.x
     static int sms = 0;
     if (!sms) {
         int dev = 0;
         cudaGetDevice(&dev);
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = LCU_SMS;
     }
-    const size_t items = ((S + BQ - 1) / BQ) * H * B;
-    const unsigned grid = (unsigned)(items < (size_t)sms ? items : (size_t)sms);
+    const size_t pairs = ((S + BQ - 1) / BQ + 1) / 2 * H * B;
+    const unsigned grid = (unsigned)(pairs < (size_t)sms ? pairs : (size_t)sms);
     k_attn_tc<<<grid, THREADS, SMEM_BYTES, lcu_as_stream(stream)>>>(d_table, base, S * H * D, (int)B, (int)S, (int)H,
                                                                      causal, scale_log2);
     lcu_note_launch();
