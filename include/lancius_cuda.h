@@ -67,6 +67,9 @@ float* lcu_node_device_ptr(lcu_ctx* ctx, const lancius_node* n);
  * lancius_schedule_execute(schedule, scratch): the second argument is the
  * device context instead of a host arena. Errors: lancius_get_error(). */
 void lancius_schedule_execute_cuda(lancius_schedule* sched, lcu_ctx* ctx);
+/* Text of the last CUDA status this thread turned into LANCIUS_ERROR_INTERNAL/OOM
+ * ("no error" if none); a diagnostic companion of lancius_get_error(). */
+const char* lcu_last_cuda_error(void);
 /* Number of kernels the last lancius_schedule_execute_cuda call launched. */
 int lcu_last_launch_count(lcu_ctx* ctx);
 /* 1 = replay the schedule through a captured CUDA graph after the first run. */

@@ -121,6 +121,7 @@ B200_FUNCS = {
     "lcu_node_device_ptr": (P, [P, NODE_P]),
     "lancius_schedule_execute_cuda": (None, [SCHED_P, P]),
     "lcu_last_launch_count": (C.c_int, [P]),
+    "lcu_last_cuda_error": (C.c_char_p, []),
     "lcu_set_graph_replay": (C.c_int, [P, C.c_int]),
     "lcu_set_fusion": (C.c_int, [P, C.c_int]),
     "lcu_host_alloc": (P, [c_size]),

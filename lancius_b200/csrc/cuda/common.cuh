@@ -10,8 +10,10 @@
 static inline cudaStream_t lcu_as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 
 // Map a CUDA status onto the Lancius thread-local error and return it.
+extern "C" void lcu_note_cuda_error(int e);
 static inline lancius_error lcu_check_cuda(cudaError_t e) {
     if (e == cudaSuccess) return LANCIUS_ERROR_OK;
+    lcu_note_cuda_error((int)e);
     lancius_error le = (e == cudaErrorMemoryAllocation) ? LANCIUS_ERROR_OOM : LANCIUS_ERROR_INTERNAL;
     lancius_set_error(le);
     return le;

@@ -5,6 +5,12 @@
 
 static thread_local int tl_launches = 0;
 extern "C" void lcu_note_launch(void) { tl_launches++; }
+
+static thread_local int tl_cuda_error = 0;
+extern "C" void lcu_note_cuda_error(int e) { tl_cuda_error = e; }
+extern "C" const char* lcu_last_cuda_error(void) {
+    return tl_cuda_error ? cudaGetErrorString((cudaError_t)tl_cuda_error) : "no error";
+}
 extern "C" void lcu_reset_launch_count(void) { tl_launches = 0; }
 extern "C" int lcu_launch_count(void) { return tl_launches; }
 

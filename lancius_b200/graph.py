@@ -14,7 +14,14 @@ from ._lib import load
 
 class LanciusError(RuntimeError):
     def __init__(self, code, what=""):
-        super().__init__(f"{what}: lancius error {code}")
+        detail = ""
+        try:
+            msg = load().lcu_last_cuda_error()
+            if msg and msg != b"no error":
+                detail = f" (CUDA: {msg.decode()})"
+        except Exception:
+            pass
+        super().__init__(f"{what}: lancius error {code}{detail}")
         self.code = code
 
 
