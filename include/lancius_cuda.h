@@ -162,6 +162,15 @@ lancius_error lcu_swiglu(float* out, const float* gate, const float* up, size_t 
 lancius_error lcu_rope(float* q, float* k, size_t B, size_t S, size_t H, size_t D, int pos_offset, void* stream); /* :248-272 */
 lancius_error lcu_gqa(float* out, const float* q, const float* k, const float* v, size_t S, size_t Hq, size_t Hkv,
                       size_t D, void* stream);                                                   /* :407-448 */
+/* KV-cache decode attention, lancius_kernels.c:338-379 (kernel_attention_kv_cache):
+ * out[H*D] = softmax(q . K^T / sqrt(D)) V over all seq_len cached rows; caches
+ * [seq_len][H][D], q and out [H*D]. head_dim <= 256. The batched form takes B
+ * sequences at once: q, out [B][H*D], caches [B][seq_len][H][D]. */
+lancius_error lcu_attention_kv_cache(float* out, const float* q, const float* k_cache, const float* v_cache,
+                                     size_t seq_len, size_t n_heads, size_t head_dim, void* stream);
+lancius_error lcu_attention_kv_cache_batched(float* out, const float* q, const float* k_cache, const float* v_cache,
+                                             size_t batch, size_t seq_len, size_t n_heads, size_t head_dim,
+                                             void* stream);
 lancius_error lcu_maxpool2d_bwd(float* out, const float* grad, const float* in, size_t N, size_t C, size_t H, size_t W,
                                 size_t K, size_t stride, void* stream);                          /* vision_ops.c:149-190 */
 lancius_error lcu_conv2d_bwd(float* out, const float* grad, const float* w, size_t N, size_t C_in, size_t H, size_t W,

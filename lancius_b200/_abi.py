@@ -154,6 +154,8 @@ B200_FUNCS = {
     "lcu_swiglu": (C.c_int, [P, P, P, c_size, P]),
     "lcu_rope": (C.c_int, [P, P, c_size, c_size, c_size, c_size, C.c_int, P]),
     "lcu_gqa": (C.c_int, [P, P, P, P, c_size, c_size, c_size, c_size, P]),
+    "lcu_attention_kv_cache": (C.c_int, [P, P, P, P, c_size, c_size, c_size, P]),
+    "lcu_attention_kv_cache_batched": (C.c_int, [P, P, P, P, c_size, c_size, c_size, c_size, P]),
     "lcu_comm_unique_id": (C.c_int, [P, c_size]),
     "lcu_comm_create": (P, [C.c_int, C.c_int, P, C.c_int]),
     "lcu_comm_destroy": (None, [P]),

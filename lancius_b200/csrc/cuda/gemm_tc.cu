@@ -439,11 +439,13 @@ static void* acquire_from(std::vector<ScratchCache>& cache, size_t bytes) {
     return c.p;
 }
 
-namespace { std::vector<ScratchCache> g_gather; }
+namespace { std::vector<ScratchCache> g_gather, g_decode; }
 // Per-device cached buffers that grow on demand: GEMM/conv operand scratch, and a
 // second one for the column-split all-gather (both alive during one colsplit call).
 extern "C" void* lcu_scratch_acquire(size_t bytes) { return acquire_from(g_scratch, bytes); }
 extern "C" void* lcu_scratch_acquire_gather(size_t bytes) { return acquire_from(g_gather, bytes); }
+// split-KV partials of the decode attention
+extern "C" void* lcu_scratch_acquire_decode(size_t bytes) { return acquire_from(g_decode, bytes); }
 
 extern "C" lancius_error lcu_gemm_tc(float* c, const float* a, const float* b, size_t M, size_t K, size_t N,
                                      const float* bias, int epi, int mode, void* stream) {

@@ -65,6 +65,7 @@ lancius_error lcu_conv2d_int8(float* out, const float* in, const int8_t* w, doub
                               size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu,
                               float* amax_scratch, void* s);
 void* lcu_scratch_acquire_gather(size_t bytes);
+void* lcu_scratch_acquire_decode(size_t bytes);
 lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, const float* k, const float* v, float* o,
                                size_t B, size_t S, size_t H, int causal, void* stream);
 int lcu_attention_watchdog_read_and_clear(void);

@@ -205,6 +205,30 @@ void orc_gqa(double* out, const double* q, const double* k, const double* v, siz
         }
 }
 
+/* lancius_kernels.c:338-379: decode attention of one query token against [S][H][D]
+ * caches, no mask; the row max starts at -1e9 as in the reference */
+void orc_attention_kv_cache(double* out, const double* q, const double* kc, const double* vc, size_t S, size_t H,
+                            size_t D) {
+    double scale = 1.0 / sqrt((double)D);
+    double* p = (double*)malloc(S * sizeof(double));
+    for (size_t h = 0; h < H; h++) {
+        double mx = -1e9, sum = 0.0;
+        for (size_t j = 0; j < S; j++) {
+            double s = 0.0;
+            for (size_t d = 0; d < D; d++) s += q[h * D + d] * kc[(j * H + h) * D + d];
+            p[j] = s * scale;
+            if (p[j] > mx) mx = p[j];
+        }
+        for (size_t j = 0; j < S; j++) { p[j] = exp(p[j] - mx); sum += p[j]; }
+        for (size_t d = 0; d < D; d++) {
+            double acc = 0.0;
+            for (size_t j = 0; j < S; j++) acc += p[j] / sum * vc[(j * H + h) * D + d];
+            out[h * D + d] = acc;
+        }
+    }
+    free(p);
+}
+
 /* lancius_kernels.c:248-272: rotary embedding on interleaved pairs, in place */
 void orc_rope(double* q, double* k, size_t B, size_t S, size_t H, size_t D, int pos_offset) {
     for (size_t b = 0; b < B; b++)

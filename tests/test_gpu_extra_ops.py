@@ -55,3 +55,40 @@ def test_rope_and_gqa_per_op(orc):
     orc.lib.orc_rope(dp(qr), dp(kr), C.c_size_t(B), C.c_size_t(S), C.c_size_t(H), C.c_size_t(D), C.c_int(3))
     assert_close(qd.cpu().numpy(), qr, 1e-5)
     assert_close(kd.cpu().numpy(), kr, 1e-5)
+
+
+@pytest.mark.parametrize("B,S,H,D", [(1, 1, 2, 64), (1, 37, 4, 64), (1, 5000, 8, 64), (3, 777, 2, 80),
+                                     (2, 1500, 4, 128), (1, 300, 2, 256), (1, 65, 3, 20)])
+def test_kv_cache_attention(orc, B, S, H, D):
+    """lcu_attention_kv_cache(_batched) against the oracle's restatement of
+    kernel_attention_kv_cache: single split (short caches) and split-KV merges."""
+    import ctypes as C
+    from lancius_b200 import data, load
+    lib = load()
+    q = data.normal(21, (B, H * D)); kc = data.normal(22, (B, S, H, D)); vc = data.normal(23, (B, S, H, D))
+    q, kc, vc = (a.astype(np.float32).astype(np.float64) for a in (q, kc, vc))
+    dev = [torch.tensor(a.astype(np.float32), device="cuda") for a in (q, kc, vc)]
+    out = torch.empty((B, H * D), device="cuda")
+    ptr = lambda t: C.c_void_p(t.data_ptr())
+    if B == 1:
+        assert lib.lcu_attention_kv_cache(ptr(out), ptr(dev[0]), ptr(dev[1]), ptr(dev[2]), S, H, D, None) == 0
+    else:
+        assert lib.lcu_attention_kv_cache_batched(ptr(out), ptr(dev[0]), ptr(dev[1]), ptr(dev[2]), B, S, H, D,
+                                                  None) == 0
+    torch.cuda.synchronize()
+    dp = lambda a: a.ctypes.data_as(C.POINTER(C.c_double))
+    want = np.empty((B, H * D))
+    for b in range(B):
+        row = np.empty(H * D)
+        qb, kb, vb = (np.ascontiguousarray(a[b]) for a in (q, kc, vc))
+        orc.lib.orc_attention_kv_cache(dp(row), dp(qb), dp(kb), dp(vb), C.c_size_t(S), C.c_size_t(H), C.c_size_t(D))
+        want[b] = row
+    assert_close(out.cpu().numpy(), want, 1e-4)
+
+
+def test_kv_cache_attention_rejects_large_head_dim():
+    import ctypes as C
+    from lancius_b200 import load
+    t = torch.zeros(4, device="cuda")
+    p = C.c_void_p(t.data_ptr())
+    assert load().lcu_attention_kv_cache(p, p, p, p, 1, 1, 512, None) != 0

@@ -45,3 +45,17 @@ def test_rope_known_values(orc):
     # position s rotates pair (0,1) by angle s (frequency 1)
     assert np.allclose(q[0, :, 0, 0], np.cos([0, 1, 2])) and np.allclose(q[0, :, 0, 1], np.sin([0, 1, 2]))
     assert np.allclose(k[0, :, 0, 0], -np.sin([0, 1, 2]))
+
+
+@pytest.mark.parametrize("S,H,D", [(1, 2, 16), (37, 4, 64), (300, 3, 80)])
+def test_kv_cache_attention_matches_reference(orc, ref, S, H, D):
+    """orc_attention_kv_cache against the reference's kernel_attention_kv_cache
+    (lancius_kernels.c:338-379) on the same FP64 inputs."""
+    import ctypes as C
+    from lancius_b200 import data
+    q = data.normal(11, (H * D,)); kc = data.normal(12, (S, H, D)); vc = data.normal(13, (S, H, D))
+    dp = lambda a: a.ctypes.data_as(C.POINTER(C.c_double))
+    mine = np.empty(H * D); theirs = np.empty(H * D)
+    orc.lib.orc_attention_kv_cache(dp(mine), dp(q), dp(kc), dp(vc), C.c_size_t(S), C.c_size_t(H), C.c_size_t(D))
+    ref.kernel_attention_kv_cache(dp(theirs), dp(q), dp(kc), dp(vc), C.c_size_t(S), C.c_size_t(H), C.c_size_t(D))
+    assert np.max(np.abs(mine - theirs)) <= 1e-12 * max(1.0, np.max(np.abs(theirs)))
