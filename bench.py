@@ -7,7 +7,7 @@ Q,K,V read + O written once, FP32 = 16*B*S*H*D per graph). Weak scaling: every
 rank runs its own batch of 8; there is no data-path collective.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                  [--config attention|mlp|conv|encoder|gemm4096|...]
+                  [--config attention|mlp|conv|encoder|encoder_b256|gemm4096|decode|...]
 """
 import argparse
 import ctypes as C
@@ -74,6 +74,8 @@ def metric_of(cfg, built, seconds_per_graph):
 
 
 def metric_names(cfg):
+    if cfg == "decode":
+        return ("decode attention GB/s", "GB/s", "kv_cache_decode_b{batch}_s{seq}_h{heads}_d{head_dim}_fp32".format(**DECODE))
     if cfg in METRIC:
         return METRIC[cfg]
     return ("GEMM TFLOP/s", "TFLOP/s", f"{cfg}_square_fp32")
@@ -356,6 +358,133 @@ def run_colsplit(args, rank, world, local_rank, n):
     dist.destroy_process_group()
 
 
+DECODE = dict(batch=32, seq=8192, heads=8, head_dim=128)
+
+
+def _decode_ref_seconds(ref, q, kc, vc, limit_s=8.0):
+    """Seconds per batch of the reference kernel_attention_kv_cache (FP64, one call per
+    sequence, sequences spread over all host threads); bounded sample of sequences."""
+    from concurrent.futures import ThreadPoolExecutor
+    B, S, H, D = kc.shape
+    dp = lambda a: a.ctypes.data_as(C.POINTER(C.c_double))
+    outs = [np.empty(H * D) for _ in range(B)]
+    cores = os.cpu_count()
+
+    def one(b):
+        ref.kernel_attention_kv_cache(dp(outs[b]), dp(q[b]), dp(kc[b]), dp(vc[b]), C.c_size_t(S), C.c_size_t(H),
+                                      C.c_size_t(D))
+    done, t0 = 0, time.perf_counter()
+    with ThreadPoolExecutor(cores) as ex:
+        while True:
+            list(ex.map(one, range(B)))
+            done += 1
+            if time.perf_counter() - t0 > limit_s:
+                break
+    return (time.perf_counter() - t0) / done, cores
+
+
+def run_decode(args, rank, world, local_rank):
+    """KV-cache decode attention (kernel_attention_kv_cache) per GPU: a batch of
+    sequences, one new query token each, against resident FP32 caches. Weak scaling."""
+    import torch
+    import lancius_b200 as L
+    from lancius_b200 import data
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    lib = L.load()
+    B, S, H, D = DECODE["batch"], DECODE["seq"], DECODE["heads"], DECODE["head_dim"]
+    g = torch.Generator(device="cuda").manual_seed(7 + rank)
+    kc = torch.randn((B, S, H, D), device="cuda", generator=g)
+    vc = torch.randn((B, S, H, D), device="cuda", generator=g)
+    q_h = data.normal(8 + rank, (B, H * D)).astype(np.float32)
+    q = torch.from_numpy(q_h).cuda()
+    out = torch.empty((B, H * D), device="cuda")
+    stream = torch.cuda.current_stream()
+    sp = C.c_void_p(stream.cuda_stream)
+    ptr = lambda t: C.c_void_p(t.data_ptr())
+    flush = torch.empty(L2_FLUSH_BYTES // 4, device="cuda")
+
+    def step():
+        rc = lib.lcu_attention_kv_cache_batched(ptr(out), ptr(q), ptr(kc), ptr(vc), B, S, H, D, sp)
+        assert rc == 0, rc
+    for _ in range(args.warmup):
+        flush.fill_(1.0); step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = Clocks(local_rank)
+    clocks.start()
+    evs = []
+    for _ in range(args.steps):
+        flush.fill_(1.0)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(); step(); e1.record()
+        evs.append((e0, e1))
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    dev_ms = [e0.elapsed_time(e1) for e0, e1 in evs]
+    total_ms = sum(dev_ms)
+    # e2e: the caches stay resident (they are the decoder's state); each step copies the
+    # new query tokens in from pinned memory and the attention output back
+    q_pin = torch.from_numpy(q_h).pin_memory()
+    o_pin = torch.empty((B, H * D)).pin_memory()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        q.copy_(q_pin, non_blocking=True)
+        step()
+        o_pin.copy_(out, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if dist:
+        t = torch.tensor([total_ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = t.tolist()
+    bytes_ = 4.0 * (2 * B * S * H * D + 2 * B * H * D)
+    if rank == 0:
+        sec = total_ms / 1e3 / args.steps
+        val = bytes_ / sec / 1e9 * world
+        pk = peaks()
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            import oracle
+            if oracle.reference_available():
+                ref = oracle.reference()
+                nb = 4   # bounded sample: 4 sequences at the full cache length
+                kd, vd = (t[:nb].double().cpu().numpy() for t in (kc, vc))
+                qd = q_h[:nb].astype(np.float64)
+                rsec, cores = _decode_ref_seconds(ref, qd, kd, vd)
+                cpu = {"value": round(4.0 * (2 * nb * S * H * D + 2 * nb * H * D) / rsec / 1e9, 4), "unit": "GB/s",
+                       "cores": cores, "kind": "reference",
+                       "sample": f"{nb} of {B} sequences (S{S} H{H} D{D}) through kernel_attention_kv_cache, "
+                                 "one call per sequence on a thread pool; FP32-equivalent bytes"}
+        line = {
+            "metric": "decode attention GB/s", "value": round(val, 3), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (N(0,1) caches, seeded)",
+            "config": {"workload": f"kv_cache_decode_b{B}_s{S}_h{H}_d{D}_fp32", "per_gpu_batch": B,
+                       "mode": "fp32", "l2": "flushed between timed steps (256 MiB write); caches 2.1 GB > L2",
+                       "parallelism": f"batch-sharded x{world}"},
+            "roofline": {"bound": "hbm", "achieved": round(bytes_ / sec / 1e9, 1), "peak": pk["hbm_gbs"],
+                         "unit": "GB/s", "frac": round(bytes_ / sec / 1e9 / pk["hbm_gbs"], 4), "traffic": None,
+                         "kernel": "k_decode_vec (split-KV) + k_decode_merge", "peak_src": pk["src"] + " hbm_gbs"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(bytes_ / (e2e_ms / 1e3 / args.steps) / 1e9 * world, 3), "unit": "GB/s",
+                    "h2d_bytes_per_step": int(q_h.nbytes), "d2h_bytes_per_step": int(4 * B * H * D)},
+            "gpu_launches": 2 * args.steps, "clocks": clk,
+            "step_ms_min_max": [round(min(dev_ms), 5), round(max(dev_ms), 5)],
+        }
+        print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+
+
 def _is_activation(cfg, node):
     # per-step inputs (weights stay resident): attention Q/K/V, conv/mlp/encoder X, gemm A and B
     return True if cfg in ("attention",) or cfg.startswith("gemm") else node.id == 0
@@ -385,6 +514,9 @@ def main():
 
     if args.config.startswith("gemm") and world > 1:
         run_colsplit(args, rank, world, local_rank, int(args.config[4:]))
+        return
+    if args.config == "decode":
+        run_decode(args, rank, world, local_rank)
         return
     built, total_ms, e2e_ms, dev_ms, launches, clk, in_b, out_b, dist = run_b200(args, rank, world, local_rank)
     if rank != 0:
@@ -440,8 +572,10 @@ def reference_arm(args, metric, unit, workload):
     from lancius_b200 import Graph, configs
     if not oracle.reference_available():
         return {"impl": "reference", "unavailable": "oracle/_ref/liblancius_ref.so was not built"}
+    if args.config == "decode":
+        return reference_arm_decode(args, metric, unit, workload)
     if args.config != "attention":
-        return {"impl": "reference", "unavailable": f"reference arm implemented for the attention workload only"}
+        return {"impl": "reference", "unavailable": f"reference arm implemented for the attention and decode workloads"}
     ref = oracle.reference()
     _all_host_threads()
     g = Graph(ref)
@@ -471,6 +605,35 @@ def reference_arm(args, metric, unit, workload):
                              "sample": "the full batch-8 graph per step on the host CPU, reference C sources "
                                        "compiled by oracle/Makefile; OpenMP threads = all host cores"},
             "e2e": {"value": round(val, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def reference_arm_decode(args, metric, unit, workload):
+    """kernel_attention_kv_cache (the reference's own FP64 C kernel) on the host cores,
+    each step a bounded sample of 4 of the batch's sequences scaled to the batch."""
+    import oracle
+    ref = oracle.reference()
+    B, S, H, D = DECODE["batch"], DECODE["seq"], DECODE["heads"], DECODE["head_dim"]
+    nb = 4
+    rng = np.random.default_rng(7)
+    kc, vc = rng.standard_normal((nb, S, H, D)), rng.standard_normal((nb, S, H, D))
+    q = rng.standard_normal((nb, H * D))
+    times = []
+    for i in range(args.warmup + args.steps):
+        sec, cores = _decode_ref_seconds(ref, q, kc, vc, limit_s=0.0)
+        if i >= args.warmup:
+            times.append(sec * B / nb)
+    sec = sum(times) / len(times)
+    val = 4.0 * (2 * B * S * H * D + 2 * B * H * D) / sec / 1e9
+    metric = "decode attention GB/s"
+    return {"impl": "reference", "metric": metric, "value": round(val, 4), "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (N(0,1) caches, seeded)",
+            "config": {"workload": workload, "per_gpu_batch": B, "executor": "kernel_attention_kv_cache per sequence"},
+            "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "kind": "reference", "cores": cores,
+                             "sample": f"{nb} of {B} sequences per step, scaled x{B // nb}; one call per sequence "
+                                       "on a thread pool of all host cores; FP32-equivalent bytes"},
+            "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 if __name__ == "__main__":

@@ -58,7 +58,7 @@ def test_rope_and_gqa_per_op(orc):
 
 
 @pytest.mark.parametrize("B,S,H,D", [(1, 1, 2, 64), (1, 37, 4, 64), (1, 5000, 8, 64), (3, 777, 2, 80),
-                                     (2, 1500, 4, 128), (1, 300, 2, 256), (1, 65, 3, 20)])
+                                     (2, 1500, 4, 128), (1, 300, 2, 256), (1, 65, 3, 20), (2, 3001, 3, 32)])
 def test_kv_cache_attention(orc, B, S, H, D):
     """lcu_attention_kv_cache(_batched) against the oracle's restatement of
     kernel_attention_kv_cache: single split (short caches) and split-KV merges."""
