@@ -359,6 +359,10 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                         st.out = O(n); st.in0 = O(n->inputs[0]); st.in1 = O(n->inputs[1]); st.dscale = n->inputs[1]->scale;
                         st.table_off = b.add_table(std::vector<float>(64, 0.f));     // one float of scratch (max |a|)
                         st.tc = 0;
+                        {   // tensor-core INT8 operands live in the context scratch
+                            size_t need = lcu_matmul_int8_scratch_bytes(st.M, st.K, st.N);
+                            if (need > c->scratch_bytes) c->scratch_bytes = need;
+                        }
                         if (ns.size() > 1) return fail(LANCIUS_ERROR_UNSUPPORTED_OP);
                         break;
                     }
@@ -432,6 +436,9 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                         // INT8 weights: dynamic quantisation of the input (vision_ops.c:16-57)
                         st.kind = S_MISC; st.lop = n->op; st.dscale = wt->scale;
                         st.table_off = b.add_table(std::vector<float>(64, 0.f));
+                        size_t need = lcu_conv2d_int8_scratch_bytes(st.cn, st.ci, st.h, st.w, st.co, st.kh, st.kw, st.stride,
+                                                                    st.pad);
+                        if (need > c->scratch_bytes) c->scratch_bytes = need;
                         break;
                     }
                     size_t ho = (st.h + 2 * st.pad - st.kh) / st.stride + 1, wo = (st.w + 2 * st.pad - st.kw) / st.stride + 1;
@@ -691,16 +698,16 @@ extern "C" void lcu_host_free(void* p) { if (p) cudaFreeHost(p); }
 // ---------------------------------------------------------------------------
 // execution
 
-static lancius_error run_misc(const Step& s, char* base, void* st) {
+static lancius_error run_misc(const Step& s, char* base, void* scratch, void* st) {
     auto F = [&](size_t off) { return reinterpret_cast<float*>(base + off); };
     switch (s.lop) {
         case LANCIUS_OP_MATMUL:
             return lcu_matmul_int8(F(s.out), F(s.in0), reinterpret_cast<const int8_t*>(base + s.in1), s.dscale, s.M, s.K, s.N,
-                                   F(s.table_off), st);
+                                   F(s.table_off), scratch, st);
         case LANCIUS_OP_CONV2D: case LANCIUS_OP_CONV2D_RELU_FUSED:
             return lcu_conv2d_int8(F(s.out), F(s.in0), reinterpret_cast<const int8_t*>(base + s.in1), s.dscale, s.cn, s.ci, s.h,
                                    s.w, s.co, s.kh, s.kw, s.stride, s.pad, s.lop == LANCIUS_OP_CONV2D_RELU_FUSED,
-                                   F(s.table_off), st);
+                                   F(s.table_off), scratch, st);
         case LANCIUS_OP_SUM: return lcu_sum(F(s.out), F(s.in0), s.n, st);
         case LANCIUS_OP_SUM_AXIS0: return lcu_sum_axis0(F(s.out), F(s.in0), s.rows, s.cols, st);
         case LANCIUS_OP_TRANSPOSE: return lcu_transpose(F(s.out), F(s.in0), s.rows, s.cols, st);
@@ -780,7 +787,7 @@ static lancius_error run_steps(lcu_ctx* c) {
                                s.relu, c->mode, st);
                 break;
             case S_MAXPOOL: e = lcu_maxpool2d(F(s.out), F(s.in0), s.cn, s.ci, s.h, s.w, s.kh, s.stride, st); break;
-            case S_MISC: e = run_misc(s, base, st); break;
+            case S_MISC: e = run_misc(s, base, c->scratch, st); break;
         }
         if (e != LANCIUS_ERROR_OK) return e;
     }

@@ -59,11 +59,23 @@ int lcu_attention_tc_supported(size_t D);
 int lcu_force_simt(void);
 lancius_error lcu_conv2d_tc(float* out, const float* in, const float* w, LcuConvShape cs, int relu, int mode, void* stream);
 void* lcu_scratch_acquire(size_t bytes);
+// INT8 weights: tensor cores (gemm_i8.cu) above lcu_int8_use_tc's size, CUDA cores below;
+// scratch = the *_scratch_bytes() of device memory, or NULL for a library buffer.
+int lcu_int8_use_tc(size_t M, size_t N, size_t K);
+size_t lcu_matmul_int8_scratch_bytes(size_t M, size_t K, size_t N);
+size_t lcu_conv2d_int8_scratch_bytes(size_t N, size_t Ci, size_t H, size_t W, size_t Co, size_t Kh, size_t Kw,
+                                     size_t stride, size_t pad);
 lancius_error lcu_matmul_int8(float* out, const float* a, const int8_t* b, double scale_b, size_t M, size_t K, size_t N,
-                              float* amax_scratch, void* s);
+                              float* amax_scratch, void* scratch, void* s);
 lancius_error lcu_conv2d_int8(float* out, const float* in, const int8_t* w, double scale_w, size_t N, size_t Ci, size_t H,
                               size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu,
-                              float* amax_scratch, void* s);
+                              float* amax_scratch, void* scratch, void* s);
+lancius_error lcu_matmul_int8_simt(float* out, const float* a, const int8_t* b, double scale_b, size_t M, size_t K,
+                                   size_t N, float* amax_scratch, void* s);
+lancius_error lcu_conv2d_int8_simt(float* out, const float* in, const int8_t* w, double scale_w, size_t N, size_t Ci,
+                                   size_t H, size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad,
+                                   int relu, float* amax_scratch, void* s);
+int lcu_int8_watchdog_read_and_clear(void);
 void* lcu_scratch_acquire_gather(size_t bytes);
 void* lcu_scratch_acquire_decode(size_t bytes);
 lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, const float* k, const float* v, float* o,

@@ -220,25 +220,23 @@ __global__ void k_absmax(float* out, const float* a, size_t n) {
         if (threadIdx.x == 0) out[0] = r;
     }
 }
-__device__ __forceinline__ int quant(float x, double inv_scale) {
-    return (int)(signed char)(int)round((double)x * inv_scale);     // round half away from zero, wraps like the C cast
+__device__ __forceinline__ int quant(float x, double scale) {
+    return (int)(signed char)(int)round((double)x / scale);         // round half away from zero, wraps like the C cast
 }
 // ... then int8 x int8 products summed in int32, times scale_a * scale_b
 __global__ void k_matmul_int8(float* out, const float* a, const int8_t* b, const float* amax, double scale_b, size_t M,
                               size_t K, size_t N) {
     const double sa = amax[0] > 0.f ? (double)amax[0] / 127.0 : 1e-8;
-    const double inv = 1.0 / sa;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < M * N; i += (size_t)gridDim.x * blockDim.x) {
         size_t r = i / N, c = i % N;
         int acc = 0;
-        for (size_t k = 0; k < K; k++) acc += quant(a[r * K + k], inv) * (int)b[k * N + c];
+        for (size_t k = 0; k < K; k++) acc += quant(a[r * K + k], sa) * (int)b[k * N + c];
         out[i] = (float)((double)acc * (sa * scale_b));
     }
 }
 __global__ void k_conv_int8(float* out, const float* in, const int8_t* w, const float* amax, double scale_w, int N, int Ci,
                             int H, int W, int Co, int Kh, int Kw, int stride, int pad, int Ho, int Wo, int relu) {
     const double sa = amax[0] > 0.f ? (double)amax[0] / 127.0 : 1e-8;
-    const double inv = 1.0 / sa;
     size_t n_el = (size_t)N * Co * Ho * Wo;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n_el; i += (size_t)gridDim.x * blockDim.x) {
         int wo = (int)(i % Wo), ho = (int)((i / Wo) % Ho), co = (int)((i / ((size_t)Wo * Ho)) % Co);
@@ -249,7 +247,7 @@ __global__ void k_conv_int8(float* out, const float* in, const int8_t* w, const 
                 for (int kw = 0; kw < Kw; kw++) {
                     int ih = ho * stride - pad + kh, iw = wo * stride - pad + kw;
                     if (ih < 0 || iw < 0 || ih >= H || iw >= W) continue;
-                    acc += quant(in[((n * Ci + ci) * H + ih) * (size_t)W + iw], inv) * (int)w[((co * Ci + ci) * Kh + kh) * Kw + kw];
+                    acc += quant(in[((n * Ci + ci) * H + ih) * (size_t)W + iw], sa) * (int)w[((co * Ci + ci) * Kh + kh) * Kw + kw];
                 }
         float v = (float)((double)acc * (sa * scale_w));
         out[i] = (relu && v < 0.f) ? 0.f : v;
@@ -350,7 +348,7 @@ lancius_error lcu_conv2d_bwd_w(float* out, const float* grad, const float* in, s
     return done();
 }
 // INT8 weights (dtype INT8 + per-tensor scale). amax_scratch: one float of device memory.
-lancius_error lcu_matmul_int8(float* out, const float* a, const int8_t* b, double scale_b, size_t M, size_t K, size_t N,
+lancius_error lcu_matmul_int8_simt(float* out, const float* a, const int8_t* b, double scale_b, size_t M, size_t K, size_t N,
                               float* amax_scratch, void* s) {
     if (!out || !a || !b || !amax_scratch) return nul();
     cudaStream_t st = lcu_as_stream(s);
@@ -359,7 +357,7 @@ lancius_error lcu_matmul_int8(float* out, const float* a, const int8_t* b, doubl
     k_matmul_int8<<<lcu_blocks(M * N, 256), 256, 0, st>>>(out, a, b, amax_scratch, scale_b, M, K, N);
     return done();
 }
-lancius_error lcu_conv2d_int8(float* out, const float* in, const int8_t* w, double scale_w, size_t N, size_t Ci, size_t H,
+lancius_error lcu_conv2d_int8_simt(float* out, const float* in, const int8_t* w, double scale_w, size_t N, size_t Ci, size_t H,
                               size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu,
                               float* amax_scratch, void* s) {
     if (!out || !in || !w || !amax_scratch) return nul();

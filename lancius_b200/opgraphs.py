@@ -59,3 +59,31 @@ def int8_matmul(g, seed=7, M=33, K=70, N=20):
     out = g.matmul(a, b)
     wq = np.round(data.uniform(seed + 1, (K, N), -127, 127)).astype(np.int8)
     return {a: data.normal(seed, (M, K))}, {b: (wq, 0.01)}, [out]
+
+
+def int8_conv(g, seed=9, N=2, Ci=3, HW=20, Co=8, k=3, stride=1, pad=1, relu=True):
+    """CONV2D (optionally ReLU-fused) with INT8 OIHW weights and a per-tensor scale:
+    the reference quantizes the FP activation on the fly (lancius_vision_ops.c:16-57)."""
+    x = g.input_4d(N, Ci, HW, HW)
+    w = g.input_4d(Co, Ci, k, k)
+    out = g.conv2d(x, w, stride, pad)
+    if relu:
+        out = g.relu(out)
+        g.optimize_fusion()            # CONV2D_RELU_FUSED, as the reference's optimizer emits it
+    wq = np.round(data.uniform(seed + 1, (Co, Ci, k, k), -127, 127)).astype(np.int8)
+    return {x: data.normal(seed, (N, Ci, HW, HW))}, {w: (wq, 0.02)}, [out]
+
+
+def int8_matmul_large(g):
+    """INT8 MATMUL big enough for the tensor-core path (2^24+ multiply-adds)."""
+    return int8_matmul(g, seed=17, M=300, K=520, N=390)
+
+
+def int8_conv_large(g):
+    """INT8 conv through the tensor-core implicit GEMM: K = 27 (re-pitched weights)."""
+    return int8_conv(g, seed=19, N=4, Ci=3, HW=64, Co=64, k=3, stride=1, pad=1, relu=False)
+
+
+def int8_conv_large_k144(g):
+    """INT8 conv, K = 144 (16-byte rows as they are), stride 2, ReLU."""
+    return int8_conv(g, seed=23, N=4, Ci=16, HW=64, Co=96, k=3, stride=2, pad=1, relu=True)

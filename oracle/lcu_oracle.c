@@ -315,6 +315,37 @@ void orc_matmul_int8(double* out, const double* a, const int8_t* b, double scale
         }
 }
 
+/* vision_ops.c:16-57 + lancius_kernels.c:176-210: the input quantised as in
+ * orc_matmul_int8 (per tensor, on first execution), int8 x int8 -> int32 direct conv
+ * (zero padding contributes nothing), result * scale_in * scale_w, then the fused ReLU */
+void orc_conv2d_int8(double* out, const double* in, const int8_t* w, double scale_w, size_t N, size_t Ci, size_t H,
+                     size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu) {
+    size_t E = N * Ci * H * W, Ho = (H + 2 * pad - Kh) / stride + 1, Wo = (W + 2 * pad - Kw) / stride + 1;
+    double mx = 0.0;
+    for (size_t i = 0; i < E; i++) { double v = fabs(in[i]); if (v > mx) mx = v; }
+    double sa = mx > 0.0 ? mx / 127.0 : 1e-8;
+    int8_t* q = (int8_t*)malloc(E ? E : 1);
+    for (size_t i = 0; i < E; i++) q[i] = (int8_t)round(in[i] / sa);
+    for (size_t n = 0; n < N; n++)
+        for (size_t co = 0; co < Co; co++)
+            for (size_t ho = 0; ho < Ho; ho++)
+                for (size_t wo = 0; wo < Wo; wo++) {
+                    int32_t acc = 0;
+                    for (size_t ci = 0; ci < Ci; ci++)
+                        for (size_t kh = 0; kh < Kh; kh++)
+                            for (size_t kw = 0; kw < Kw; kw++) {
+                                long ih = (long)(ho * stride) - (long)pad + (long)kh;
+                                long iw = (long)(wo * stride) - (long)pad + (long)kw;
+                                if (ih < 0 || iw < 0 || ih >= (long)H || iw >= (long)W) continue;
+                                acc += (int32_t)q[((n * Ci + ci) * H + ih) * W + iw] *
+                                       (int32_t)w[((co * Ci + ci) * Kh + kh) * Kw + kw];
+                            }
+                    double v = (double)acc * (sa * scale_w);
+                    out[((n * Co + co) * Ho + ho) * Wo + wo] = relu && v < 0.0 ? 0.0 : v;
+                }
+    free(q);
+}
+
 /* ---- arena-mode graph executor: src/runtime/lancius_scheduler.c:61-362 ----- */
 
 static size_t elems(const lancius_node* n) { return lancius_node_elements(n); }
@@ -409,6 +440,12 @@ static void run_node(const lancius_node* n, double* o, double** R) {
         break;
     case LANCIUS_OP_ATTENTION: orc_attention(o, a, b, c, n->shape[0], n->shape[1], n->shape[2], n->attr_val != 1.0); break;
     case LANCIUS_OP_CONV2D: case LANCIUS_OP_CONV2D_RELU_FUSED:                           /* vision_ops.c:60-81 */
+        if (i1->runtime_data_int8 && i1->dtype == LANCIUS_DTYPE_INT8) {
+            orc_conv2d_int8(o, a, i1->runtime_data_int8, i1->scale, i0->shape[0], i0->shape[1], i0->shape[2],
+                            i0->shape[3], i1->shape[0], i1->shape[2], i1->shape[3], n->stride, n->pad,
+                            n->op == LANCIUS_OP_CONV2D_RELU_FUSED);
+            break;
+        }
         orc_conv2d(o, a, b, i0->shape[0], i0->shape[1], i0->shape[2], i0->shape[3], i1->shape[0],
                    i1->shape[2], i1->shape[3], n->stride, n->pad, n->op == LANCIUS_OP_CONV2D_RELU_FUSED);
         break;

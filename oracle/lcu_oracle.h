@@ -24,6 +24,8 @@ void orc_sum_axis1(double* out, const double* in, size_t rows, size_t cols);
 void orc_swiglu(double* out, const double* gate, const double* up, size_t n);
 void orc_attention_kv_cache(double* out, const double* q, const double* kc, const double* vc, size_t S, size_t H,
                             size_t D);
+void orc_conv2d_int8(double* out, const double* in, const int8_t* w, double scale_w, size_t N, size_t Ci, size_t H,
+                     size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu);
 void orc_gqa(double* out, const double* q, const double* k, const double* v, size_t S, size_t Hq, size_t Hkv, size_t D);
 void orc_rope(double* q, double* k, size_t B, size_t S, size_t H, size_t D, int pos_offset);
 void orc_conv2d_bwd_in(double* out, const double* grad, const double* w, size_t N, size_t Ci, size_t H, size_t W,

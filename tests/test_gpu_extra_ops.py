@@ -21,7 +21,9 @@ def device():
     d.close()
 
 
-@pytest.mark.parametrize("build", [opgraphs.training_ops, opgraphs.llm_ops, opgraphs.int8_matmul])
+@pytest.mark.parametrize("build", [opgraphs.training_ops, opgraphs.llm_ops, opgraphs.int8_matmul,
+                                   opgraphs.int8_conv, opgraphs.int8_matmul_large, opgraphs.int8_conv_large,
+                                   opgraphs.int8_conv_large_k144])
 def test_extra_ops_on_gpu(device, orc, build):
     g = L.Graph()
     r = build(g)
@@ -36,9 +38,15 @@ def test_extra_ops_on_gpu(device, orc, build):
     device.bind(s)
     device.upload_bound_inputs()
     device.execute(s)
+    if "large" in build.__name__:   # absmax + quantise (+ transpose / re-pitch) + tcgen05 kind::i8 GEMM
+        assert device.last_launch_count >= 3
     want = orc.run_graph(g, outputs)
     for o in outputs:
-        assert_close(device.download(o), want[o.id], 1e-4)
+        got = device.download(o)
+        assert_close(got, want[o.id], 1e-4)
+        if build.__name__.startswith("int8"):
+            # integer accumulation is exact: the FP32 result is the reference's value rounded once
+            assert np.array_equal(np.asarray(got, np.float32), np.asarray(want[o.id], np.float32))
 
 
 def test_rope_and_gqa_per_op(orc):

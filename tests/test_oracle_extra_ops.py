@@ -28,7 +28,8 @@ def run_both(orc, ref, build):
     return outs
 
 
-@pytest.mark.parametrize("build", [opgraphs.training_ops, opgraphs.llm_ops, opgraphs.int8_matmul])
+@pytest.mark.parametrize("build", [opgraphs.training_ops, opgraphs.llm_ops, opgraphs.int8_matmul,
+                                   opgraphs.int8_conv])
 def test_extra_ops_match_reference(orc, ref, build):
     mine, theirs = run_both(orc, ref, build)
     for a, b in zip(mine[:-1], theirs[:-1]):
