@@ -485,6 +485,101 @@ def run_decode(args, rank, world, local_rank):
         dist.destroy_process_group()
 
 
+def run_int8_gemm(args, rank, world, local_rank, n):
+    """MATMUL with INT8 weights (the reference's mixed-precision path) at n x n x n through
+    the executor: per step max|A| + quantise A + transpose B + tcgen05 kind::i8 GEMM."""
+    import torch
+    import lancius_b200 as L
+    from lancius_b200 import data
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    dev = L.Device(local_rank)
+    g = L.Graph()
+    a = g.input(n, n)
+    b = g.input(n, n)
+    out = g.matmul(a, b)
+    a_h = data.uniform(data.sub_seed(4 + rank, 1), (n, n), -1.0, 1.0).astype(np.float32)
+    wq = np.round(data.uniform(data.sub_seed(4, 2), (n, n), -127, 127)).astype(np.int8)
+    g.bind(a, a_h.astype(np.float64))
+    g.bind_int8(b, wq, 0.01)
+    sched = g.schedule()
+    dev.set_graph_replay(True)
+    dev.bind(sched)
+    dev.upload_bound_inputs()
+    ext = torch.cuda.ExternalStream(dev.stream)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device="cuda")
+
+    def step(e0=None, e1=None):
+        with torch.cuda.stream(ext):
+            flush.fill_(1.0)
+            if e0: e0.record(ext)
+        dev.execute(sched)
+        if e1:
+            with torch.cuda.stream(ext):
+                e1.record(ext)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    clocks = Clocks(local_rank)
+    clocks.start()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for e0, e1 in evs:
+        step(e0, e1)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    dev_ms = [e0.elapsed_time(e1) for e0, e1 in evs]
+    total_ms = sum(dev_ms)
+    launches = dev.last_launch_count
+    # e2e: A in from pinned memory, C out, weights resident
+    pa = dev.lib.lcu_host_alloc(n * n * 4)
+    pc = dev.lib.lcu_host_alloc(n * n * 4)
+    np.ctypeslib.as_array(C.cast(pa, C.POINTER(C.c_float)), shape=(n * n,))[:] = a_h.ravel()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(ext)
+    for _ in range(args.steps):
+        dev.upload_ptr(a, pa, 2)
+        dev.execute(sched)
+        dev.download_ptr(out, pc, 2)
+    e1.record(ext)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    dev.lib.lcu_host_free(pa); dev.lib.lcu_host_free(pc)
+    if dist:
+        t = torch.tensor([total_ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms, e2e_ms = t.tolist()
+    if rank == 0:
+        ops = 2.0 * n ** 3
+        sec = total_ms / 1e3 / args.steps
+        val = ops / sec / 1e12 * world
+        pk = peaks()
+        line = {
+            "metric": "INT8 GEMM TOPS", "value": round(val, 2), "unit": "TOPS", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "s8 x s8 -> s32",
+            "data": "synthetic (A ~ U[-1,1), int8 weights ~ U[-127,127], seeded)",
+            "config": {"workload": f"int8_weight_matmul{n}", "mode": "dynamic per-tensor INT8 (reference semantics)",
+                       "l2": "flushed between timed steps (256 MiB write)", "parallelism": f"replicas x{world}"},
+            "roofline": {"bound": "tensor", "achieved": round(ops / sec / 1e12, 2), "peak": pk["bf16_tflops"] * 2,
+                         "unit": "TOPS", "frac": round(ops / sec / 1e12 / (pk["bf16_tflops"] * 2), 4), "traffic": None,
+                         "peak_src": pk["src"] + " bf16 x 2 (INT8 dense rate is twice BF16)"},
+            "cpu_baseline": None,
+            "e2e": {"value": round(ops / (e2e_ms / 1e3 / args.steps) / 1e12 * world, 2), "unit": "TOPS",
+                    "h2d_bytes_per_step": 4 * n * n, "d2h_bytes_per_step": 4 * n * n},
+            "gpu_launches": launches * args.steps, "clocks": clk,
+            "step_ms_min_max": [round(min(dev_ms), 4), round(max(dev_ms), 4)],
+        }
+        print(json.dumps(line))
+    if dist:
+        dist.destroy_process_group()
+
+
 def _is_activation(cfg, node):
     # per-step inputs (weights stay resident): attention Q/K/V, conv/mlp/encoder X, gemm A and B
     return True if cfg in ("attention",) or cfg.startswith("gemm") else node.id == 0
@@ -517,6 +612,9 @@ def main():
         return
     if args.config == "decode":
         run_decode(args, rank, world, local_rank)
+        return
+    if args.config.startswith("int8gemm"):
+        run_int8_gemm(args, rank, world, local_rank, int(args.config[8:]))
         return
     built, total_ms, e2e_ms, dev_ms, launches, clk, in_b, out_b, dist = run_b200(args, rank, world, local_rank)
     if rank != 0:

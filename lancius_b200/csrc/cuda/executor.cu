@@ -43,6 +43,7 @@ struct Step {
     size_t in2 = 0;            // third input (S_MISC)
     int lop = 0;               // lancius opcode (S_MISC); LANCIUS_OP_MATMUL / CONV2D* mean the INT8-weight forms
     double dscale = 1.0;       // INT8 weight scale
+    size_t packed_off = (size_t)-1;   // INT8 MATMUL: K-major copy of the weights in ctx->packed
     float eps = 1e-5f;
 };
 
@@ -70,6 +71,12 @@ struct lcu_ctx {
     size_t staging_elems = 0;
     void* scratch = nullptr;            // tensor-core GEMM hi/lo operand copies
     size_t scratch_bytes = 0;
+    // INT8 weights feeding a tensor-core MATMUL, kept K-major ([N][Kp]) and refreshed by
+    // every upload of the weight node
+    struct Pack { uint32_t node; size_t off, K, N, Kp; };
+    std::vector<Pack> packs;
+    int8_t* packed = nullptr;
+    size_t packed_bytes = 0;
     std::vector<LcuTcGemmPlan> tc_plans;
     std::vector<size_t> off;            // node id -> byte offset in dmem (NPOS: no storage)
     std::vector<Step> steps;
@@ -86,6 +93,8 @@ static void release_binding(lcu_ctx* c) {
     if (c->dmem) { cudaFree(c->dmem); c->dmem = nullptr; }
     if (c->staging) { cudaFree(c->staging); c->staging = nullptr; }
     if (c->scratch) { cudaFree(c->scratch); c->scratch = nullptr; }
+    if (c->packed) { cudaFree(c->packed); c->packed = nullptr; }
+    c->packs.clear(); c->packed_bytes = 0;
     c->dmem_bytes = 0; c->staging_elems = 0; c->scratch_bytes = 0;
     c->tc_plans.clear();
     c->off.clear(); c->steps.clear();
@@ -359,9 +368,18 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                         st.out = O(n); st.in0 = O(n->inputs[0]); st.in1 = O(n->inputs[1]); st.dscale = n->inputs[1]->scale;
                         st.table_off = b.add_table(std::vector<float>(64, 0.f));     // one float of scratch (max |a|)
                         st.tc = 0;
-                        {   // tensor-core INT8 operands live in the context scratch
-                            size_t need = lcu_matmul_int8_scratch_bytes(st.M, st.K, st.N);
+                        if (size_t need = lcu_matmul_int8_scratch_bytes(st.M, st.K, st.N)) {
+                            // tensor-core INT8: quantised A in the context scratch, weights pre-packed
                             if (need > c->scratch_bytes) c->scratch_bytes = need;
+                            const size_t Kp = (st.K + 15) & ~size_t(15);
+                            const uint32_t wid = n->inputs[1]->id;
+                            for (const auto& pk : c->packs)
+                                if (pk.node == wid) st.packed_off = pk.off;
+                            if (st.packed_off == (size_t)-1) {
+                                st.packed_off = c->packed_bytes;
+                                c->packs.push_back({wid, c->packed_bytes, st.K, st.N, Kp});
+                                c->packed_bytes += align_up(st.N * Kp, 256);
+                            }
                         }
                         if (ns.size() > 1) return fail(LANCIUS_ERROR_UNSUPPORTED_OP);
                         break;
@@ -609,6 +627,10 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
         ce = cudaMalloc(&c->scratch, c->scratch_bytes);
         if (ce != cudaSuccess) { cudaGetLastError(); release_binding(c); return fail(LANCIUS_ERROR_OOM); }
     }
+    if (c->packed_bytes) {
+        ce = cudaMalloc(&c->packed, c->packed_bytes);
+        if (ce != cudaSuccess) { cudaGetLastError(); release_binding(c); return fail(LANCIUS_ERROR_OOM); }
+    }
     ce = cudaMalloc(&c->staging, (max_io ? max_io : 1) * sizeof(double));
     if (ce != cudaSuccess) { cudaGetLastError(); release_binding(c); return fail(LANCIUS_ERROR_OOM); }
     c->staging_elems = max_io;
@@ -644,8 +666,17 @@ extern "C" lancius_error lcu_upload(lcu_ctx* c, const lancius_node* n, const voi
     cudaSetDevice(c->device);
     if (dt == LANCIUS_DTYPE_FP32)
         return cuda_fail(cudaMemcpyAsync(d, host, E * 4, cudaMemcpyHostToDevice, c->stream));
-    if (dt == LANCIUS_DTYPE_INT8)       // INT8 weights are stored as bytes in the node's slot
-        return cuda_fail(cudaMemcpyAsync(d, host, E, cudaMemcpyHostToDevice, c->stream));
+    if (dt == LANCIUS_DTYPE_INT8) {     // INT8 weights are stored as bytes in the node's slot
+        cudaError_t ce = cudaMemcpyAsync(d, host, E, cudaMemcpyHostToDevice, c->stream);
+        if (ce != cudaSuccess) return cuda_fail(ce);
+        for (const auto& pk : c->packs)     // and re-packed K-major for the tensor-core MATMULs
+            if (pk.node == n->id) {
+                lancius_error e = lcu_int8_pack_kmajor(c->packed + pk.off, reinterpret_cast<const int8_t*>(d), pk.K, pk.N,
+                                                       pk.Kp, c->stream);
+                if (e != LANCIUS_ERROR_OK) return e;
+            }
+        return LANCIUS_ERROR_OK;
+    }
     if (dt != LANCIUS_DTYPE_FP64) return fail(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
     if (E > c->staging_elems) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
     cudaError_t ce = cudaMemcpyAsync(c->staging, host, E * 8, cudaMemcpyHostToDevice, c->stream);
@@ -698,12 +729,12 @@ extern "C" void lcu_host_free(void* p) { if (p) cudaFreeHost(p); }
 // ---------------------------------------------------------------------------
 // execution
 
-static lancius_error run_misc(const Step& s, char* base, void* scratch, void* st) {
+static lancius_error run_misc(const Step& s, char* base, void* scratch, const int8_t* packed, void* st) {
     auto F = [&](size_t off) { return reinterpret_cast<float*>(base + off); };
     switch (s.lop) {
         case LANCIUS_OP_MATMUL:
             return lcu_matmul_int8(F(s.out), F(s.in0), reinterpret_cast<const int8_t*>(base + s.in1), s.dscale, s.M, s.K, s.N,
-                                   F(s.table_off), scratch, st);
+                                   s.packed_off == (size_t)-1 ? nullptr : packed + s.packed_off, F(s.table_off), scratch, st);
         case LANCIUS_OP_CONV2D: case LANCIUS_OP_CONV2D_RELU_FUSED:
             return lcu_conv2d_int8(F(s.out), F(s.in0), reinterpret_cast<const int8_t*>(base + s.in1), s.dscale, s.cn, s.ci, s.h,
                                    s.w, s.co, s.kh, s.kw, s.stride, s.pad, s.lop == LANCIUS_OP_CONV2D_RELU_FUSED,
@@ -787,7 +818,7 @@ static lancius_error run_steps(lcu_ctx* c) {
                                s.relu, c->mode, st);
                 break;
             case S_MAXPOOL: e = lcu_maxpool2d(F(s.out), F(s.in0), s.cn, s.ci, s.h, s.w, s.kh, s.stride, st); break;
-            case S_MISC: e = run_misc(s, base, c->scratch, st); break;
+            case S_MISC: e = run_misc(s, base, c->scratch, c->packed, st); break;
         }
         if (e != LANCIUS_ERROR_OK) return e;
     }

@@ -10,8 +10,8 @@
 //      CONV: the im2col matrix [N*Ho*Wo][Kp]); MATMUL weights [K][N] are transposed
 //      to [N][Kp], CONV weights [Co][K] are used as they are (or re-pitched)
 //   3. D[M][N] = A[M][Kp] . B[N][Kp]^T: TMA (128-byte swizzle) -> 4-stage ring ->
-//      tcgen05.mma kind::i8 (M=128, N=256, K=32 per instruction) into an int32 TMEM
-//      accumulator; warp 0 lane 0 loads, warp 1 lane 0 issues, all four warps run
+//      tcgen05.mma kind::i8 (M=128, N=256, K=32 per instruction) into two int32 TMEM
+//      accumulators (256 x 256 CTA tile: the B tile is read once for both row halves); warp 0 lane 0 loads, warp 1 lane 0 issues, all four warps run
 //      the epilogue (tcgen05.ld -> scale -> ReLU -> row-major or NCHW store).
 // Every mbarrier wait is bounded; a timeout sets the watchdog word and unwinds.
 #include "tc_common.cuh"
@@ -20,12 +20,12 @@
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 128, STAGES = 4, THREADS = 128;
-constexpr int A_TILE = BM * BK;                    // 16 KB
+constexpr int BM = 256, BN = 256, BK = 128, STAGES = 3, THREADS = 128;
+constexpr int A_TILE = BM * BK;                    // 32 KB (two 128-row halves)
 constexpr int B_TILE = BN * BK;                    // 32 KB
 constexpr int STAGE_BYTES = A_TILE + B_TILE;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
-constexpr uint32_t TMEM_COLS = BN;                 // one 128 x 256 int32 accumulator
+constexpr uint32_t TMEM_COLS = 2 * BN;             // two 128 x 256 int32 accumulators (rows 0-127, 128-255)
 
 __device__ int g_i8_watchdog = 0;
 
@@ -91,7 +91,7 @@ k_gemm_i8(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
             issued = kt + 1;
         }
     } else if (warp == 1 && lane == 0) {
-        constexpr uint32_t idesc = idesc_s8(BM, BN);
+        constexpr uint32_t idesc = idesc_s8(128, BN);
         bool ok = true;
         for (int kt = 0; kt < KT; kt++) {
             const int s = kt % STAGES;
@@ -99,9 +99,13 @@ k_gemm_i8(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
             tc::tc_fence_after();
             const uint32_t a = tc::smem_u32(tiles + s * STAGE_BYTES), b = a + A_TILE;
 #pragma unroll
-            for (int kk = 0; kk < BK / 32; kk++)   // 32 int8 = 32 bytes of K per instruction
-                mma_i8(tmem, tc::smem_desc(a + kk * 32, 16, 1024, tc::SWZ_128B),
-                       tc::smem_desc(b + kk * 32, 16, 1024, tc::SWZ_128B), idesc, (kt | kk) ? 1u : 0u);
+            for (int kk = 0; kk < BK / 32; kk++) {   // 32 int8 = 32 bytes of K per instruction
+                const uint64_t db = tc::smem_desc(b + kk * 32, 16, 1024, tc::SWZ_128B);
+#pragma unroll
+                for (int half = 0; half < 2; half++)   // both row halves share the B tile
+                    mma_i8(tmem + (uint32_t)half * BN, tc::smem_desc(a + half * (128 * BK) + kk * 32, 16, 1024, tc::SWZ_128B),
+                           db, idesc, (kt | kk) ? 1u : 0u);
+            }
             tc::mma_commit(&sm->empty[s]);
             sm->consumed = kt + 1;
         }
@@ -112,11 +116,12 @@ k_gemm_i8(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
     if (tc::mbar_wait(&sm->accum, 0, abort, &g_i8_watchdog, 3)) {
         tc::tc_fence_after();
         const double scale = act_scale(amax, scale_w);
-        const int row = m0 + 32 * warp + lane;
+        for (int half = 0; half < 2; half++)
         for (int c = 0; c < BN; c += 32) {
-            if (n0 + c >= N) break;                      // warp-uniform
+            const int row = m0 + half * 128 + 32 * warp + lane;
+            if (n0 + c >= N || m0 + half * 128 >= M) break;   // warp-uniform
             float v[32];
-            tc::tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)c, v);
+            tc::tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(half * BN + c), v);
             if (row >= M) continue;
 #pragma unroll
             for (int j = 0; j < 32; j++) {
@@ -152,30 +157,55 @@ k_gemm_i8(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
 // max |a| as float bits (non-negative floats order like their bit patterns)
 __global__ void k_absmax_bits(unsigned* out, const float* __restrict__ a, size_t n) {
     float m = 0.f;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
-        m = fmaxf(m, fabsf(a[i]));
+    const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nth = (size_t)gridDim.x * blockDim.x;
+    if ((reinterpret_cast<uintptr_t>(a) & 15) == 0) {
+        const float4* a4 = reinterpret_cast<const float4*>(a);
+        for (size_t i = tid; i < n / 4; i += nth) {
+            const float4 v = __ldg(a4 + i);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+        for (size_t i = n / 4 * 4 + tid; i < n; i += nth) m = fmaxf(m, fabsf(a[i]));
+    } else {
+        for (size_t i = tid; i < n; i += nth) m = fmaxf(m, fabsf(a[i]));
+    }
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
     if ((threadIdx.x & 31) == 0 && m > 0.f) atomicMax(out, __float_as_uint(m));
 }
 
-// (int8)round(x / scale_a) as the reference computes it (round half away from zero)
-__device__ __forceinline__ int8_t quant8(float x, const float* amax) {
+struct QScale { double sa, inv; };
+__device__ __forceinline__ QScale qscale(const float* amax) {
     const double sa = amax[0] > 0.f ? (double)amax[0] / 127.0 : 1e-8;
-    return (int8_t)(int)round((double)x / sa);
+    return {sa, 1.0 / sa};
+}
+// (int8)round(x / scale_a) exactly as the reference computes it (a double division,
+// round half away from zero). x * (1 / scale_a) is within a few ulp of the quotient,
+// which only matters next to a half-integer; there the division is redone.
+__device__ __forceinline__ int8_t quant8(float x, QScale q) {
+    double y = (double)x * q.inv;
+    const double f = fabs(y - trunc(y));
+    if (fabs(f - 0.5) < 1e-9) y = (double)x / q.sa;
+    return (int8_t)(int)round(y);
 }
 
 // a [M][K] fp32 -> [M][Kp] int8, zero padded; four bytes per thread
 __global__ void k_quant_rows(int8_t* __restrict__ dst, const float* __restrict__ a, const float* __restrict__ amax,
                              size_t M, size_t K, size_t Kp) {
+    const QScale q = qscale(amax);
     const size_t words = M * Kp / 4;
+    const bool vec = K % 4 == 0 && (reinterpret_cast<uintptr_t>(a) & 15) == 0;
     for (size_t w = blockIdx.x * (size_t)blockDim.x + threadIdx.x; w < words; w += (size_t)gridDim.x * blockDim.x) {
         const size_t m = (w * 4) / Kp, k0 = (w * 4) % Kp;
-        char4 q;
-        int8_t* qb = reinterpret_cast<int8_t*>(&q);
+        char4 r;
+        if (vec) {
+            float4 v = k0 < K ? __ldg(reinterpret_cast<const float4*>(a + m * K + k0)) : make_float4(0.f, 0.f, 0.f, 0.f);
+            r = make_char4(quant8(v.x, q), quant8(v.y, q), quant8(v.z, q), quant8(v.w, q));
+        } else {
+            int8_t* rb = reinterpret_cast<int8_t*>(&r);
 #pragma unroll
-        for (int t = 0; t < 4; t++) qb[t] = k0 + t < K ? quant8(a[m * K + k0 + t], amax) : (int8_t)0;
-        reinterpret_cast<char4*>(dst)[w] = q;
+            for (int t = 0; t < 4; t++) rb[t] = k0 + t < K ? quant8(a[m * K + k0 + t], q) : (int8_t)0;
+        }
+        reinterpret_cast<char4*>(dst)[w] = r;
     }
 }
 
@@ -183,6 +213,7 @@ __global__ void k_quant_rows(int8_t* __restrict__ dst, const float* __restrict__
 __global__ void k_im2col_q(int8_t* __restrict__ dst, const float* __restrict__ in, const float* __restrict__ amax,
                            LcuConvShape cs, size_t Kp) {
     const int K = cs.ci * cs.kh * cs.kw, hw = cs.ho * cs.wo;
+    const QScale qs = qscale(amax);
     const size_t words = (size_t)cs.n * hw * Kp / 4;
     for (size_t w = blockIdx.x * (size_t)blockDim.x + threadIdx.x; w < words; w += (size_t)gridDim.x * blockDim.x) {
         const size_t p = (w * 4) / Kp;
@@ -199,7 +230,7 @@ __global__ void k_im2col_q(int8_t* __restrict__ dst, const float* __restrict__ i
                 const int ih = ho * cs.stride - cs.pad + kh, iw = wo * cs.stride - cs.pad + kw;
                 // zero padding quantises to 0 (round(0 / scale) = 0)
                 if (ih >= 0 && iw >= 0 && ih < cs.h && iw < cs.w)
-                    v = quant8(in[(((size_t)n * cs.ci + ci) * cs.h + ih) * (size_t)cs.w + iw], amax);
+                    v = quant8(in[(((size_t)n * cs.ci + ci) * cs.h + ih) * (size_t)cs.w + iw], qs);
             }
             qb[t] = v;
         }
@@ -207,18 +238,32 @@ __global__ void k_im2col_q(int8_t* __restrict__ dst, const float* __restrict__ i
     }
 }
 
-// b [K][N] int8 -> [N][Kp] int8 (32 x 32 tiles through shared memory), zero padded
-__global__ void k_transpose_i8(int8_t* __restrict__ dst, const int8_t* __restrict__ b, size_t K, size_t N, size_t Kp) {
-    __shared__ int8_t t[32][33];
-    const size_t k0 = blockIdx.y * 32, n0 = blockIdx.x * 32;
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const size_t k = k0 + i, n = n0 + threadIdx.x;
-        t[i][threadIdx.x] = (k < K && n < N) ? b[k * N + n] : (int8_t)0;
+// b [K][N] int8 -> [N][Kp] int8, zero padded: 64 x 64 byte tiles through shared
+// memory, 4-byte words on both sides
+__global__ void __launch_bounds__(256) k_transpose_i8(int8_t* __restrict__ dst, const int8_t* __restrict__ b, size_t K,
+                                                      size_t N, size_t Kp) {
+    __shared__ int8_t t[64][68];
+    const size_t k0 = blockIdx.y * 64, n0 = blockIdx.x * 64;
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;     // 16 words x 16 rows per pass
+    const bool vec_in = N % 4 == 0 && (reinterpret_cast<uintptr_t>(b) & 3) == 0;
+    for (int i = ty; i < 64; i += 16) {
+        const size_t k = k0 + i, n = n0 + 4 * tx;
+        char4 v = make_char4(0, 0, 0, 0);
+        if (k < K) {
+            if (vec_in && n + 3 < N) v = *reinterpret_cast<const char4*>(b + k * N + n);
+            else {
+                int8_t* vb = reinterpret_cast<int8_t*>(&v);
+                for (int u = 0; u < 4; u++) vb[u] = n + u < N ? b[k * N + n + u] : (int8_t)0;
+            }
+        }
+        *reinterpret_cast<char4*>(&t[i][4 * tx]) = v;
     }
     __syncthreads();
-    for (int i = threadIdx.y; i < 32; i += blockDim.y) {
-        const size_t n = n0 + i, k = k0 + threadIdx.x;
-        if (n < N && k < Kp) dst[n * Kp + k] = t[threadIdx.x][i];
+    for (int i = ty; i < 64; i += 16) {
+        const size_t n = n0 + i, k = k0 + 4 * tx;
+        if (n >= N || k >= Kp) continue;
+        const char4 v = make_char4(t[4 * tx][i], t[4 * tx + 1][i], t[4 * tx + 2][i], t[4 * tx + 3][i]);
+        *reinterpret_cast<char4*>(dst + n * Kp + k) = v;   // Kp % 16 == 0: whole words stay in the row
     }
 }
 
@@ -335,8 +380,18 @@ size_t lcu_conv2d_int8_scratch_bytes(size_t N, size_t Ci, size_t H, size_t W, si
 // scratch: lcu_matmul_int8_scratch_bytes() bytes of device memory, or NULL for a
 // library-owned per-device buffer (then the call synchronises the stream before it
 // returns, so the buffer can be reused by the next call).
+// B [K][N] int8 -> K-major [N][Kp] rows (Kp = K rounded up to 16), the tensor-core
+// layout of the weights; the executor runs it when an INT8 weight is uploaded.
+lancius_error lcu_int8_pack_kmajor(int8_t* dst, const int8_t* b, size_t K, size_t N, size_t Kp, void* s) {
+    if (!K || !N) return LANCIUS_ERROR_OK;
+    k_transpose_i8<<<dim3((unsigned)((N + 63) / 64), (unsigned)((Kp + 63) / 64)), 256, 0, lcu_as_stream(s)>>>(dst, b, K, N,
+                                                                                                            Kp);
+    lcu_note_launch();
+    return lcu_launch_status();
+}
+
 lancius_error lcu_matmul_int8(float* out, const float* a, const int8_t* b, double scale_b, size_t M, size_t K, size_t N,
-                              float* amax_scratch, void* scratch, void* s) {
+                              const int8_t* b_packed, float* amax_scratch, void* scratch, void* s) {
     if (!out || !a || !b || !amax_scratch) { lancius_set_error(LANCIUS_ERROR_NULL_PTR); return LANCIUS_ERROR_NULL_PTR; }
     const size_t need = lcu_matmul_int8_scratch_bytes(M, K, N);
     if (!need) return lcu_matmul_int8_simt(out, a, b, scale_b, M, K, N, amax_scratch, s);
@@ -350,8 +405,8 @@ lancius_error lcu_matmul_int8(float* out, const float* a, const int8_t* b, doubl
     if (e != LANCIUS_ERROR_OK) return e;
     k_quant_rows<<<lcu_blocks(M * Kp / 4, 256, 148u * 16u), 256, 0, st>>>(a8, a, amax_scratch, M, K, Kp);
     lcu_note_launch();
-    k_transpose_i8<<<dim3((unsigned)((N + 31) / 32), (unsigned)((Kp + 31) / 32)), dim3(32, 8), 0, st>>>(b8, b, K, N, Kp);
-    lcu_note_launch();
+    if (b_packed) b8 = const_cast<int8_t*>(b_packed);
+    else if ((e = lcu_int8_pack_kmajor(b8, b, K, N, Kp, s)) != LANCIUS_ERROR_OK) return e;
     if ((e = lcu_launch_status()) != LANCIUS_ERROR_OK) return e;
     e = run_gemm(a8, b8, out, amax_scratch, scale_b, M, N, Kp, 0, 0, st);
     if (e == LANCIUS_ERROR_OK && own) e = lcu_check_cuda(cudaStreamSynchronize(st));

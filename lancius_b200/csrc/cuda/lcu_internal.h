@@ -65,8 +65,10 @@ int lcu_int8_use_tc(size_t M, size_t N, size_t K);
 size_t lcu_matmul_int8_scratch_bytes(size_t M, size_t K, size_t N);
 size_t lcu_conv2d_int8_scratch_bytes(size_t N, size_t Ci, size_t H, size_t W, size_t Co, size_t Kh, size_t Kw,
                                      size_t stride, size_t pad);
+// b_packed: the weights already K-major ([N][Kp], lcu_int8_pack_kmajor), or NULL
 lancius_error lcu_matmul_int8(float* out, const float* a, const int8_t* b, double scale_b, size_t M, size_t K, size_t N,
-                              float* amax_scratch, void* scratch, void* s);
+                              const int8_t* b_packed, float* amax_scratch, void* scratch, void* s);
+lancius_error lcu_int8_pack_kmajor(int8_t* dst, const int8_t* b, size_t K, size_t N, size_t Kp, void* s);
 lancius_error lcu_conv2d_int8(float* out, const float* in, const int8_t* w, double scale_w, size_t N, size_t Ci, size_t H,
                               size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu,
                               float* amax_scratch, void* scratch, void* s);

@@ -100,3 +100,29 @@ def test_kv_cache_attention_rejects_large_head_dim():
     t = torch.zeros(4, device="cuda")
     p = C.c_void_p(t.data_ptr())
     assert load().lcu_attention_kv_cache(p, p, p, p, 1, 1, 512, None) != 0
+
+
+def test_int8_weights_repacked_on_upload(device, orc):
+    """The tensor-core INT8 MATMUL reads a K-major copy of the weights made at upload
+    time: uploading new weights must change the next result."""
+    from lancius_b200 import data
+    g = L.Graph()
+    inputs, int8s, outputs = opgraphs.int8_matmul_large(g)
+    for n, arr in inputs.items():
+        g.bind(n, np.asarray(arr, np.float32).astype(np.float64))
+    (wnode, (wq, scale)), = int8s.items()
+    g.bind_int8(wnode, wq, scale)
+    s = g.schedule()
+    device.set_graph_replay(True)
+    device.bind(s)
+    device.upload_bound_inputs()
+    device.execute(s)
+    first = device.download(outputs[0])
+    wq2 = np.round(data.uniform(99, wq.shape, -127, 127)).astype(np.int8)
+    g.bind_int8(wnode, wq2, scale)
+    device.upload_bound_inputs()
+    device.execute(s)                      # replays the captured graph
+    second = device.download(outputs[0])
+    want = orc.run_graph(g, outputs)[outputs[0].id]
+    assert not np.array_equal(first, second)
+    assert np.array_equal(np.asarray(second, np.float32), np.asarray(want, np.float32))
