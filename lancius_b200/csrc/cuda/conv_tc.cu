@@ -1,0 +1,341 @@
+// Implicit-GEMM CONV2D on the tcgen05 tensor cores without a materialised im2col
+// (FP32-exact, 3xTF32). Restates kernel_conv2d_fwd (lancius_kernels.c:28-60): NCHW
+// input, OIHW weights, zero padding, stride, optional fused ReLU
+// (lancius_vision_ops.c:60-81).
+//
+//   C[Co][P] = W'[Co][K'] . X'[P][K']^T,  P = N*Ho*Wo,  K' = (kh, kw, ci)
+//
+// The input is rewritten once as NHWC TF32 hi/lo copies (one pass over it, instead
+// of the Kh*Kw-times larger im2col). For one k-step (kh, kw, 16 channels) the B tile
+// of r whole output rows (r * Wo <= 256 pixels of one image) is ONE 4-D TMA load at
+// (c, kw - pad, ho0*s - pad + kh, n) with both spatial traversal strides set to the
+// conv stride, so the hardware performs the gather and the padding (out-of-range
+// coordinates read zeros); pixels land as 64-byte K-major rows in the 64-byte swizzle.
+// Weights are rewritten as [Co][kh][kw][ci] hi/lo and loaded as 2-D tiles.
+//
+//   warp 0      TMA producer (one lane)
+//   warp 1      TMEM allocation + tcgen05.mma issue (one lane)
+//   warps 2-5   epilogue: tcgen05.ld -> ReLU -> NCHW store
+// Tile 256 (two M=128 TMEM accumulators) x r*Wo pixels x 16 channels, 3 stages.
+// Requirements (else the im2col path runs): Ci % 16 == 0, Wo * stride <= 256, some
+// r with r * Wo % 16 == 0, K' <= 8192.
+// Every mbarrier wait is bounded; a timeout sets the watchdog word and unwinds.
+#include "tc_common.cuh"
+#include <mutex>
+
+namespace {
+
+constexpr int BM = 256, BN = 256, BK = 16, STAGES = 3, THREADS = 192;
+constexpr int A_TILE = BM * BK * 4;                  // 16 KB (two 128-row halves)
+constexpr int B_TILE = BN * BK * 4;                  // 16 KB
+constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE; // hi + lo of both
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr uint32_t TMEM_COLS = 512;
+
+__device__ int g_conv_watchdog = 0;
+
+struct Smem {
+    uint64_t full[STAGES], empty[STAGES], accum, drain;
+    uint32_t tmem;
+    int abort, consumed;
+};
+
+struct ConvArgs {
+    int n, ci, co, kh, kw, stride, pad, ho, wo;
+    int rows;        // output rows per tile: the tile is rows x Wo pixels of one image
+    int halves;      // 1 when Co <= 128
+    int passes, relu;
+};
+
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5, %6}], [%2];"
+        ::"r"(tc::smem_u32(dst)), "l"(reinterpret_cast<uint64_t>(map)), "r"(tc::smem_u32(bar)), "r"(c0), "r"(c1),
+          "r"(c2), "r"(c3)
+        : "memory");
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+k_conv_tc(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap tw_lo,
+          const __grid_constant__ CUtensorMap tx_hi, const __grid_constant__ CUtensorMap tx_lo, float* __restrict__ out,
+          ConvArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Smem* sm = reinterpret_cast<Smem*>(tiles + STAGES * STAGE_BYTES);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hw = a.ho * a.wo;
+    const int tiles_per_img = (a.ho + a.rows - 1) / a.rows;
+    const int img = blockIdx.x / tiles_per_img, ho0 = (blockIdx.x % tiles_per_img) * a.rows;
+    const int bn = a.rows * a.wo;                    // pixels (MMA N) of this tile
+    const int m0 = blockIdx.y * BM;
+    const int CB = a.ci / BK, KT = a.kh * a.kw * CB;
+    volatile int* abort = &sm->abort;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; s++) { tc::mbar_init(&sm->full[s], 1); tc::mbar_init(&sm->empty[s], 1); }
+        tc::mbar_init(&sm->accum, 1);
+        tc::mbar_init(&sm->drain, 1);
+        sm->abort = 0;
+        sm->consumed = 0;
+        tc::fence_barrier_init();
+        tc::prefetch_tmap(&tw_hi); tc::prefetch_tmap(&tx_hi);
+        if (a.passes > 1) { tc::prefetch_tmap(&tw_lo); tc::prefetch_tmap(&tx_lo); }
+    }
+    if (warp == 1) tc::tmem_alloc(&sm->tmem, TMEM_COLS);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = sm->tmem;
+    int issued = 0;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer ----------------
+        // a box counts all of its bytes, the zero-filled out-of-range part included
+        const uint32_t tx = (a.passes > 1 ? 2u : 1u) * (uint32_t)(A_TILE + bn * BK * 4);
+        for (int kt = 0; kt < KT; kt++) {
+            const int s = kt % STAGES;
+            if (kt >= STAGES && !tc::mbar_wait(&sm->empty[s], ((kt / STAGES) - 1) & 1, abort, &g_conv_watchdog, 1)) break;
+            const int cb = kt % CB, r = kt / CB, kw = r % a.kw, kh = r / a.kw;
+            uint8_t* st = tiles + s * STAGE_BYTES;
+            tc::mbar_expect_tx(&sm->full[s], tx);
+            tc::tma_load_3d(st, &tw_hi, &sm->full[s], kt * BK, m0, 0);
+            if (a.passes > 1) tc::tma_load_3d(st + A_TILE, &tw_lo, &sm->full[s], kt * BK, m0, 0);
+            // one box: rows x Wo output pixels, both spatial traversals at the conv stride
+            const int ix = -a.pad + kw, iy = ho0 * a.stride - a.pad + kh;
+            uint8_t* dst = st + 2 * A_TILE;
+            tma_load_4d(dst, &tx_hi, &sm->full[s], cb * BK, ix, iy, img);
+            if (a.passes > 1) tma_load_4d(dst + B_TILE, &tx_lo, &sm->full[s], cb * BK, ix, iy, img);
+            issued = kt + 1;
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer ----------------
+        const uint32_t idesc = tc::idesc_tf32(128, bn, false, false);
+        bool ok = true;
+        for (int kt = 0; kt < KT; kt++) {
+            const int s = kt % STAGES;
+            if (!tc::mbar_wait(&sm->full[s], (kt / STAGES) & 1, abort, &g_conv_watchdog, 2)) { ok = false; break; }
+            tc::tc_fence_after();
+            const uint32_t st = tc::smem_u32(tiles + s * STAGE_BYTES);
+            const uint32_t a_hi = st, a_lo = st + A_TILE, b_hi = st + 2 * A_TILE, b_lo = b_hi + B_TILE;
+#pragma unroll
+            for (int kb = 0; kb < BK / 8; kb++) {
+                const uint64_t dbh = tc::smem_desc(b_hi + kb * 32, 16, 512, tc::SWZ_64B);
+                const uint64_t dbl = tc::smem_desc(b_lo + kb * 32, 16, 512, tc::SWZ_64B);
+                for (int half = 0; half < a.halves; half++) {
+                    const uint32_t hoff = (uint32_t)half * (128 * BK * 4), d = tmem + (uint32_t)half * BN;
+                    const uint64_t dah = tc::smem_desc(a_hi + hoff + kb * 32, 16, 512, tc::SWZ_64B);
+                    const uint32_t acc = (kt | kb) ? 1u : 0u;
+                    if (a.passes > 1) {
+                        const uint64_t dal = tc::smem_desc(a_lo + hoff + kb * 32, 16, 512, tc::SWZ_64B);
+                        tc::mma_tf32(d, dal, dbh, idesc, acc);      // small terms first
+                        tc::mma_tf32(d, dah, dbl, idesc, 1u);
+                        tc::mma_tf32(d, dah, dbh, idesc, 1u);
+                    } else {
+                        tc::mma_tf32(d, dah, dbh, idesc, acc);
+                    }
+                }
+            }
+            tc::mma_commit(&sm->empty[s]);
+            sm->consumed = kt + 1;
+        }
+        if (ok) tc::mma_commit(&sm->accum);
+    } else if (warp >= 2) {
+        // ---------------- epilogue: rows = output channels, columns = pixels ----------------
+        if (tc::mbar_wait(&sm->accum, 0, abort, &g_conv_watchdog, 3)) {
+            tc::tc_fence_after();
+            const int q = warp & 3;
+            for (int half = 0; half < a.halves; half++) {
+                const int co = m0 + half * 128 + 32 * q + lane;
+                // the tile's pixels are consecutive in the image: rows ho0.. of width Wo
+                const int valid = min(bn, (a.ho - ho0) * a.wo);
+                float* orow = out + ((size_t)img * a.co + co) * hw + (size_t)ho0 * a.wo;
+                const bool vec = (reinterpret_cast<uintptr_t>(orow) & 15) == 0;
+                for (int c = 0; c < bn; c += 32) {
+                    float v[32];
+                    tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * BN + c), v);
+                    if (co >= a.co) continue;
+                    if (a.relu) {
+#pragma unroll
+                        for (int j = 0; j < 32; j++) v[j] = v[j] > 0.f ? v[j] : 0.f;
+                    }
+                    if (vec && c + 32 <= valid) {
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(orow + c + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    } else {
+                        for (int j = 0; j < 32 && c + j < valid; j++) orow[c + j] = v[j];
+                    }
+                }
+            }
+        }
+    }
+
+    tc::tc_fence_before();
+    __syncthreads();
+    if (sm->abort) {
+        int never = 0;
+        if (warp == 0 && lane == 0)
+            for (int kt = sm->consumed; kt < issued; kt++)
+                if (!tc::mbar_wait(&sm->full[kt % STAGES], (kt / STAGES) & 1, &never, nullptr, 0)) break;
+        if (warp == 1 && lane == 0) {
+            tc::mma_commit(&sm->drain);
+            tc::mbar_wait(&sm->drain, 0, &never, nullptr, 0);
+        }
+        __syncthreads();
+    }
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// NCHW -> NHWC TF32 hi / lo (lo = 0 pointer: TF32 mode), 32 x 32 (c, w) tiles per (n, h)
+__global__ void k_nhwc_split(const float* __restrict__ in, float* __restrict__ hi, float* __restrict__ lo, int C, int H,
+                             int W) {
+    __shared__ float t[32][33];
+    const int nh = blockIdx.z, n = nh / H, h = nh % H;
+    const int c0 = blockIdx.y * 32, w0 = blockIdx.x * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;      // 32 x 8
+    for (int i = ty; i < 32; i += 8) {
+        const int c = c0 + i, w = w0 + tx;
+        t[i][tx] = (c < C && w < W) ? __ldg(in + (((size_t)n * C + c) * H + h) * W + w) : 0.f;
+    }
+    __syncthreads();
+    for (int i = ty; i < 32; i += 8) {
+        const int w = w0 + i, c = c0 + tx;
+        if (w >= W || c >= C) continue;
+        const float x = t[tx][i], xh = tc::tf32_rna(x);
+        const size_t o = (((size_t)n * H + h) * W + w) * C + c;
+        hi[o] = xh;
+        if (lo) lo[o] = tc::tf32_rna(x - xh);
+    }
+}
+
+// OIHW -> [Co][Kh][Kw][Ci] TF32 hi / lo
+__global__ void k_weight_khwc_split(const float* __restrict__ w, float* __restrict__ hi, float* __restrict__ lo, int Co,
+                                    int Ci, int Kh, int Kw) {
+    const size_t n = (size_t)Co * Ci * Kh * Kw;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+        const int ci = (int)(i % Ci);
+        size_t r = i / Ci;
+        const int kw = (int)(r % Kw); r /= Kw;
+        const int kh = (int)(r % Kh);
+        const int co = (int)(r / Kh);
+        const float x = w[(((size_t)co * Ci + ci) * Kh + kh) * Kw + kw], xh = tc::tf32_rna(x);
+        hi[i] = xh;
+        if (lo) lo[i] = tc::tf32_rna(x - xh);
+    }
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    });
+    return fn;
+}
+
+size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
+
+// output rows per tile: the most rows r with r * Wo <= 256 and r * Wo % 16 == 0 (the
+// MMA's N), the box spans (r - 1) * stride + 1 input rows of at most 256; 0 if none
+int pick_rows(int wo, int ho, int stride) {
+    if (wo <= 0 || wo * stride > 256) return 0;
+    for (int r = BN / wo; r >= 1; r--)
+        if ((r * wo) % 16 == 0 && r * stride <= 256 && r <= ho) return r;
+    return 0;
+}
+
+bool configure() {
+    static bool done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && done[dev]) return true;
+    if (cudaFuncSetAttribute(k_conv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+        return false;
+    if (dev >= 0 && dev < 64) done[dev] = true;
+    return true;
+}
+
+}  // namespace
+
+extern "C" int lcu_conv_nhwc_supported(LcuConvShape cs) {
+    return cs.ci % BK == 0 && cs.ci > 0 && cs.stride >= 1 && cs.stride <= 8 && pick_rows(cs.wo, cs.ho, cs.stride) &&
+           cs.kh * cs.kw * cs.ci <= 8192 && (size_t)cs.n * cs.ho * cs.wo < (1u << 31);
+}
+
+extern "C" size_t lcu_conv_nhwc_scratch_bytes(LcuConvShape cs, int passes) {
+    const size_t x = (size_t)cs.n * cs.h * cs.w * cs.ci * 4, w = (size_t)cs.co * cs.ci * cs.kh * cs.kw * 4;
+    return (passes > 1 ? 2 : 1) * (al256(x) + al256(w));
+}
+
+extern "C" lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const float* w, LcuConvShape cs, int relu,
+                                            int mode, void* scratch, void* stream) {
+    const int passes = mode == LCU_MODE_TF32 ? 1 : 3;
+    if (!lcu_conv_nhwc_supported(cs) || !scratch) { lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP; }
+    cudaStream_t st = lcu_as_stream(stream);
+    const size_t xe = (size_t)cs.n * cs.h * cs.w * cs.ci, K = (size_t)cs.ci * cs.kh * cs.kw, we = (size_t)cs.co * K;
+    char* s = static_cast<char*>(scratch);
+    float* xh = reinterpret_cast<float*>(s); s += al256(xe * 4);
+    float* xl = passes > 1 ? reinterpret_cast<float*>(s) : nullptr; if (passes > 1) s += al256(xe * 4);
+    float* wh = reinterpret_cast<float*>(s); s += al256(we * 4);
+    float* wl = passes > 1 ? reinterpret_cast<float*>(s) : nullptr;
+
+    k_nhwc_split<<<dim3((unsigned)((cs.w + 31) / 32), (unsigned)((cs.ci + 31) / 32), (unsigned)(cs.n * cs.h)), 256, 0, st>>>(
+        in, xh, xl, cs.ci, cs.h, cs.w);
+    lcu_note_launch();
+    k_weight_khwc_split<<<lcu_blocks(we, 256), 256, 0, st>>>(w, wh, wl, cs.co, cs.ci, cs.kh, cs.kw);
+    lcu_note_launch();
+    lancius_error e = lcu_launch_status();
+    if (e != LANCIUS_ERROR_OK) return e;
+
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || !configure()) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    const int rows = pick_rows(cs.wo, cs.ho, cs.stride);
+    CUtensorMap mw_hi, mw_lo, mx_hi, mx_lo;
+    bool ok = true;
+    {   // weights: [1][Co][K] rows of K floats, box {16, 256}
+        cuuint64_t dims[3] = {K, (cuuint64_t)cs.co, 1};
+        cuuint64_t strides[2] = {K * 4, we * 4};
+        cuuint32_t box[3] = {BK, BM, 1}, es[3] = {1, 1, 1};
+        ok = ok && fn(&mw_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, wh, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        if (passes > 1)
+            ok = ok && fn(&mw_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, wl, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        else mw_lo = mw_hi;
+    }
+    {   // input NHWC: dims {C, W, H, N}; box {16 channels, Wo x rows pixels at the conv stride, 1 image}
+        cuuint64_t dims[4] = {(cuuint64_t)cs.ci, (cuuint64_t)cs.w, (cuuint64_t)cs.h, (cuuint64_t)cs.n};
+        cuuint64_t strides[3] = {(cuuint64_t)cs.ci * 4, (cuuint64_t)cs.w * cs.ci * 4, (cuuint64_t)cs.h * cs.w * cs.ci * 4};
+        cuuint32_t box[4] = {BK, (cuuint32_t)(cs.wo * cs.stride), (cuuint32_t)(rows * cs.stride), 1};
+        cuuint32_t es[4] = {1, (cuuint32_t)cs.stride, (cuuint32_t)cs.stride, 1};
+        ok = ok && fn(&mx_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xh, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        if (passes > 1)
+            ok = ok && fn(&mx_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xl, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        else mx_lo = mx_hi;
+    }
+    if (!ok) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    ConvArgs a{cs.n, cs.ci, cs.co, cs.kh, cs.kw, cs.stride, cs.pad, cs.ho, cs.wo, rows, cs.co > 128 ? 2 : 1, passes, relu};
+    dim3 grid((unsigned)(cs.n * ((cs.ho + rows - 1) / rows)), (unsigned)((cs.co + BM - 1) / BM));
+    k_conv_tc<<<grid, THREADS, SMEM_BYTES, st>>>(mw_hi, mw_lo, mx_hi, mx_lo, out, a);
+    lcu_note_launch();
+    return lcu_launch_status();
+}
+
+extern "C" int lcu_conv_watchdog_read_and_clear(void) {
+    int v = 0, z = 0;
+    cudaMemcpyFromSymbol(&v, g_conv_watchdog, sizeof(int));
+    if (v) cudaMemcpyToSymbol(g_conv_watchdog, &z, sizeof(int));
+    return v;
+}

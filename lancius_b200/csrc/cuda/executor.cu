@@ -464,6 +464,10 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                     st.tc = st.cn && st.ci && lcu_use_tensor_cores(st.M, st.N, st.K);
                     if (st.tc) {
                         size_t need = lcu_gemm_tc_scratch_bytes(st.M, st.N, st.K, 1, 1, 1, 3);
+                        const LcuConvShape cs{(int)st.cn, (int)st.ci, (int)st.h, (int)st.w, (int)st.co, (int)st.kh,
+                                              (int)st.kw, (int)st.stride, (int)st.pad, (int)ho, (int)wo};
+                        if (lcu_conv_nhwc_supported(cs) && lcu_conv_nhwc_scratch_bytes(cs, 3) > need)
+                            need = lcu_conv_nhwc_scratch_bytes(cs, 3);
                         if (need > c->scratch_bytes) c->scratch_bytes = need;
                         st.plan_idx = (int)c->tc_plans.size();
                         c->tc_plans.push_back(LcuTcGemmPlan());
@@ -802,6 +806,13 @@ static lancius_error run_steps(lcu_ctx* c) {
             case S_BCAST: e = lcu_broadcast(F(s.out), F(s.in0), s.in_elems, s.rows, s.cols, st); break;
             case S_CONV:
                 if (s.tc) {
+                    const size_t ho = (s.h + 2 * s.pad - s.kh) / s.stride + 1, wo = (s.w + 2 * s.pad - s.kw) / s.stride + 1;
+                    const LcuConvShape cs{(int)s.cn, (int)s.ci, (int)s.h, (int)s.w, (int)s.co, (int)s.kh, (int)s.kw,
+                                          (int)s.stride, (int)s.pad, (int)ho, (int)wo};
+                    if (lcu_conv_nhwc_supported(cs) && !lcu_conv_force_im2col()) {
+                        e = lcu_conv2d_tc_nhwc(F(s.out), F(s.in0), F(s.in1), cs, s.relu, c->mode, c->scratch, st);
+                        break;
+                    }
                     LcuTcGemmPlan& p = c->tc_plans[s.plan_idx];
                     int passes = c->mode == LCU_MODE_TF32 ? 1 : 3;
                     if (p.passes != passes || p.M != s.M) {

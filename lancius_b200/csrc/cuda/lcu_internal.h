@@ -58,6 +58,14 @@ int lcu_use_tensor_cores(size_t M, size_t N, size_t K);
 int lcu_attention_tc_supported(size_t D);
 int lcu_force_simt(void);
 lancius_error lcu_conv2d_tc(float* out, const float* in, const float* w, LcuConvShape cs, int relu, int mode, void* stream);
+// direct implicit-GEMM conv over NHWC hi/lo copies (conv_tc.cu); scratch of
+// lcu_conv_nhwc_scratch_bytes(cs, passes) bytes
+int lcu_conv_nhwc_supported(LcuConvShape cs);
+size_t lcu_conv_nhwc_scratch_bytes(LcuConvShape cs, int passes);
+lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const float* w, LcuConvShape cs, int relu, int mode,
+                                 void* scratch, void* stream);
+int lcu_conv_force_im2col(void);   // LCU_CONV_IM2COL=1: keep the materialised-im2col conv
+int lcu_conv_watchdog_read_and_clear(void);
 void* lcu_scratch_acquire(size_t bytes);
 // INT8 weights: tensor cores (gemm_i8.cu) above lcu_int8_use_tc's size, CUDA cores below;
 // scratch = the *_scratch_bytes() of device memory, or NULL for a library buffer.

@@ -26,6 +26,11 @@ static int force_mode() {
     return force;
 }
 extern "C" int lcu_force_simt(void) { return force_mode() == 0; }
+extern "C" int lcu_conv_force_im2col(void) {
+    static int f = -1;
+    if (f < 0) { const char* e = getenv("LCU_CONV_IM2COL"); f = e && e[0] == '1'; }
+    return f;
+}
 extern "C" int lcu_use_tensor_cores(size_t M, size_t N, size_t K) {
     int force = force_mode();
     if (force != 2) return force && K > 0;
@@ -68,6 +73,14 @@ lancius_error lcu_conv2d(float* out, const float* in, const float* w, size_t N, 
     if (N && C_in && lcu_use_tensor_cores(C_out, N * Ho * Wo, C_in * K_h * K_w)) {
         LcuConvShape cs{(int)N, (int)C_in, (int)H_in, (int)W_in, (int)C_out, (int)K_h, (int)K_w, (int)stride, (int)pad,
                         (int)Ho, (int)Wo};
+        if (lcu_conv_nhwc_supported(cs) && !lcu_conv_force_im2col()) {
+            void* scratch = lcu_scratch_acquire(lcu_conv_nhwc_scratch_bytes(cs, mode == LCU_MODE_TF32 ? 1 : 3));
+            if (!scratch) return bad(LANCIUS_ERROR_OOM);
+            lancius_error e = lcu_conv2d_tc_nhwc(out, in, w, cs, relu, mode, scratch, stream);
+            // the per-device scratch is reused by the next call
+            if (e == LANCIUS_ERROR_OK) e = lcu_check_cuda(cudaStreamSynchronize(lcu_as_stream(stream)));
+            return e;
+        }
         return lcu_conv2d_tc(out, in, w, cs, relu, mode, stream);
     }
     return lcu_conv2d_simt(out, in, w, N, C_in, H_in, W_in, C_out, K_h, K_w, stride, pad, relu, stream);

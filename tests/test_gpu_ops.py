@@ -102,7 +102,11 @@ def test_attention(lib, orc, B, S, H, D, causal):
 @pytest.mark.parametrize("shape", [(2, 3, 17, 19, 8, 3, 3, 1, 1), (2, 64, 28, 28, 128, 3, 3, 2, 1),
                                    (4, 3, 64, 64, 64, 3, 3, 1, 1), (2, 128, 30, 30, 256, 3, 3, 2, 1),
                                    (3, 64, 25, 25, 128, 3, 3, 1, 1),
-                                   (1, 3, 32, 32, 6, 5, 5, 1, 2), (4, 5, 9, 9, 7, 1, 1, 1, 0)])
+                                   (1, 3, 32, 32, 6, 5, 5, 1, 2), (4, 5, 9, 9, 7, 1, 1, 1, 0),
+                                   # direct NHWC implicit-GEMM path (Ci % 16 == 0, Wo % 8 == 0)
+                                   (2, 64, 32, 32, 128, 3, 3, 1, 1), (4, 32, 64, 64, 64, 3, 3, 2, 1),
+                                   (3, 16, 24, 24, 200, 3, 3, 1, 1), (2, 64, 48, 48, 96, 1, 1, 1, 0),
+                                   (2, 16, 64, 64, 48, 5, 5, 2, 2)])
 @pytest.mark.parametrize("relu", [0, 1])
 def test_conv2d(lib, orc, shape, relu):
     N, Ci, H, W, Co, Kh, Kw, s, p = shape
