@@ -189,25 +189,39 @@ k_conv_tc(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
     }
 }
 
-// NCHW -> NHWC TF32 hi / lo (lo = 0 pointer: TF32 mode), 32 x 32 (c, w) tiles per (n, h)
-__global__ void k_nhwc_split(const float* __restrict__ in, float* __restrict__ hi, float* __restrict__ lo, int C, int H,
-                             int W) {
-    __shared__ float t[32][33];
+// NCHW -> NHWC TF32 hi / lo (lo = 0 pointer: TF32 mode): per (n, h) tiles of 32
+// channels x 64 columns through shared memory, float4 on both sides (C % 4 == 0).
+__global__ void __launch_bounds__(256) k_nhwc_split(const float* __restrict__ in, float* __restrict__ hi,
+                                                    float* __restrict__ lo, int C, int H, int W) {
+    __shared__ float t[32][65];
     const int nh = blockIdx.z, n = nh / H, h = nh % H;
-    const int c0 = blockIdx.y * 32, w0 = blockIdx.x * 32;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;      // 32 x 8
-    for (int i = ty; i < 32; i += 8) {
-        const int c = c0 + i, w = w0 + tx;
-        t[i][tx] = (c < C && w < W) ? __ldg(in + (((size_t)n * C + c) * H + h) * W + w) : 0.f;
+    const int c0 = blockIdx.y * 32, w0 = blockIdx.x * 64;
+    const bool vin = W % 4 == 0 && (reinterpret_cast<uintptr_t>(in) & 15) == 0;
+    for (int idx = threadIdx.x; idx < 32 * 16; idx += 256) {
+        const int c = idx >> 4, w = 4 * (idx & 15);
+        const float* src = in + (((size_t)n * C + c0 + c) * H + h) * W + w0 + w;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (c0 + c < C) {
+            if (vin && w0 + w + 3 < W) v = __ldg(reinterpret_cast<const float4*>(src));
+            else {
+                if (w0 + w < W) v.x = src[0];
+                if (w0 + w + 1 < W) v.y = src[1];
+                if (w0 + w + 2 < W) v.z = src[2];
+                if (w0 + w + 3 < W) v.w = src[3];
+            }
+        }
+        t[c][w] = v.x; t[c][w + 1] = v.y; t[c][w + 2] = v.z; t[c][w + 3] = v.w;
     }
     __syncthreads();
-    for (int i = ty; i < 32; i += 8) {
-        const int w = w0 + i, c = c0 + tx;
-        if (w >= W || c >= C) continue;
-        const float x = t[tx][i], xh = tc::tf32_rna(x);
-        const size_t o = (((size_t)n * H + h) * W + w) * C + c;
-        hi[o] = xh;
-        if (lo) lo[o] = tc::tf32_rna(x - xh);
+    for (int idx = threadIdx.x; idx < 64 * 8; idx += 256) {
+        const int w = idx >> 3, c = 4 * (idx & 7);
+        if (w0 + w >= W || c0 + c >= C) continue;
+        float x[4] = {t[c][w], t[c + 1][w], t[c + 2][w], t[c + 3][w]}, xh[4], xl[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) { xh[j] = tc::tf32_rna(x[j]); xl[j] = tc::tf32_rna(x[j] - xh[j]); }
+        const size_t o = (((size_t)n * H + h) * W + w0 + w) * C + c0 + c;
+        *reinterpret_cast<float4*>(hi + o) = make_float4(xh[0], xh[1], xh[2], xh[3]);
+        if (lo) *reinterpret_cast<float4*>(lo + o) = make_float4(xl[0], xl[1], xl[2], xl[3]);
     }
 }
 
@@ -289,7 +303,7 @@ extern "C" lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const f
     float* wh = reinterpret_cast<float*>(s); s += al256(we * 4);
     float* wl = passes > 1 ? reinterpret_cast<float*>(s) : nullptr;
 
-    k_nhwc_split<<<dim3((unsigned)((cs.w + 31) / 32), (unsigned)((cs.ci + 31) / 32), (unsigned)(cs.n * cs.h)), 256, 0, st>>>(
+    k_nhwc_split<<<dim3((unsigned)((cs.w + 63) / 64), (unsigned)((cs.ci + 31) / 32), (unsigned)(cs.n * cs.h)), 256, 0, st>>>(
         in, xh, xl, cs.ci, cs.h, cs.w);
     lcu_note_launch();
     k_weight_khwc_split<<<lcu_blocks(we, 256), 256, 0, st>>>(w, wh, wl, cs.co, cs.ci, cs.kh, cs.kw);

@@ -461,7 +461,8 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                     }
                     size_t ho = (st.h + 2 * st.pad - st.kh) / st.stride + 1, wo = (st.w + 2 * st.pad - st.kw) / st.stride + 1;
                     st.M = st.co; st.N = st.cn * ho * wo; st.K = st.ci * st.kh * st.kw;
-                    st.tc = st.cn && st.ci && lcu_use_tensor_cores(st.M, st.N, st.K);
+                    st.tc = st.cn && st.ci && lcu_use_tensor_cores(st.M, st.N, st.K) &&
+                            !(lcu_conv_smallk_supported(st.ci, st.kh, st.kw, st.co) && !lcu_force_tc_conv());
                     if (st.tc) {
                         size_t need = lcu_gemm_tc_scratch_bytes(st.M, st.N, st.K, 1, 1, 1, 3);
                         const LcuConvShape cs{(int)st.cn, (int)st.ci, (int)st.h, (int)st.w, (int)st.co, (int)st.kh,

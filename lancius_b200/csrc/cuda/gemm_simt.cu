@@ -29,7 +29,83 @@ __global__ void __launch_bounds__(THREADS) k_conv_simt(float* out, const float* 
     gemm_tile(A, B, C, Kdim, (size_t)blockIdx.y * BM, (size_t)blockIdx.x * BN);
 }
 
+// Direct conv for a short reduction (Ci*Kh*Kw <= 32, e.g. an RGB input layer): one
+// output pixel per thread, its K input values (zero padding) in registers, the
+// weights [Co][K4*4] in shared memory read as broadcast float4s, every output
+// channel accumulated in FP32 in k order and stored coalesced across the warp's
+// neighbouring pixels. Restates kernel_conv2d_fwd (lancius_kernels.c:28-60).
+template <int K4>
+__global__ void __launch_bounds__(256) k_conv_smallk(float* __restrict__ out, const float* __restrict__ in,
+                                                     const float* __restrict__ w, int N, int Ci, int H, int W, int Co,
+                                                     int Kh, int Kw, int stride, int pad, int Ho, int Wo, int relu) {
+    extern __shared__ float4 wsh[];                     // [Co][K4]
+    const int K = Ci * Kh * Kw;
+    for (int i = threadIdx.x; i < Co * K4 * 4; i += blockDim.x) {
+        const int co = i / (K4 * 4), k = i % (K4 * 4);
+        reinterpret_cast<float*>(wsh)[i] = k < K ? w[(size_t)co * K + k] : 0.f;
+    }
+    __syncthreads();
+    const size_t hw = (size_t)Ho * Wo, P = (size_t)N * hw;
+    for (size_t p = blockIdx.x * (size_t)blockDim.x + threadIdx.x; p < P; p += (size_t)gridDim.x * blockDim.x) {
+        const int n = (int)(p / hw), r = (int)(p % hw), ho = r / Wo, wo = r % Wo;
+        float x[K4 * 4];
+#pragma unroll
+        for (int k = 0; k < K4 * 4; k++) {
+            float v = 0.f;
+            if (k < K) {
+                const int kw = k % Kw, kh = (k / Kw) % Kh, ci = k / (Kw * Kh);
+                const int ih = ho * stride - pad + kh, iw = wo * stride - pad + kw;
+                if (ih >= 0 && iw >= 0 && ih < H && iw < W) v = __ldg(in + (((size_t)n * Ci + ci) * H + ih) * W + iw);
+            }
+            x[k] = v;
+        }
+        float* o = out + (size_t)n * Co * hw + r;
+        for (int co = 0; co < Co; co++) {
+            float acc = 0.f;
+#pragma unroll
+            for (int k4 = 0; k4 < K4; k4++) {
+                const float4 wv = wsh[co * K4 + k4];
+                acc = fmaf(wv.x, x[4 * k4], acc);
+                acc = fmaf(wv.y, x[4 * k4 + 1], acc);
+                acc = fmaf(wv.z, x[4 * k4 + 2], acc);
+                acc = fmaf(wv.w, x[4 * k4 + 3], acc);
+            }
+            o[(size_t)co * hw] = relu && acc < 0.f ? 0.f : acc;
+        }
+    }
+}
+
 extern "C" {
+
+int lcu_conv_smallk_supported(size_t Ci, size_t Kh, size_t Kw, size_t Co) {
+    return Ci * Kh * Kw <= 32 && Co <= 512 && Ci * Kh * Kw > 0;
+}
+
+lancius_error lcu_conv2d_smallk(float* out, const float* in, const float* w, size_t N, size_t Ci, size_t H, size_t W,
+                                size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu, void* stream) {
+    const size_t Ho = (H + 2 * pad - Kh) / stride + 1, Wo = (W + 2 * pad - Kw) / stride + 1;
+    const size_t P = N * Ho * Wo, K = Ci * Kh * Kw;
+    if (P == 0 || Co == 0) return LANCIUS_ERROR_OK;
+    const int K4 = (int)((K + 3) / 4);
+    const size_t smem = Co * K4 * sizeof(float4);
+    const unsigned grid = lcu_blocks(P, 256, 148u * 8u);
+    cudaStream_t st = lcu_as_stream(stream);
+#define LCU_SMALLK(k4)                                                                                                \
+    case k4:                                                                                                          \
+        if (smem > 48 * 1024 && cudaFuncSetAttribute(k_conv_smallk<k4>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \
+                                                     (int)smem) != cudaSuccess)                                       \
+            return lcu_launch_status();                                                                               \
+        k_conv_smallk<k4><<<grid, 256, smem, st>>>(out, in, w, (int)N, (int)Ci, (int)H, (int)W, (int)Co, (int)Kh,    \
+                                                  (int)Kw, (int)stride, (int)pad, (int)Ho, (int)Wo, relu);            \
+        break;
+    switch (K4) {
+        LCU_SMALLK(1) LCU_SMALLK(2) LCU_SMALLK(3) LCU_SMALLK(4) LCU_SMALLK(5) LCU_SMALLK(6) LCU_SMALLK(7) LCU_SMALLK(8)
+        default: lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP;
+    }
+#undef LCU_SMALLK
+    lcu_note_launch();
+    return lcu_launch_status();
+}
 
 // Grouped launch over a device-resident table of `count` products of one shape.
 lancius_error lcu_gemm_simt_grouped(const LcuGemmGroup* d_groups, int count, size_t M, size_t N, size_t K, int epi,

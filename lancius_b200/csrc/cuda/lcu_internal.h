@@ -64,7 +64,12 @@ int lcu_conv_nhwc_supported(LcuConvShape cs);
 size_t lcu_conv_nhwc_scratch_bytes(LcuConvShape cs, int passes);
 lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const float* w, LcuConvShape cs, int relu, int mode,
                                  void* scratch, void* stream);
-int lcu_conv_force_im2col(void);   // LCU_CONV_IM2COL=1: keep the materialised-im2col conv
+int lcu_conv_force_im2col(void);
+// direct CUDA-core conv for Ci*Kh*Kw <= 32 (first layers), any stride and padding
+int lcu_conv_smallk_supported(size_t Ci, size_t Kh, size_t Kw, size_t Co);
+int lcu_force_tc_conv(void);
+lancius_error lcu_conv2d_smallk(float* out, const float* in, const float* w, size_t N, size_t Ci, size_t H, size_t W,
+                                size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu, void* stream);   // LCU_CONV_IM2COL=1: keep the materialised-im2col conv
 int lcu_conv_watchdog_read_and_clear(void);
 void* lcu_scratch_acquire(size_t bytes);
 // INT8 weights: tensor cores (gemm_i8.cu) above lcu_int8_use_tc's size, CUDA cores below;

@@ -26,6 +26,8 @@ static int force_mode() {
     return force;
 }
 extern "C" int lcu_force_simt(void) { return force_mode() == 0; }
+// LCU_FORCE_TC=1 also sends short-reduction convs to the tensor cores (tests)
+extern "C" int lcu_force_tc_conv(void) { return force_mode() == 1; }
 extern "C" int lcu_conv_force_im2col(void) {
     static int f = -1;
     if (f < 0) { const char* e = getenv("LCU_CONV_IM2COL"); f = e && e[0] == '1'; }
@@ -70,6 +72,8 @@ lancius_error lcu_conv2d(float* out, const float* in, const float* w, size_t N, 
     if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
     if (stride == 0 || H_in + 2 * pad < K_h || W_in + 2 * pad < K_w) return bad(LANCIUS_ERROR_SHAPE_MISMATCH);
     size_t Ho = (H_in + 2 * pad - K_h) / stride + 1, Wo = (W_in + 2 * pad - K_w) / stride + 1;
+    if (lcu_conv_smallk_supported(C_in, K_h, K_w, C_out) && !lcu_force_tc_conv())
+        return lcu_conv2d_smallk(out, in, w, N, C_in, H_in, W_in, C_out, K_h, K_w, stride, pad, relu, stream);
     if (N && C_in && lcu_use_tensor_cores(C_out, N * Ho * Wo, C_in * K_h * K_w)) {
         LcuConvShape cs{(int)N, (int)C_in, (int)H_in, (int)W_in, (int)C_out, (int)K_h, (int)K_w, (int)stride, (int)pad,
                         (int)Ho, (int)Wo};
