@@ -29,48 +29,62 @@ __global__ void __launch_bounds__(THREADS) k_conv_simt(float* out, const float* 
     gemm_tile(A, B, C, Kdim, (size_t)blockIdx.y * BM, (size_t)blockIdx.x * BN);
 }
 
-// Direct conv for a short reduction (Ci*Kh*Kw <= 32, e.g. an RGB input layer): one
-// output pixel per thread, its K input values (zero padding) in registers, the
-// weights [Co][K4*4] in shared memory read as broadcast float4s, every output
-// channel accumulated in FP32 in k order and stored coalesced across the warp's
-// neighbouring pixels. Restates kernel_conv2d_fwd (lancius_kernels.c:28-60).
+// Direct conv for a short reduction (Ci*Kh*Kw <= 32, e.g. an RGB input layer): each
+// thread takes two output pixels (one grid stride apart, so stores stay coalesced),
+// gathers their K input values (zero padding) into registers through a per-k offset
+// table, and accumulates every output channel in FP32 in k order against weights
+// [Co][K4*4] read from shared memory as broadcast float4s (one read feeds both
+// pixels). Restates kernel_conv2d_fwd (lancius_kernels.c:28-60).
 template <int K4>
 __global__ void __launch_bounds__(256) k_conv_smallk(float* __restrict__ out, const float* __restrict__ in,
                                                      const float* __restrict__ w, int N, int Ci, int H, int W, int Co,
                                                      int Kh, int Kw, int stride, int pad, int Ho, int Wo, int relu) {
     extern __shared__ float4 wsh[];                     // [Co][K4]
+    __shared__ int koff[K4 * 4], kdy[K4 * 4], kdx[K4 * 4];
     const int K = Ci * Kh * Kw;
     for (int i = threadIdx.x; i < Co * K4 * 4; i += blockDim.x) {
         const int co = i / (K4 * 4), k = i % (K4 * 4);
         reinterpret_cast<float*>(wsh)[i] = k < K ? w[(size_t)co * K + k] : 0.f;
     }
+    for (int k = threadIdx.x; k < K4 * 4; k += blockDim.x) {
+        const int kw = k % Kw, kh = (k / Kw) % Kh, ci = k / (Kw * Kh);
+        koff[k] = k < K ? (ci * H + kh) * W + kw : 0;
+        kdy[k] = k < K ? kh : -(1 << 20);               // padded k: always out of range
+        kdx[k] = kw;
+    }
     __syncthreads();
-    const size_t hw = (size_t)Ho * Wo, P = (size_t)N * hw;
-    for (size_t p = blockIdx.x * (size_t)blockDim.x + threadIdx.x; p < P; p += (size_t)gridDim.x * blockDim.x) {
-        const int n = (int)(p / hw), r = (int)(p % hw), ho = r / Wo, wo = r % Wo;
-        float x[K4 * 4];
+    const int hw = Ho * Wo, P = N * hw, chw = Ci * H * W;
+    const int S = gridDim.x * blockDim.x;
+    for (int p0 = blockIdx.x * blockDim.x + threadIdx.x; p0 < P; p0 += 2 * S) {
+        const int pp[2] = {p0, p0 + S};
+        float x[2][K4 * 4];
+        int obase[2];
 #pragma unroll
-        for (int k = 0; k < K4 * 4; k++) {
-            float v = 0.f;
-            if (k < K) {
-                const int kw = k % Kw, kh = (k / Kw) % Kh, ci = k / (Kw * Kh);
-                const int ih = ho * stride - pad + kh, iw = wo * stride - pad + kw;
-                if (ih >= 0 && iw >= 0 && ih < H && iw < W) v = __ldg(in + (((size_t)n * Ci + ci) * H + ih) * W + iw);
+        for (int j = 0; j < 2; j++) {
+            const int p = pp[j] < P ? pp[j] : p0;
+            const int n = p / hw, r = p - n * hw, ho = r / Wo, wo = r - ho * Wo;
+            const int y0 = ho * stride - pad, x0 = wo * stride - pad;
+            const float* base = in + (size_t)n * chw + y0 * W + x0;
+            obase[j] = n * Co * hw + r;
+#pragma unroll
+            for (int k = 0; k < K4 * 4; k++) {
+                const int iy = y0 + kdy[k], ix = x0 + kdx[k];
+                x[j][k] = (iy >= 0 && ix >= 0 && iy < H && ix < W) ? __ldg(base + koff[k]) : 0.f;
             }
-            x[k] = v;
         }
-        float* o = out + (size_t)n * Co * hw + r;
+        const bool second = pp[1] < P;
         for (int co = 0; co < Co; co++) {
-            float acc = 0.f;
+            float a0 = 0.f, a1 = 0.f;
 #pragma unroll
             for (int k4 = 0; k4 < K4; k4++) {
                 const float4 wv = wsh[co * K4 + k4];
-                acc = fmaf(wv.x, x[4 * k4], acc);
-                acc = fmaf(wv.y, x[4 * k4 + 1], acc);
-                acc = fmaf(wv.z, x[4 * k4 + 2], acc);
-                acc = fmaf(wv.w, x[4 * k4 + 3], acc);
+                a0 = fmaf(wv.x, x[0][4 * k4], a0); a1 = fmaf(wv.x, x[1][4 * k4], a1);
+                a0 = fmaf(wv.y, x[0][4 * k4 + 1], a0); a1 = fmaf(wv.y, x[1][4 * k4 + 1], a1);
+                a0 = fmaf(wv.z, x[0][4 * k4 + 2], a0); a1 = fmaf(wv.z, x[1][4 * k4 + 2], a1);
+                a0 = fmaf(wv.w, x[0][4 * k4 + 3], a0); a1 = fmaf(wv.w, x[1][4 * k4 + 3], a1);
             }
-            o[(size_t)co * hw] = relu && acc < 0.f ? 0.f : acc;
+            out[(size_t)obase[0] + (size_t)co * hw] = relu && a0 < 0.f ? 0.f : a0;
+            if (second) out[(size_t)obase[1] + (size_t)co * hw] = relu && a1 < 0.f ? 0.f : a1;
         }
     }
 }
@@ -80,12 +94,17 @@ extern "C" {
 int lcu_conv_smallk_supported(size_t Ci, size_t Kh, size_t Kw, size_t Co) {
     return Ci * Kh * Kw <= 32 && Co <= 512 && Ci * Kh * Kw > 0;
 }
+static bool smallk_fits_int(size_t N, size_t Ci, size_t H, size_t W, size_t Co, size_t Ho, size_t Wo) {
+    return N * Co * Ho * Wo < (1u << 31) && Ci * H * W < (1u << 31);
+}
 
 lancius_error lcu_conv2d_smallk(float* out, const float* in, const float* w, size_t N, size_t Ci, size_t H, size_t W,
                                 size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu, void* stream) {
     const size_t Ho = (H + 2 * pad - Kh) / stride + 1, Wo = (W + 2 * pad - Kw) / stride + 1;
     const size_t P = N * Ho * Wo, K = Ci * Kh * Kw;
     if (P == 0 || Co == 0) return LANCIUS_ERROR_OK;
+    if (!smallk_fits_int(N, Ci, H, W, Co, Ho, Wo))
+        return lcu_conv2d_simt(out, in, w, N, Ci, H, W, Co, Kh, Kw, stride, pad, relu, stream);
     const int K4 = (int)((K + 3) / 4);
     const size_t smem = Co * K4 * sizeof(float4);
     const unsigned grid = lcu_blocks(P, 256, 148u * 8u);
