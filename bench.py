@@ -145,34 +145,75 @@ def _all_host_threads():
     return os.cpu_count()
 
 
+def _ref_sample(cfg):
+    """One bounded sample of `cfg` for the reference's own CPU executor: (graph builder,
+    factor from the sample's time to one full unit of the metric, description)."""
+    from lancius_b200 import configs
+    if cfg == "attention":
+        return (lambda g: configs.attention(g, batch=2, seq=512, heads=8, head_dim=64, seed=1)), 4.0, \
+            "2 of 8 batch elements (S512 H8 D64 causal), scaled x4 to one batch-8 graph"
+    if cfg == "mlp":
+        return (lambda g: configs.mlp(g, batch=64, seed=0)), 1.0, "the full batch-64 graph"
+    if cfg == "conv":
+        return (lambda g: configs.conv_stack(g, batch=1, hw=224, seed=2)), 32.0, \
+            "1 of 32 images through the conv stack, scaled x32"
+    if cfg in ("encoder", "encoder_b256"):
+        nb = 16 if cfg == "encoder" else 256
+        # the reference's ATTENTION is always causal; it still visits every key (masking by
+        # -1e9), so its cost equals the unmasked attention of this config
+        return (lambda g: configs.encoder(g, batch=1, seq=512, layers=1, seed=3, causal=True)), 12.0 * nb, \
+            f"1 layer of 1 sequence (S512, d768; causal ATTENTION node, same cost), scaled x12 layers x{nb} sequences"
+    if cfg.startswith("gemm"):
+        n = int(cfg[4:])
+        ns = min(n, 1024)
+        return (lambda g: configs.gemm(g, ns, seed=4)), (n / ns) ** 3, \
+            f"a {ns}^3 product, scaled by (N/{ns})^3 to {n}^3 (the reference MATMUL is one thread, i-k-j)"
+    return None
+
+
+def _ref_run_seconds(ref, build, min_s=3.0, max_reps=None):
+    """Seconds per run of the sample graph through lancius_schedule_execute (arena mode),
+    and the sample's Built record (its algorithmic FLOPs and bytes)."""
+    import oracle
+    from lancius_b200 import Graph
+    g = Graph(ref)
+    b = build(g)
+    b.bind_host()
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        oracle.run_reference_graph(ref, g, b.outputs[:1], arena_bytes=512 << 20)
+        reps += 1
+        if time.perf_counter() - t0 > min_s or (max_reps and reps >= max_reps):
+            break
+    return (time.perf_counter() - t0) / reps, reps, b
+
+
+def _sample_value(cfg, b, sec):
+    """The metric's throughput measured on the sample (the scaling factor cancels)."""
+    if cfg == "mlp":
+        return 1.0 / sec
+    if cfg == "attention":
+        return b.bytes / sec / 1e9
+    return b.flops / sec / 1e12
+
+
 def cpu_baseline(cfg, steps=None):
     """Times the reference's arena-mode executor on a bounded sample of the workload.
     Returns (value in the metric's unit, description dict)."""
     import oracle
-    from lancius_b200 import Graph, configs
     if not oracle.reference_available():
+        return None
+    smp = _ref_sample(cfg)
+    if smp is None:
         return None
     ref = oracle.reference()
     cores = _all_host_threads()
-    if cfg == "attention":
-        # sample: 2 of the 8 batch elements (one ATTENTION node each), scaled per graph
-        g = Graph(ref)
-        b = configs.attention(g, batch=2, seq=512, heads=8, head_dim=64, seed=1)
-        b.bind_host()
-        t0 = time.perf_counter()
-        reps = 0
-        while True:
-            oracle.run_reference_graph(ref, g, b.outputs[:1])
-            reps += 1
-            if time.perf_counter() - t0 > 3.0 or (steps and reps >= steps):
-                break
-        sec = (time.perf_counter() - t0) / reps * 4.0    # 2 elements -> 8
-        val = 16.0 * 8 * 512 * 512 / sec / 1e9
-        return val, {"kind": "reference", "cores": cores,
-                     "sample": f"{reps} runs of 2 of 8 batch elements (S512 H8 D64 causal) through "
-                               "lancius_schedule_execute, scaled x4 to one batch-8 graph; "
-                               f"OpenMP threads = {cores}"}
-    return None
+    build, factor, what = smp
+    sec, reps, b = _ref_run_seconds(ref, build, max_reps=steps)
+    return _sample_value(cfg, b, sec), {
+        "kind": "reference", "cores": cores,
+        "sample": f"{reps} runs of {what} through lancius_schedule_execute; OpenMP threads = {cores}"}
 
 
 # the B200 arm -----------------------------------------------------------------------
@@ -673,7 +714,7 @@ def reference_arm(args, metric, unit, workload):
     if args.config == "decode":
         return reference_arm_decode(args, metric, unit, workload)
     if args.config != "attention":
-        return {"impl": "reference", "unavailable": f"reference arm implemented for the attention and decode workloads"}
+        return reference_arm_sampled(args, metric, unit, workload)
     ref = oracle.reference()
     _all_host_threads()
     g = Graph(ref)
@@ -703,6 +744,34 @@ def reference_arm(args, metric, unit, workload):
                              "sample": "the full batch-8 graph per step on the host CPU, reference C sources "
                                        "compiled by oracle/Makefile; OpenMP threads = all host cores"},
             "e2e": {"value": round(val, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def reference_arm_sampled(args, metric, unit, workload):
+    """The reference's own executor on the host cores for the non-attention configs: each
+    step runs one bounded sample of the workload (see _ref_sample)."""
+    import oracle
+    smp = _ref_sample(args.config)
+    if smp is None:
+        return {"impl": "reference", "unavailable": f"no reference sample defined for {args.config}"}
+    ref = oracle.reference()
+    cores = _all_host_threads()
+    build, factor, what = smp
+    secs = []
+    b = None
+    for i in range(args.warmup + args.steps):
+        sec, _, b = _ref_run_seconds(ref, build, min_s=0.0, max_reps=1)
+        if i >= args.warmup:
+            secs.append(sec)
+    sec = sum(secs) / len(secs)
+    val = _sample_value(args.config, b, sec)
+    return {"impl": "reference", "metric": metric, "value": round(val, 6), "unit": unit, "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * factor * 1e3, 3),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded, splitmix64)",
+            "config": {"workload": workload, "executor": "lancius_schedule_execute (arena mode)"},
+            "cpu_baseline": {"value": round(val, 6), "unit": unit, "kind": "reference", "cores": cores,
+                             "sample": f"each step: {what}; OpenMP threads = all host cores"},
+            "e2e": {"value": round(val, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
 def reference_arm_decode(args, metric, unit, workload):

@@ -105,7 +105,7 @@ def conv_stack(g, batch=32, hw=224, seed=2, fuse=True):
     return b
 
 
-def encoder(g, batch=16, seq=512, layers=12, d_model=768, heads=12, ffn=3072, seed=3, first=0):
+def encoder(g, batch=16, seq=512, layers=12, d_model=768, heads=12, ffn=3072, seed=3, first=0, causal=False):
     """Config 4: pre-LN BERT-shape encoder, GELU FFN, unmasked attention, eps 1e-5.
 
     One subgraph per batch element (the IR has no slice op); weight INPUT nodes are
@@ -141,7 +141,8 @@ def encoder(g, batch=16, seq=512, layers=12, d_model=768, heads=12, ffn=3072, se
             x = xs[e]
             h = g.layernorm(x, g1, be1)
             q, kk, v = (g.reshape(lin(h, nm, d_model), seq, heads, hd) for nm in ("q", "k", "v"))
-            a = g.reshape(g.attention_noncausal(q, kk, v), seq, d_model)
+            att = g.attention(q, kk, v) if causal else g.attention_noncausal(q, kk, v)
+            a = g.reshape(att, seq, d_model)
             o = g.add(lin(a, "o", d_model), x)
             h2 = g.layernorm(o, g2, be2)
             f = g.gelu(lin(h2, "f1", ffn))

@@ -138,11 +138,11 @@ def reference():
     return lib
 
 
-def run_reference_graph(lib, graph, nodes):
+def run_reference_graph(lib, graph, nodes, arena_bytes=64 << 20):
     """Executes `graph` (built with the reference library) in arena mode with the
     reference's own lancius_schedule_execute; returns {node_id: ndarray}."""
     sched = lib.lancius_ir_schedule(graph.ptr)
-    arena = lib.lancius_arena_create(64 << 20)
+    arena = lib.lancius_arena_create(arena_bytes)
     try:
         lib.lancius_schedule_execute(sched, arena)
         out = {}
