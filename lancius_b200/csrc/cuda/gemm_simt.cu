@@ -12,6 +12,73 @@ __global__ void __launch_bounds__(THREADS) k_gemm_simt(const LcuGemmGroup* __res
     gemm_tile(A, B, C, K, (size_t)blockIdx.y * BM, (size_t)blockIdx.x * BN);
 }
 
+// Small products (the MLP's 64 x 784 x 256): a 128 x 128 tile grid would leave almost
+// every SM idle, so each CTA takes a 16 x 32 output tile. K is walked in chunks of 128:
+// all 256 threads load the chunk's A (16 x 128) and B (128 x 32) tiles into shared memory
+// at once (one memory round trip per chunk), then warp w accumulates k = 16w .. 16w+15 of
+// the chunk; the eight warps' partial tiles are summed in a fixed order (deterministic)
+// and the epilogue is applied as in DenseC.
+constexpr int SK_TM = 16, SK_TN = 32, SK_WARPS = 8, SK_KC = 128;
+__global__ void __launch_bounds__(256) k_gemm_skinny(const LcuGemmGroup* __restrict__ groups, LcuGemmGroup one,
+                                                     size_t M, size_t N, size_t K, int epi) {
+    __shared__ float As[SK_TM][SK_KC + 1];
+    __shared__ float Bs[SK_KC][SK_TN];
+    __shared__ float part[SK_WARPS][SK_TM][SK_TN + 1];
+    const LcuGemmGroup gr = groups ? groups[blockIdx.z] : one;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const size_t m0 = (size_t)blockIdx.y * SK_TM, n0 = (size_t)blockIdx.x * SK_TN;
+    float acc[SK_TM];
+#pragma unroll
+    for (int i = 0; i < SK_TM; i++) acc[i] = 0.f;
+    for (size_t k0 = 0; k0 < K; k0 += SK_KC) {
+        float av[SK_TM * SK_KC / 256], bv[SK_KC * SK_TN / 256];
+#pragma unroll
+        for (int r = 0; r < SK_TM * SK_KC / 256; r++) {        // A: 16 rows x 128 k, coalesced along k
+            const int idx = threadIdx.x + 256 * r, i = idx / SK_KC, kk = idx % SK_KC;
+            av[r] = (m0 + i < M && k0 + kk < K) ? __ldg(gr.a + (m0 + i) * K + k0 + kk) : 0.f;
+        }
+#pragma unroll
+        for (int r = 0; r < SK_KC * SK_TN / 256; r++) {        // B: 128 k x 32 n, coalesced along n
+            const int idx = threadIdx.x + 256 * r, kk = idx / SK_TN, j = idx % SK_TN;
+            bv[r] = (k0 + kk < K && n0 + j < N) ? __ldg(gr.b + (k0 + kk) * N + n0 + j) : 0.f;
+        }
+        __syncthreads();                                        // the previous chunk is consumed
+#pragma unroll
+        for (int r = 0; r < SK_TM * SK_KC / 256; r++) {
+            const int idx = threadIdx.x + 256 * r;
+            As[idx / SK_KC][idx % SK_KC] = av[r];
+        }
+#pragma unroll
+        for (int r = 0; r < SK_KC * SK_TN / 256; r++) {
+            const int idx = threadIdx.x + 256 * r;
+            Bs[idx / SK_TN][idx % SK_TN] = bv[r];
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = warp * (SK_KC / SK_WARPS); kk < (warp + 1) * (SK_KC / SK_WARPS); kk++) {
+            const float b = Bs[kk][lane];
+#pragma unroll
+            for (int i = 0; i < SK_TM; i++) acc[i] = fmaf(As[i][kk], b, acc[i]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < SK_TM; i++) part[warp][i][lane] = acc[i];
+    __syncthreads();
+    const DenseC C{gr.c, gr.bias, gr.resid, M, N, N, epi};
+    for (int o = threadIdx.x; o < SK_TM * SK_TN; o += blockDim.x) {
+        const int i = o / SK_TN, j = o % SK_TN;
+        float sum = 0.f;
+#pragma unroll
+        for (int w = 0; w < SK_WARPS; w++) sum += part[w][i][j];
+        C(m0 + i, n0 + j, sum);
+    }
+}
+
+static bool use_skinny(size_t M, size_t N, int count) {
+    const size_t tiles = ((N + BN - 1) / BN) * ((M + BM - 1) / BM) * (size_t)count;
+    return tiles < 64 && M * N <= (1u << 20);
+}
+
 __global__ void __launch_bounds__(THREADS) k_gemm_simt1(LcuGemmGroup gr, size_t M, size_t N, size_t K, int epi) {
     DenseA A{gr.a, M, K, K};
     DenseB B{gr.b, K, N, N};
@@ -130,6 +197,12 @@ lancius_error lcu_conv2d_smallk(float* out, const float* in, const float* w, siz
 lancius_error lcu_gemm_simt_grouped(const LcuGemmGroup* d_groups, int count, size_t M, size_t N, size_t K, int epi,
                                     void* stream) {
     if (count <= 0 || M == 0 || N == 0) return LANCIUS_ERROR_OK;
+    if (use_skinny(M, N, count)) {
+        dim3 g((unsigned)((N + SK_TN - 1) / SK_TN), (unsigned)((M + SK_TM - 1) / SK_TM), (unsigned)count);
+        k_gemm_skinny<<<g, 256, 0, lcu_as_stream(stream)>>>(d_groups, LcuGemmGroup{}, M, N, K, epi);
+        lcu_note_launch();
+        return lcu_launch_status();
+    }
     dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), (unsigned)count);
     k_gemm_simt<<<grid, THREADS, 0, lcu_as_stream(stream)>>>(d_groups, M, N, K, epi);
     lcu_note_launch();
@@ -140,6 +213,12 @@ lancius_error lcu_gemm_simt(float* c, const float* a, const float* b, size_t M, 
                             int epi, void* stream) {
     if (M == 0 || N == 0) return LANCIUS_ERROR_OK;
     LcuGemmGroup g{a, b, c, bias, nullptr};
+    if (use_skinny(M, N, 1)) {
+        dim3 gs((unsigned)((N + SK_TN - 1) / SK_TN), (unsigned)((M + SK_TM - 1) / SK_TM), 1);
+        k_gemm_skinny<<<gs, 256, 0, lcu_as_stream(stream)>>>(nullptr, g, M, N, K, epi);
+        lcu_note_launch();
+        return lcu_launch_status();
+    }
     dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM), 1);
     k_gemm_simt1<<<grid, THREADS, 0, lcu_as_stream(stream)>>>(g, M, N, K, epi);
     lcu_note_launch();
