@@ -15,6 +15,7 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ORACLE_SO = os.path.join(HERE, "liblcu_oracle.so")
 REF_SO = os.path.join(HERE, "_ref", "liblancius_ref.so")
+BASIS_REF_SO = os.path.join(HERE, "_ref", "libbasis_ref.so")
 
 _D = C.POINTER(C.c_double)
 _S = C.c_size_t
@@ -153,3 +154,11 @@ def run_reference_graph(lib, graph, nodes, arena_bytes=64 << 20):
     finally:
         lib.lancius_arena_destroy(arena)
         lib.lancius_schedule_destroy(sched)
+
+
+def basis_reference():
+    """The reference's BASIS graph builder (src/basis/stage6_ir/graph.c, compiled here), or
+    None when it was not built."""
+    if not os.path.exists(BASIS_REF_SO):
+        return None
+    return C.CDLL(BASIS_REF_SO, mode=os.RTLD_LOCAL)

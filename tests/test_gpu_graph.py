@@ -135,3 +135,28 @@ def test_lenet_model_file_on_gpu(device, orc):
     ort = np.fromfile(os.path.join(gold, "baseline_out.bin"), dtype=np.float32)
     assert_close(y, ort, 1e-4)
     assert_close(y, orc.run_graph(g, [out])[out.id].ravel(), 1e-4)
+
+
+def test_basis_graph_lowered_on_gpu(device, orc):
+    """A BASIS stage-6 graph (the reference's legacy builder API), lowered onto the Lancius
+    IR and run by the B200 executor, against the oracle on the same lowered graph."""
+    from lancius_b200 import data
+    from lancius_b200.basis import BasisGraph
+    g = BasisGraph()
+    x = g.input("x", 64, 784)
+    w1, b1 = g.input("w1", 784, 256), g.input("b1", 1, 256)
+    w2, b2 = g.input("w2", 256, 10), g.input("b2", 1, 10)
+    h = g.relu(g.broadcast_add(g.matmul(x, w1), b1))
+    y = g.tanh(g.broadcast_add(g.matmul(h, w2), b2))
+    lg, m = g.lower()
+    arrays = {x: data.normal(1, (64, 784)), w1: data.normal(2, (784, 256), 0, 0.05), b1: data.normal(3, (1, 256)),
+              w2: data.normal(4, (256, 10), 0, 0.1), b2: data.normal(5, (1, 10))}
+    for bid, arr in arrays.items():
+        lg.bind(m[bid], np.asarray(arr, np.float32).astype(np.float64))
+    s = lg.schedule()
+    device.set_graph_replay(False)
+    device.bind(s)
+    device.upload_bound_inputs()
+    device.execute(s)
+    want = orc.run_graph(lg, [m[y]])[m[y].id]
+    assert_close(device.download(m[y]), want, 1e-4)
