@@ -674,11 +674,19 @@ def main():
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": 25256448,
                 "kernel": "attention (one grouped launch over the 8 ATTENTION nodes)",
-                "peak_src": pk["src"] + " hbm_gbs (burst copy)"}
+                "peak_src": pk["src"] + " hbm_gbs (burst copy)",
+                # the kernel is compute-bound: its algorithmic FLOPs (QK^T and PV over the
+                # causal triangle) against the 3xTF32 ceiling = TF32 dense (bf16 / 2) / 3
+                "tensor_view": {"achieved_tflops": round(built.flops / sec_per_graph / 1e12, 2),
+                                "mode_ceiling_tflops": round(pk["bf16_tflops"] / 6, 1),
+                                "frac_of_mode_ceiling": round(built.flops / sec_per_graph / 1e12 / (pk["bf16_tflops"] / 6), 4)}}
     else:
         achieved = built.flops / sec_per_graph / 1e12
         roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": None, "peak_src": pk["src"] + " bf16"}
+                "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": None, "peak_src": pk["src"] + " bf16",
+                # FP32-exact = 3 TF32 MMAs per product; TF32 dense rate = bf16 / 2
+                "tf32_peak": round(pk["bf16_tflops"] / 2, 1), "frac_of_tf32_peak": round(achieved / (pk["bf16_tflops"] / 2), 4),
+                "mode_ceiling": round(pk["bf16_tflops"] / 6, 1), "frac_of_mode_ceiling": round(achieved / (pk["bf16_tflops"] / 6), 4)}
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         try:
