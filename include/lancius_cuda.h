@@ -58,6 +58,10 @@ lancius_error lcu_bind_plan(lcu_ctx* ctx, lancius_schedule* sched, lancius_graph
  * quantized weights (bytes, uploaded as they are). */
 lancius_error lcu_upload(lcu_ctx* ctx, const lancius_node* n, const void* host, lancius_dtype host_dtype);
 lancius_error lcu_download(lcu_ctx* ctx, const lancius_node* n, void* host, lancius_dtype host_dtype);
+/* FP32 download queued on the context's stream without waiting (complete after
+ * lcu_synchronize); for pipelining requests over two contexts. The reference has no
+ * device copies, so no counterpart. */
+lancius_error lcu_download_async(lcu_ctx* ctx, const lancius_node* n, void* host);
 /* Uploads every INPUT node whose runtime_data (FP64) is bound on the host. */
 lancius_error lcu_upload_bound_inputs(lcu_ctx* ctx);
 float* lcu_node_device_ptr(lcu_ctx* ctx, const lancius_node* n);

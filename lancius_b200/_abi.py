@@ -117,6 +117,7 @@ B200_FUNCS = {
     "lcu_bind_plan": (C.c_int, [P, SCHED_P, GRAPH_P, PLAN_P]),
     "lcu_upload": (C.c_int, [P, NODE_P, P, C.c_int]),
     "lcu_download": (C.c_int, [P, NODE_P, P, C.c_int]),
+    "lcu_download_async": (C.c_int, [P, NODE_P, C.c_void_p]),
     "lcu_upload_bound_inputs": (C.c_int, [P]),
     "lcu_node_device_ptr": (P, [P, NODE_P]),
     "lancius_schedule_execute_cuda": (None, [SCHED_P, P]),

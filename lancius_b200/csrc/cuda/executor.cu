@@ -689,6 +689,17 @@ extern "C" lancius_error lcu_upload(lcu_ctx* c, const lancius_node* n, const voi
     return lcu_convert_f64_to_f32(d, c->staging, E, c->stream);
 }
 
+// FP32 device -> host copy queued on the context's stream; returns at once (the data is
+// there after lcu_synchronize). With page-locked `host` the copy overlaps other streams'
+// work, e.g. the next request's uploads on a second context.
+extern "C" lancius_error lcu_download_async(lcu_ctx* c, const lancius_node* n, void* host) {
+    float* d; size_t E;
+    if (!host) return fail(LANCIUS_ERROR_NULL_PTR);
+    if (!node_slot(c, n, &d, &E)) return fail(LANCIUS_ERROR_NULL_PTR);
+    cudaSetDevice(c->device);
+    return cuda_fail(cudaMemcpyAsync(host, d, E * 4, cudaMemcpyDeviceToHost, c->stream));
+}
+
 extern "C" lancius_error lcu_download(lcu_ctx* c, const lancius_node* n, void* host, lancius_dtype dt) {
     float* d; size_t E;
     if (!host) return fail(LANCIUS_ERROR_NULL_PTR);
