@@ -43,6 +43,10 @@ void lcu_destroy(lcu_ctx* ctx);
 lancius_error lcu_set_mode(lcu_ctx* ctx, lcu_mode mode);
 void* lcu_stream(lcu_ctx* ctx);                 /* the context's cudaStream_t */
 lancius_error lcu_synchronize(lcu_ctx* ctx);     /* also reports device watchdog flags */
+/* Test hook (no reference counterpart): launches a kernel whose bounded wait on an
+ * mbarrier nothing arrives on gives up and sets the GEMM watchdog word, so the next
+ * lcu_synchronize returns LANCIUS_ERROR_INTERNAL (and clears the word). */
+lancius_error lcu_watchdog_selftest(void* stream);
 
 /* ---- graph binding: the memory plan's offsets map onto one device allocation.
  * plan == NULL: the backend plans the FP32 device pool itself

@@ -118,6 +118,7 @@ B200_FUNCS = {
     "lcu_upload": (C.c_int, [P, NODE_P, P, C.c_int]),
     "lcu_download": (C.c_int, [P, NODE_P, P, C.c_int]),
     "lcu_download_async": (C.c_int, [P, NODE_P, C.c_void_p]),
+    "lcu_watchdog_selftest": (C.c_int, [P]),
     "lcu_upload_bound_inputs": (C.c_int, [P]),
     "lcu_node_device_ptr": (P, [P, NODE_P]),
     "lancius_schedule_execute_cuda": (None, [SCHED_P, P]),

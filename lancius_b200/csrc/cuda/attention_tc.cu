@@ -441,3 +441,9 @@ extern "C" int lcu_attention_watchdog_read_and_clear(void) {
     if (v) cudaMemcpyToSymbol(g_attn_watchdog, &z, sizeof(int));
     return v;
 }
+
+// Device address of this file's watchdog word on the current device (0 if unavailable).
+extern "C" int* lcu_attention_watchdog_addr(void) {
+    void* p = nullptr;
+    return cudaGetSymbolAddress(&p, g_attn_watchdog) == cudaSuccess ? static_cast<int*>(p) : nullptr;
+}

@@ -353,3 +353,9 @@ extern "C" int lcu_conv_watchdog_read_and_clear(void) {
     if (v) cudaMemcpyToSymbol(g_conv_watchdog, &z, sizeof(int));
     return v;
 }
+
+// Device address of this file's watchdog word on the current device (0 if unavailable).
+extern "C" int* lcu_conv_watchdog_addr(void) {
+    void* p = nullptr;
+    return cudaGetSymbolAddress(&p, g_conv_watchdog) == cudaSuccess ? static_cast<int*>(p) : nullptr;
+}

@@ -81,6 +81,7 @@ struct lcu_ctx {
     std::vector<size_t> off;            // node id -> byte offset in dmem (NPOS: no storage)
     std::vector<Step> steps;
     cudaGraphExec_t exec = nullptr;
+    int* wd_host = nullptr;             // page-locked copies of the watchdog words
     int graph_launches = 0;
     int last_launches = 0;
 };
@@ -128,6 +129,7 @@ void lcu_destroy(lcu_ctx* c) {
     cudaStreamSynchronize(c->stream);
     release_binding(c);
     cudaStreamDestroy(c->stream);
+    if (c->wd_host) cudaFreeHost(c->wd_host);
     delete c;
 }
 
@@ -154,10 +156,36 @@ lancius_error lcu_set_fusion(lcu_ctx* c, int enable) {
 
 void* lcu_stream(lcu_ctx* c) { return c ? (void*)c->stream : nullptr; }
 
+// Waits for the context's stream, then reads the tensor-core kernels' watchdog words
+// (set when a bounded mbarrier wait gave up): any set word is cleared and reported as
+// LANCIUS_ERROR_INTERNAL. The words are per device, shared by all contexts on it.
 lancius_error lcu_synchronize(lcu_ctx* c) {
     if (!c) return fail(LANCIUS_ERROR_NULL_PTR);
     cudaSetDevice(c->device);
-    return cuda_fail(cudaStreamSynchronize(c->stream));
+    int* words[4] = {lcu_gemm_watchdog_addr(), lcu_attention_watchdog_addr(), lcu_conv_watchdog_addr(),
+                     lcu_int8_watchdog_addr()};
+    if (!c->wd_host) {
+        if (cudaMallocHost(&c->wd_host, 4 * sizeof(int)) != cudaSuccess) { cudaGetLastError(); c->wd_host = nullptr; }
+    }
+    if (c->wd_host)
+        for (int i = 0; i < 4; i++) {
+            c->wd_host[i] = 0;
+            if (words[i]) cudaMemcpyAsync(&c->wd_host[i], words[i], sizeof(int), cudaMemcpyDeviceToHost, c->stream);
+        }
+    cudaError_t ce = cudaStreamSynchronize(c->stream);
+    if (ce != cudaSuccess) return cuda_fail(ce);
+    bool tripped = false;
+    if (c->wd_host)
+        for (int i = 0; i < 4; i++)
+            if (c->wd_host[i] && words[i]) {
+                tripped = true;
+                cudaMemsetAsync(words[i], 0, sizeof(int), c->stream);
+            }
+    if (tripped) {
+        cudaStreamSynchronize(c->stream);
+        return fail(LANCIUS_ERROR_INTERNAL);
+    }
+    return LANCIUS_ERROR_OK;
 }
 
 int lcu_last_launch_count(lcu_ctx* c) { return c ? c->last_launches : 0; }
@@ -717,7 +745,7 @@ extern "C" lancius_error lcu_download(lcu_ctx* c, const lancius_node* n, void* h
         return fail(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
     }
     if (ce != cudaSuccess) return cuda_fail(ce);
-    return cuda_fail(cudaStreamSynchronize(c->stream));
+    return lcu_synchronize(c);    // also reports a tripped watchdog of the kernels that produced it
 }
 
 extern "C" lancius_error lcu_upload_bound_inputs(lcu_ctx* c) {

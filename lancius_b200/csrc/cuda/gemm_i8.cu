@@ -452,3 +452,9 @@ int lcu_int8_watchdog_read_and_clear(void) {
 }
 
 }  // extern "C"
+
+// Device address of this file's watchdog word on the current device (0 if unavailable).
+extern "C" int* lcu_int8_watchdog_addr(void) {
+    void* p = nullptr;
+    return cudaGetSymbolAddress(&p, g_i8_watchdog) == cudaSuccess ? static_cast<int*>(p) : nullptr;
+}

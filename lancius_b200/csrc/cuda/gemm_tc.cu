@@ -490,3 +490,30 @@ extern "C" lancius_error lcu_conv2d_tc(float* out, const float* in, const float*
     if (e == LANCIUS_ERROR_OK) e = lcu_check_cuda(cudaStreamSynchronize(st));
     return e;
 }
+
+// Device address of this file's watchdog word on the current device (0 if unavailable).
+extern "C" int* lcu_gemm_watchdog_addr(void) {
+    void* p = nullptr;
+    return cudaGetSymbolAddress(&p, g_gemm_watchdog) == cudaSuccess ? static_cast<int*>(p) : nullptr;
+}
+
+// Self-test of the timeout path: one thread waits on an mbarrier that nothing arrives on,
+// with a short poll limit, then records a timeout in this file's watchdog word exactly as
+// the GEMM's own waits do. No fault, no hang: the kernel returns after the limit.
+namespace {
+__global__ void k_watchdog_selftest(int where) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x != 0) return;
+    tc::mbar_init(&bar, 1);
+    tc::fence_barrier_init();
+    for (int i = 0; i < 1024; i++)
+        if (tc::mbar_try(&bar, 0)) return;       // phase 0 never completes
+    atomicCAS(&g_gemm_watchdog, 0, where);
+}
+}  // namespace
+
+extern "C" lancius_error lcu_watchdog_selftest(void* stream) {
+    k_watchdog_selftest<<<1, 32, 0, lcu_as_stream(stream)>>>(99);
+    lcu_note_launch();
+    return lcu_launch_status();
+}

@@ -91,6 +91,10 @@ lancius_error lcu_conv2d_int8_simt(float* out, const float* in, const int8_t* w,
                                    size_t H, size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad,
                                    int relu, float* amax_scratch, void* s);
 int lcu_int8_watchdog_read_and_clear(void);
+int* lcu_attention_watchdog_addr(void);
+int* lcu_conv_watchdog_addr(void);
+int* lcu_int8_watchdog_addr(void);
+int* lcu_gemm_watchdog_addr(void);
 void* lcu_scratch_acquire_gather(size_t bytes);
 void* lcu_scratch_acquire_decode(size_t bytes);
 lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, const float* k, const float* v, float* o,

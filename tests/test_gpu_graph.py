@@ -160,3 +160,16 @@ def test_basis_graph_lowered_on_gpu(device, orc):
     device.execute(s)
     want = orc.run_graph(lg, [m[y]])[m[y].id]
     assert_close(device.download(m[y]), want, 1e-4)
+
+
+def test_watchdog_reported_by_synchronize(device):
+    """A kernel whose bounded mbarrier wait gives up (nothing ever arrives) records it in the
+    watchdog word; lcu_synchronize reports LANCIUS_ERROR_INTERNAL once and clears it. The
+    GPU stays usable: the next execution runs normally."""
+    lib = device.lib
+    assert lib.lcu_synchronize(device.ptr) == 0
+    assert lib.lcu_watchdog_selftest(lib.lcu_stream(device.ptr)) == 0
+    assert lib.lcu_synchronize(device.ptr) == -10
+    assert lib.lcu_synchronize(device.ptr) == 0
+    b = configs.mlp(L.Graph(), batch=8, seed=5)
+    run_gpu(device, b)
