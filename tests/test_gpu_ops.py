@@ -87,7 +87,12 @@ def test_matmul_tf32_mode(lib, orc, M, K, N):
 
 
 @pytest.mark.parametrize("B,S,H,D,causal", [(1, 64, 1, 64, 1), (2, 100, 3, 64, 1), (8, 512, 8, 64, 1),
-                                            (2, 512, 12, 64, 0), (1, 200, 2, 128, 0), (1, 1, 1, 64, 1)])
+                                            (2, 512, 12, 64, 0), (1, 200, 2, 128, 0), (1, 1, 1, 64, 1),
+                                            # tcgen05 path: odd tile count (unpaired middle tile), a
+                                            # ragged last tile, and more tile pairs than SMs (several
+                                            # items per persistent CTA), causal and not
+                                            (1, 300, 3, 64, 1), (2, 129, 2, 64, 1), (10, 256, 20, 64, 1),
+                                            (10, 256, 20, 64, 0), (1, 1000, 2, 64, 1)])
 def test_attention(lib, orc, B, S, H, D, causal):
     q = data.normal(11, (B, S, H, D))
     k = data.normal(12, (B, S, H, D))
