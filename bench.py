@@ -363,9 +363,13 @@ def run_colsplit(args, rank, world, local_rank, n):
     sp = C.c_void_p(stream.cuda_stream)
     flush = torch.empty(L2_FLUSH_BYTES // 4, device="cuda")
 
+    # default: the fused kernel (epilogue stores into every rank's C over NVLink);
+    # LCU_COLSPLIT_NCCL=1 selects GEMM + ncclAllGather + repack
+    nccl_path = os.environ.get("LCU_COLSPLIT_NCCL") == "1"
+    fn = lib.lcu_gemm_colsplit if nccl_path else lib.lcu_gemm_colsplit_fused
+
     def step():
-        rc = lib.lcu_gemm_colsplit(comm, C.c_void_p(c.data_ptr()), C.c_void_p(a.data_ptr()), C.c_void_p(b.data_ptr()),
-                                   n, n, n, 0, sp)
+        rc = fn(comm, C.c_void_p(c.data_ptr()), C.c_void_p(a.data_ptr()), C.c_void_p(b.data_ptr()), n, n, n, 0, sp)
         assert rc == 0, rc
     for _ in range(args.warmup):
         step()
@@ -410,6 +414,7 @@ def run_colsplit(args, rank, world, local_rank, n):
             "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded U[-1,1), splitmix64)",
             "config": {"workload": f"gemm{n}_square_fp32_column_split_allgather", "mode": "fp32_exact",
+                       "exchange": "ncclAllGather + repack" if nccl_path else "fused: epilogue stores to peer C over NVLink",
                        "l2": "flushed between timed steps (256 MiB write)", "parallelism": f"column-split x{world}"},
             "roofline": {"bound": "tensor", "achieved": round(val / world, 2), "peak": pk["bf16_tflops"],
                          "unit": "TFLOP/s per GPU", "frac": round(val / world / pk["bf16_tflops"], 4), "traffic": None,
@@ -417,7 +422,9 @@ def run_colsplit(args, rank, world, local_rank, n):
             "cpu_baseline": None,
             "e2e": {"value": round(flops / (e2e_ms / 1e3 / args.steps) / 1e12, 3), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": int(a_h.nbytes + b_h.nbytes), "d2h_bytes_per_step": int(4 * n * n)},
-            "gpu_launches": 4 * args.steps, "clocks": clk,
+            # per step: A and B hi/lo splits, the GEMM, the split-K reduce when K > 8192, and
+            # the repack on the NCCL path
+            "gpu_launches": (3 + (1 if n > 8192 else 0) + (1 if nccl_path else 0)) * args.steps, "clocks": clk,
         }
         print(json.dumps(line))
     dist.destroy_process_group()

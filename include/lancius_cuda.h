@@ -139,6 +139,13 @@ int lcu_comm_size(const lcu_comm* comm);
  * b_slab [K, N / nranks]. N % nranks == 0. */
 lancius_error lcu_gemm_colsplit(lcu_comm* comm, float* c, const float* a, const float* b_slab, size_t M, size_t K,
                                 size_t N, int mode, void* stream);
+/* Same result, compute and exchange fused: this rank's GEMM epilogue stores its finished
+ * tiles into every rank's C over NVLink (C opened on each rank through CUDA IPC on the
+ * first call with a given C; that call is collective), then a 4-byte NCCL all-gather acts
+ * as the barrier. C must be 16-byte aligned device memory from cudaMalloc (or a pool on
+ * top of it); nranks <= 8. Returns after the stream has drained. */
+lancius_error lcu_gemm_colsplit_fused(lcu_comm* comm, float* c, const float* a, const float* b_slab, size_t M,
+                                      size_t K, size_t N, int mode, void* stream);
 
 /* lcu_matmul without device allocation (no counterpart in the reference, whose
  * kernels run on the host). For callers that may not call cudaMalloc once they are

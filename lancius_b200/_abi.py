@@ -164,6 +164,7 @@ B200_FUNCS = {
     "lcu_comm_abort": (None, [P]),
     "lcu_comm_size": (C.c_int, [P]),
     "lcu_gemm_colsplit": (C.c_int, [P, P, P, P, c_size, c_size, c_size, C.c_int, P]),
+    "lcu_gemm_colsplit_fused": (C.c_int, [P, P, P, P, c_size, c_size, c_size, C.c_int, P]),
     "lcu_matmul_noalloc": (C.c_int, [P, P, P, c_size, c_size, c_size, P, C.c_int, C.c_int, P]),
     "lcu_noalloc_scratch_capacity": (c_size, []),
 }

@@ -72,6 +72,12 @@ __global__ void k_repack_v4(float4* __restrict__ c, const float4* __restrict__ g
 struct lcu_comm {
     ncclComm_t comm;
     int nranks, rank, device;
+    // fused path: every rank's C, opened through CUDA IPC for the C pointer last used
+    float* c_key = nullptr;             // this rank's C those pointers belong to
+    size_t c_bytes = 0;
+    float* peer_c[8] = {};              // peer_c[r] = rank r's C (this rank's own at [rank])
+    void* peer_base[8] = {};            // IPC mappings to close
+    void* dev_buf = nullptr;            // small device buffer for handle exchange and the barrier
 };
 
 extern "C" lancius_error lcu_comm_unique_id(void* out, size_t bytes) {
@@ -98,8 +104,21 @@ extern "C" lcu_comm* lcu_comm_create(int nranks, int rank, const void* unique_id
     return c;
 }
 
+static void close_peers(lcu_comm* c) {
+    for (int r = 0; r < 8; r++) {
+        if (c->peer_base[r]) cudaIpcCloseMemHandle(c->peer_base[r]);
+        c->peer_base[r] = nullptr;
+        c->peer_c[r] = nullptr;
+    }
+    c->c_key = nullptr;
+    c->c_bytes = 0;
+}
+
 extern "C" void lcu_comm_destroy(lcu_comm* c) {
     if (!c) return;
+    cudaSetDevice(c->device);
+    close_peers(c);
+    if (c->dev_buf) cudaFree(c->dev_buf);
     nccl().comm_destroy(c->comm);
     delete c;
 }
@@ -139,4 +158,113 @@ extern "C" lancius_error lcu_gemm_colsplit(lcu_comm* comm, float* c, const float
         k_repack<<<lcu_blocks(M * N, 256 * 4), 256, 0, st>>>(c, gathered, g, M, ns);
     lcu_note_launch();
     return lcu_launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Fused variant: the GEMM's epilogue stores each finished tile of this rank's column
+// slab straight into every rank's row-major C over NVLink (peer pointers opened with
+// CUDA IPC once per C buffer), so there is no NCCL data movement and no repack; one
+// 4-byte ncclAllGather afterwards is the barrier that tells each rank its C is complete.
+
+namespace {
+typedef CUresult (*GetRangeFn)(CUdeviceptr*, size_t*, CUdeviceptr);
+GetRangeFn get_range_fn() {
+    static GetRangeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<GetRangeFn>(p);
+    });
+    return fn;
+}
+struct PeerRecord {               // what each rank publishes about its C
+    cudaIpcMemHandle_t handle;    // of the allocation that contains C
+    uint64_t offset;              // C - allocation base
+    uint64_t usable;              // allocation bytes from C on
+    uint64_t pad[6];
+};
+static_assert(sizeof(PeerRecord) % 16 == 0, "record size");
+}  // namespace
+
+// Opens every rank's C for this C pointer (collective: all ranks call with their own C).
+static lancius_error open_peers(lcu_comm* comm, float* c, size_t bytes, cudaStream_t st) {
+    if (comm->c_key == c && comm->c_bytes >= bytes) return LANCIUS_ERROR_OK;
+    close_peers(comm);
+    GetRangeFn range = get_range_fn();
+    if (!range) { lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP; }
+    const int g = comm->nranks;
+    if (!comm->dev_buf && cudaMalloc(&comm->dev_buf, 8 * sizeof(PeerRecord) + 256) != cudaSuccess) {
+        cudaGetLastError(); lancius_set_error(LANCIUS_ERROR_OOM); return LANCIUS_ERROR_OOM;
+    }
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, (CUdeviceptr)c) != CUDA_SUCCESS) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    PeerRecord mine{};
+    if (cudaIpcGetMemHandle(&mine.handle, (void*)base) != cudaSuccess) { cudaGetLastError(); lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    mine.offset = (uint64_t)((CUdeviceptr)c - base);
+    mine.usable = (uint64_t)(size - mine.offset);
+    PeerRecord all[8];
+    char* d = static_cast<char*>(comm->dev_buf);
+    if (cudaMemcpyAsync(d + comm->rank * sizeof(PeerRecord), &mine, sizeof(PeerRecord), cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return lcu_check_cuda(cudaGetLastError());
+    ncclResult_t r = nccl().all_gather(d + comm->rank * sizeof(PeerRecord), d, sizeof(PeerRecord), ncclInt8, comm->comm, st);
+    if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather (IPC handles)");
+    if (cudaMemcpyAsync(all, d, g * sizeof(PeerRecord), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess)
+        return lcu_check_cuda(cudaGetLastError());
+    for (int k = 0; k < g; k++) {
+        if (all[k].usable < bytes) { close_peers(comm); lancius_set_error(LANCIUS_ERROR_SHAPE_MISMATCH); return LANCIUS_ERROR_SHAPE_MISMATCH; }
+        if (k == comm->rank) { comm->peer_c[k] = c; continue; }
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, all[k].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError(); close_peers(comm); lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL;
+        }
+        comm->peer_base[k] = p;
+        comm->peer_c[k] = reinterpret_cast<float*>(static_cast<char*>(p) + all[k].offset);
+    }
+    comm->c_key = c;
+    comm->c_bytes = bytes;
+    return LANCIUS_ERROR_OK;
+}
+
+extern "C" lancius_error lcu_gemm_colsplit_fused(lcu_comm* comm, float* c, const float* a, const float* b_slab, size_t M,
+                                                size_t K, size_t N, int mode, void* stream) {
+    if (!comm || !c || !a || !b_slab) { lancius_set_error(LANCIUS_ERROR_NULL_PTR); return LANCIUS_ERROR_NULL_PTR; }
+    const int g = comm->nranks;
+    if (g > 8 || N % (size_t)g || M == 0 || K == 0 || ((uintptr_t)c & 15)) {
+        lancius_set_error(LANCIUS_ERROR_SHAPE_MISMATCH); return LANCIUS_ERROR_SHAPE_MISMATCH;
+    }
+    if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32) { lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_DTYPE); return LANCIUS_ERROR_UNSUPPORTED_DTYPE; }
+    const size_t ns = N / g;
+    cudaStream_t st = lcu_as_stream(stream);
+    lancius_error e = open_peers(comm, c, M * N * sizeof(float), st);
+    if (e != LANCIUS_ERROR_OK) return e;
+    const int passes = mode == LCU_MODE_TF32 ? 1 : 3;
+    const size_t need = lcu_gemm_tc_scratch_bytes(M, ns, K, 1, 1, 1, passes) + 256;
+    char* scratch = static_cast<char*>(lcu_scratch_acquire(need));
+    if (!scratch) { lancius_set_error(LANCIUS_ERROR_OOM); return LANCIUS_ERROR_OOM; }
+    LcuGemmGroup* d_group = reinterpret_cast<LcuGemmGroup*>(scratch + need - 256);
+    LcuGemmGroup h{a, b_slab, comm->peer_c[comm->rank], nullptr, nullptr};
+    cudaError_t ce = cudaMemcpyAsync(d_group, &h, sizeof(h), cudaMemcpyHostToDevice, st);
+    if (ce != cudaSuccess) return lcu_check_cuda(ce);
+    LcuTcGemmPlan p;
+    e = lcu_gemm_tc_prepare(&p, scratch, M, ns, K, 1, 1, 1, passes);
+    if (e != LANCIUS_ERROR_OK) return e;
+    LcuColDest dst{};
+    for (int k = 0; k < g; k++) dst.ptr[k] = comm->peer_c[k];
+    dst.n_dst = g;
+    dst.ldc = N;
+    dst.col_off = (size_t)comm->rank * ns;
+    e = lcu_gemm_tc_run_dst(&p, d_group, LCU_EPI_NONE, dst, stream);
+    if (e != LANCIUS_ERROR_OK) return e;
+    if (g > 1) {   // barrier: completes once every rank's kernels (and their peer stores) are done
+        char* d = static_cast<char*>(comm->dev_buf) + 8 * sizeof(PeerRecord);
+        ncclResult_t r = nccl().all_gather(d + comm->rank * 4, d, 4, ncclInt8, comm->comm, st);
+        if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather (barrier)");
+    }
+    // the host record of the group table must stay valid until the copy ran
+    return lcu_check_cuda(cudaStreamSynchronize(st));
 }

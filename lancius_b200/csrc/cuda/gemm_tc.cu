@@ -44,11 +44,12 @@ struct Smem {
     int consumed;
 };
 
+template <bool DST>   // DST: the epilogue stores into LcuColDest's destinations
 __global__ void __launch_bounds__(THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
           const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
           const LcuGemmGroup* __restrict__ groups, int M, int N, int K, int epi, int passes,
-          int splits, int kchunk, float* __restrict__ partial, int conv_hw) {
+          int splits, int kchunk, float* __restrict__ partial, int conv_hw, LcuColDest dst) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Smem* sm = reinterpret_cast<Smem*>(tiles + STAGES * STAGE_BYTES);
@@ -178,7 +179,33 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
                     }
                     continue;
                 }
-                float* dst = gr.c + (size_t)row * N + col0;
+                if (DST && splits == 1) {
+                    // fused all-gather: the finished values go straight to every rank's C
+                    float x[32];
+#pragma unroll
+                    for (int j = 0; j < 32; j++) {
+                        float y = v[j];
+                        if (col0 + j < N) {
+                            if (gr.bias) y += __ldg(gr.bias + col0 + j);
+                            y = lcu_apply_epi(y, epi_here);
+                            if (gr.resid) y += gr.resid[(size_t)row * N + col0 + j];
+                        }
+                        x[j] = y;
+                    }
+                    const size_t o = (size_t)row * dst.ldc + dst.col_off + col0;
+                    const bool v4 = col0 + 32 <= N && dst.ldc % 4 == 0 && o % 4 == 0;
+                    for (int q = 0; q < dst.n_dst; q++) {
+                        float* d = dst.ptr[q] + o;
+                        if (v4) {
+#pragma unroll
+                            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(d + j) = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
+                        } else {
+                            for (int j = 0; j < 32 && col0 + j < N; j++) d[j] = x[j];
+                        }
+                    }
+                    continue;
+                }
+                float* dst_p = gr.c + (size_t)row * N + col0;
                 const float* res = gr.resid ? gr.resid + (size_t)row * N + col0 : nullptr;
                 if (vec && col0 + 32 <= N) {
 #pragma unroll
@@ -195,7 +222,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
                             float4 r = *reinterpret_cast<const float4*>(res + j);
                             o.x += r.x; o.y += r.y; o.z += r.z; o.w += r.w;
                         }
-                        *reinterpret_cast<float4*>(dst + j) = o;
+                        *reinterpret_cast<float4*>(dst_p + j) = o;
                     }
                 } else {
                     for (int j = 0; j < 32 && col0 + j < N; j++) {
@@ -203,11 +230,12 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
                         if (gr.bias) x += __ldg(gr.bias + col0 + j);
                         x = lcu_apply_epi(x, epi_here);
                         if (res) x += res[j];
-                        dst[j] = x;
+                        dst_p[j] = x;
                     }
                 }
             }
             }   // half
+            if (DST) __threadfence_system();   // peer stores complete before the kernel does
         }
     }
 
@@ -275,7 +303,7 @@ __global__ void k_im2col_split(const LcuGemmGroup* __restrict__ groups, LcuConvS
 
 // out = act(sum over splits of the partials + bias) + resid, splits summed in order
 __global__ void k_splitk_reduce(const LcuGemmGroup* __restrict__ groups, const float* __restrict__ partial, int splits,
-                                size_t M, size_t N, int epi, size_t conv_hw) {
+                                size_t M, size_t N, int epi, size_t conv_hw, LcuColDest dst) {
     const LcuGemmGroup gr = groups[blockIdx.y];
     const float* p = partial + (size_t)blockIdx.y * splits * M * N;
     size_t n = M * N;
@@ -285,13 +313,17 @@ __global__ void k_splitk_reduce(const LcuGemmGroup* __restrict__ groups, const f
         if (gr.bias) acc += __ldg(gr.bias + i % N);
         acc = lcu_apply_epi(acc, epi);
         if (gr.resid) acc += gr.resid[i];
-        if (conv_hw) {
+        if (dst.n_dst > 0) {
+            const size_t o = (i / N) * dst.ldc + dst.col_off + i % N;
+            for (int q = 0; q < dst.n_dst; q++) dst.ptr[q][o] = acc;
+        } else if (conv_hw) {
             size_t r = i / N, c = i % N;
             gr.c[(c / conv_hw) * M * conv_hw + r * conv_hw + c % conv_hw] = acc;
         } else {
             gr.c[i] = acc;
         }
     }
+    if (dst.n_dst > 0) __threadfence_system();
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
@@ -372,12 +404,19 @@ extern "C" lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, si
 }
 
 extern "C" lancius_error lcu_gemm_tc_run(const LcuTcGemmPlan* p, const LcuGemmGroup* d_groups, int epi, void* stream) {
+    LcuColDest none{};
+    return lcu_gemm_tc_run_dst(p, d_groups, epi, none, stream);
+}
+
+extern "C" lancius_error lcu_gemm_tc_run_dst(const LcuTcGemmPlan* p, const LcuGemmGroup* d_groups, int epi,
+                                             LcuColDest dst, void* stream) {
     static bool configured[64] = {};     // the attribute is per device
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
     if (!configured[dev]) {
-        if (cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+        if (cudaFuncSetAttribute(k_gemm_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemm_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
             return lcu_launch_status();
         configured[dev] = true;
     }
@@ -395,14 +434,20 @@ extern "C" lancius_error lcu_gemm_tc_run(const LcuTcGemmPlan* p, const LcuGemmGr
         lcu_note_launch();
     }
     dim3 grid((unsigned)((p->N + BN - 1) / BN), (unsigned)((p->M + BM - 1) / BM), (unsigned)(p->G * p->splits));
-    k_gemm_tc<<<grid, THREADS, SMEM_BYTES, st>>>(p->a_hi, p->a_lo, p->b_hi, p->b_lo, d_groups, (int)p->M, (int)p->N,
-                                                 (int)p->K, epi, p->passes,
-                                                 p->splits, p->kchunk, p->partial, p->conv.n ? p->conv.ho * p->conv.wo : 0);
+    if (dst.n_dst > 0)
+        k_gemm_tc<true><<<grid, THREADS, SMEM_BYTES, st>>>(p->a_hi, p->a_lo, p->b_hi, p->b_lo, d_groups, (int)p->M, (int)p->N,
+                                                           (int)p->K, epi, p->passes, p->splits, p->kchunk, p->partial,
+                                                           p->conv.n ? p->conv.ho * p->conv.wo : 0, dst);
+    else
+        k_gemm_tc<false><<<grid, THREADS, SMEM_BYTES, st>>>(p->a_hi, p->a_lo, p->b_hi, p->b_lo, d_groups, (int)p->M, (int)p->N,
+                                                            (int)p->K, epi, p->passes, p->splits, p->kchunk, p->partial,
+                                                            p->conv.n ? p->conv.ho * p->conv.wo : 0, dst);
     lcu_note_launch();
     if (p->splits > 1) {
         k_splitk_reduce<<<dim3(lcu_blocks(p->M * p->N, 256 * 4, 148 * 8), p->G), 256, 0, st>>>(d_groups, p->partial, p->splits,
                                                                                                p->M, p->N, epi,
-                                                                                               p->conv.n ? (size_t)p->conv.ho * p->conv.wo : 0);
+                                                                                               p->conv.n ? (size_t)p->conv.ho * p->conv.wo : 0,
+                                                                                               dst);
         lcu_note_launch();
     }
     return lcu_launch_status();

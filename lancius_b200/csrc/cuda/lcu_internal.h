@@ -21,6 +21,11 @@ struct LcuRowGroup { float* out; const float* in; const float* gamma; const floa
 
 struct LcuConvShape { int n, ci, h, w, co, kh, kw, stride, pad, ho, wo; };   // n == 0: not a conv
 
+// Extra destinations of a GEMM result (the column-split GEMM's fused all-gather): element
+// (m, n) of the [M, N] product is stored at ptr[i][m * ldc + col_off + n] for every i < n_dst,
+// local and peer (NVLink) memory alike, instead of into the group's own C.
+struct LcuColDest { float* ptr[8]; int n_dst; size_t ldc, col_off; };
+
 // A prepared tensor-core GEMM: TMA maps over the hi/lo scratch copies of A and B.
 struct LcuTcGemmPlan {
     CUtensorMap a_hi, a_lo, b_hi, b_lo;
@@ -37,6 +42,8 @@ size_t lcu_gemm_tc_scratch_bytes(size_t M, size_t N, size_t K, int G, int Ga, in
 lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, size_t M, size_t N, size_t K, int G, int Ga, int Gb,
                                   int passes);
 lancius_error lcu_gemm_tc_run(const LcuTcGemmPlan* p, const LcuGemmGroup* d_groups, int epi, void* stream);
+lancius_error lcu_gemm_tc_run_dst(const LcuTcGemmPlan* p, const LcuGemmGroup* d_groups, int epi, LcuColDest dst,
+                                  void* stream);
 lancius_error lcu_gemm_simt_grouped(const LcuGemmGroup* d_groups, int count, size_t M, size_t N, size_t K, int epi,
                                     void* stream);
 lancius_error lcu_gemm_simt(float* c, const float* a, const float* b, size_t M, size_t K, size_t N, const float* bias,

@@ -1,5 +1,6 @@
-"""Column-split GEMM (lcu_gemm_colsplit) against the FP64 oracle: one rank on one GPU
-here, and 2 ranks (one process per GPU, NCCL all-gather) when 2 GPUs are visible."""
+"""Column-split GEMM (lcu_gemm_colsplit, NCCL all-gather; lcu_gemm_colsplit_fused, epilogue
+stores into every rank's C over NVLink) against the FP64 oracle: one rank on one GPU here,
+and 2 ranks (one process per GPU) when 2 GPUs are visible."""
 import ctypes as C
 import multiprocessing as mproc
 
@@ -12,14 +13,15 @@ from lancius_b200 import MODE_FP32_EXACT, data, load
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
 
-M, K, N = 384, 1536, 1024
+SHAPES = {"plain": (384, 1536, 1024), "splitk": (128, 9000, 256)}   # K > 8192: split-K reduce stores
 
 
-def operands():
+def operands(M, K, N):
     return data.uniform(81, (M, K), -1, 1), data.uniform(82, (K, N), -1, 1)
 
 
-def _rank(rank, world, uid, q):
+def _rank(rank, world, uid, q, fused=False, shape="plain"):
+    M, K, N = SHAPES[shape]
     import torch
     from lancius_b200 import load as _load
     lib = _load()
@@ -28,25 +30,30 @@ def _rank(rank, world, uid, q):
     if not comm:
         q.put((rank, None, lib.lancius_get_error()))
         return
-    a, b = operands()
+    a, b = operands(M, K, N)
     ns = N // world
     da = torch.tensor(a.astype(np.float32), device="cuda")
     db = torch.tensor(np.ascontiguousarray(b[:, rank * ns:(rank + 1) * ns]).astype(np.float32), device="cuda")
     c = torch.empty((M, N), device="cuda")
-    rc = lib.lcu_gemm_colsplit(comm, C.c_void_p(c.data_ptr()), C.c_void_p(da.data_ptr()), C.c_void_p(db.data_ptr()),
-                               M, K, N, MODE_FP32_EXACT, None)
-    torch.cuda.synchronize()
+    fn = lib.lcu_gemm_colsplit_fused if fused else lib.lcu_gemm_colsplit
+    rc = 0
+    for _ in range(2 if fused else 1):      # the fused path's second call reuses the opened peer C
+        c.fill_(float("nan"))
+        torch.cuda.synchronize()
+        rc = rc or fn(comm, C.c_void_p(c.data_ptr()), C.c_void_p(da.data_ptr()), C.c_void_p(db.data_ptr()),
+                      M, K, N, MODE_FP32_EXACT, None)
+        torch.cuda.synchronize()
     q.put((rank, c.cpu().numpy() if rc == 0 else None, rc))
     lib.lcu_comm_destroy(comm)
 
 
-def run_ranks(world):
+def run_ranks(world, fused=False, shape="plain"):
     lib = load()
     uid = C.create_string_buffer(128)
     assert lib.lcu_comm_unique_id(uid, 128) == 0
     ctx = mproc.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(r, world, uid.raw, q)) for r in range(world)]
+    procs = [ctx.Process(target=_rank, args=(r, world, uid.raw, q, fused, shape)) for r in range(world)]
     for p in procs:
         p.start()
     out = [q.get(timeout=300) for _ in range(world)]
@@ -56,11 +63,12 @@ def run_ranks(world):
 
 
 @pytest.mark.parametrize("world", [1, 2])
-def test_colsplit_matches_oracle(orc, world):
+@pytest.mark.parametrize("fused,shape", [(False, "plain"), (True, "plain"), (True, "splitk")])
+def test_colsplit_matches_oracle(orc, world, fused, shape):
     if not torch.cuda.is_available() or torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
-    a, b = operands()
+    a, b = operands(*SHAPES[shape])
     ref = orc.matmul(a, b)
-    for rank, c, rc in run_ranks(world):
+    for rank, c, rc in run_ranks(world, fused, shape):
         assert rc == 0, f"rank {rank}: error {rc}"
         assert_close(c, ref, 1e-4)
