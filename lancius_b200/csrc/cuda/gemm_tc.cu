@@ -149,92 +149,81 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
                 gr.bias = nullptr; gr.resid = nullptr;
             }
             const int epi_here = splits > 1 ? LCU_EPI_NONE : epi;
+            // Each warp owns 32 TMEM lanes (rows). Per 32-column chunk it stages the 32x32
+            // block in shared memory (the drained pipeline buffers) and writes it back by
+            // rows: every store instruction covers whole 128-byte row segments (coalesced),
+            // and the loop body (bias, activation, residual, destination) stays small
+            // instead of being unrolled 32-fold.
             const int q = warp & 3;                    // TMEM lane quadrant of this warp
+            float* sb = reinterpret_cast<float*>(tiles) + (size_t)q * 32 * 36;
+            // float4 path: every pointer 16-byte aligned and rows a multiple of 4 floats
+            const bool v4 = N % 4 == 0 && !conv_hw && ((reinterpret_cast<uintptr_t>(gr.c) | reinterpret_cast<uintptr_t>(gr.resid) |
+                                                        reinterpret_cast<uintptr_t>(gr.bias)) & 15) == 0 &&
+                            (!DST || (dst.ldc % 4 == 0 && dst.col_off % 4 == 0));
             for (int half = 0; half < 2; half++) {
-            const int row = m0 + half * 128 + 32 * q + lane;
-            if (m0 + half * 128 >= M) break;           // warp-uniform
-            const bool vec = (N % 4 == 0) && ((reinterpret_cast<uintptr_t>(gr.c) & 15) == 0) &&
-                             (!gr.resid || (reinterpret_cast<uintptr_t>(gr.resid) & 15) == 0);
-            for (int c = 0; c < BN; c += 32) {
-                if (n0 + c >= N) break;                // warp-uniform
-                float v[32];
-                tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * BN + c), v);
-                if (LCU_GEMM_DEBUG && blockIdx.x == 0 && blockIdx.y == 0 && c == 0 && (lane == 0 || lane == 1) && q == 0)
-                    printf("row %d v=%g %g %g %g %g %g\n", row, v[0], v[1], v[2], v[3], v[4], v[5]);
-                if (row >= M) continue;
-                const int col0 = n0 + c;
-                if (conv_hw && splits == 1) {
-                    // implicit-GEMM conv: row = output channel, column = n*HoWo + pixel -> NCHW
-                    if (conv_hw % 32 == 0 && col0 + 32 <= N && (reinterpret_cast<uintptr_t>(gr.c) & 15) == 0) {
-                        float* d = gr.c + (size_t)(col0 / conv_hw) * M * conv_hw + (size_t)row * conv_hw + col0 % conv_hw;
+                const int row0 = m0 + half * 128 + 32 * q;
+                if (m0 + half * 128 >= M) break;       // warp-uniform
+                for (int c = 0; c < BN; c += 32) {
+                    if (n0 + c >= N) break;            // warp-uniform
+                    float v[32];
+                    tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * BN + c), v);
 #pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *reinterpret_cast<float4*>(d + j) = make_float4(lcu_apply_epi(v[j], epi_here), lcu_apply_epi(v[j + 1], epi_here),
-                                                                            lcu_apply_epi(v[j + 2], epi_here), lcu_apply_epi(v[j + 3], epi_here));
+                    for (int j = 0; j < 32; j += 4)
+                        *reinterpret_cast<float4*>(sb + lane * 36 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    __syncwarp();
+                    if (v4) {
+                        // 8 lanes per row, 4 columns each: 4 rows (128-byte segments) per step
+                        const int col = n0 + c + 4 * (lane & 7);
+                        if (col < N) {
+                            const float4 bv = gr.bias ? __ldg(reinterpret_cast<const float4*>(gr.bias + col))
+                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 2
+                            for (int it = 0; it < 8; it++) {
+                                const int r = 4 * it + (lane >> 3), row = row0 + r;
+                                if (row >= M) break;
+                                float4 x = *reinterpret_cast<const float4*>(sb + r * 36 + 4 * (lane & 7));
+                                x.x = lcu_apply_epi(x.x + bv.x, epi_here); x.y = lcu_apply_epi(x.y + bv.y, epi_here);
+                                x.z = lcu_apply_epi(x.z + bv.z, epi_here); x.w = lcu_apply_epi(x.w + bv.w, epi_here);
+                                if (gr.resid) {
+                                    const float4 rv = *reinterpret_cast<const float4*>(gr.resid + (size_t)row * N + col);
+                                    x.x += rv.x; x.y += rv.y; x.z += rv.z; x.w += rv.w;
+                                }
+                                if (DST && splits == 1) {
+                                    const size_t o = (size_t)row * dst.ldc + dst.col_off + col;
+                                    for (int k = 0; k < dst.n_dst; k++) *reinterpret_cast<float4*>(dst.ptr[k] + o) = x;
+                                } else {
+                                    *reinterpret_cast<float4*>(gr.c + (size_t)row * N + col) = x;
+                                }
+                            }
+                        }
                     } else {
-                        for (int j = 0; j < 32 && col0 + j < N; j++) {
-                            const int cc = col0 + j;
-                            gr.c[(size_t)(cc / conv_hw) * M * conv_hw + (size_t)row * conv_hw + cc % conv_hw] = lcu_apply_epi(v[j], epi_here);
+                        // any shape: lane j takes column j of each row (coalesced per row)
+                        const int col = n0 + c + lane;
+                        if (col < N) {
+                            const float bv = gr.bias ? __ldg(gr.bias + col) : 0.f;
+#pragma unroll 4
+                            for (int r = 0; r < 32; r++) {
+                                const int row = row0 + r;
+                                if (row >= M) break;
+                                float x = lcu_apply_epi(sb[r * 36 + lane] + bv, epi_here);
+                                if (conv_hw && splits == 1) {
+                                    // implicit-GEMM conv: row = output channel, column = n*HoWo + pixel -> NCHW
+                                    gr.c[(size_t)(col / conv_hw) * M * conv_hw + (size_t)row * conv_hw + col % conv_hw] = x;
+                                    continue;
+                                }
+                                if (gr.resid) x += gr.resid[(size_t)row * N + col];
+                                if (DST && splits == 1) {   // fused all-gather: straight into every rank's C
+                                    const size_t o = (size_t)row * dst.ldc + dst.col_off + col;
+                                    for (int k = 0; k < dst.n_dst; k++) dst.ptr[k][o] = x;
+                                } else {
+                                    gr.c[(size_t)row * N + col] = x;
+                                }
+                            }
                         }
                     }
-                    continue;
-                }
-                if (DST && splits == 1) {
-                    // fused all-gather: the finished values go straight to every rank's C
-                    float x[32];
-#pragma unroll
-                    for (int j = 0; j < 32; j++) {
-                        float y = v[j];
-                        if (col0 + j < N) {
-                            if (gr.bias) y += __ldg(gr.bias + col0 + j);
-                            y = lcu_apply_epi(y, epi_here);
-                            if (gr.resid) y += gr.resid[(size_t)row * N + col0 + j];
-                        }
-                        x[j] = y;
-                    }
-                    const size_t o = (size_t)row * dst.ldc + dst.col_off + col0;
-                    const bool v4 = col0 + 32 <= N && dst.ldc % 4 == 0 && o % 4 == 0;
-                    for (int q = 0; q < dst.n_dst; q++) {
-                        float* d = dst.ptr[q] + o;
-                        if (v4) {
-#pragma unroll
-                            for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(d + j) = make_float4(x[j], x[j + 1], x[j + 2], x[j + 3]);
-                        } else {
-                            for (int j = 0; j < 32 && col0 + j < N; j++) d[j] = x[j];
-                        }
-                    }
-                    continue;
-                }
-                float* dst_p = gr.c + (size_t)row * N + col0;
-                const float* res = gr.resid ? gr.resid + (size_t)row * N + col0 : nullptr;
-                if (vec && col0 + 32 <= N) {
-#pragma unroll
-                    for (int j = 0; j < 32; j += 4) {
-                        float4 o;
-                        float* ov = reinterpret_cast<float*>(&o);
-#pragma unroll
-                        for (int t = 0; t < 4; t++) {
-                            float x = v[j + t];
-                            if (gr.bias) x += __ldg(gr.bias + col0 + j + t);
-                            ov[t] = lcu_apply_epi(x, epi_here);
-                        }
-                        if (res) {
-                            float4 r = *reinterpret_cast<const float4*>(res + j);
-                            o.x += r.x; o.y += r.y; o.z += r.z; o.w += r.w;
-                        }
-                        *reinterpret_cast<float4*>(dst_p + j) = o;
-                    }
-                } else {
-                    for (int j = 0; j < 32 && col0 + j < N; j++) {
-                        float x = v[j];
-                        if (gr.bias) x += __ldg(gr.bias + col0 + j);
-                        x = lcu_apply_epi(x, epi_here);
-                        if (res) x += res[j];
-                        dst_p[j] = x;
-                    }
+                    __syncwarp();
                 }
             }
-            }   // half
             if (DST) __threadfence_system();   // peer stores complete before the kernel does
         }
     }
