@@ -144,27 +144,40 @@ k_conv_tc(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
         // ---------------- epilogue: rows = output channels, columns = pixels ----------------
         if (tc::mbar_wait(&sm->accum, 0, abort, &g_conv_watchdog, 3)) {
             tc::tc_fence_after();
+            // Each warp owns 32 output channels (TMEM lanes). Per 32-pixel chunk the 32x32
+            // block is staged in the drained pipeline smem and stored by channel rows: 8
+            // lanes per row x 4 pixels, so every store instruction writes whole 128-byte
+            // segments (coalesced) from a compact loop.
             const int q = warp & 3;
+            float* sb = reinterpret_cast<float*>(tiles) + (size_t)q * 32 * 36;
+            // the tile's pixels are consecutive in the image: rows ho0.. of width Wo
+            const int valid = min(bn, (a.ho - ho0) * a.wo);
+            const bool v4 = hw % 4 == 0 && ((size_t)ho0 * a.wo) % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
             for (int half = 0; half < a.halves; half++) {
-                const int co = m0 + half * 128 + 32 * q + lane;
-                // the tile's pixels are consecutive in the image: rows ho0.. of width Wo
-                const int valid = min(bn, (a.ho - ho0) * a.wo);
-                float* orow = out + ((size_t)img * a.co + co) * hw + (size_t)ho0 * a.wo;
-                const bool vec = (reinterpret_cast<uintptr_t>(orow) & 15) == 0;
+                const int co0 = m0 + half * 128 + 32 * q;
                 for (int c = 0; c < bn; c += 32) {
                     float v[32];
                     tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * BN + c), v);
-                    if (co >= a.co) continue;
-                    if (a.relu) {
 #pragma unroll
-                        for (int j = 0; j < 32; j++) v[j] = v[j] > 0.f ? v[j] : 0.f;
+                    for (int j = 0; j < 32; j += 4)
+                        *reinterpret_cast<float4*>(sb + lane * 36 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+                    __syncwarp();
+                    const int px = c + 4 * (lane & 7);
+#pragma unroll 2
+                    for (int it = 0; it < 8; it++) {
+                        const int r = 4 * it + (lane >> 3), co = co0 + r;
+                        if (co >= a.co || px >= valid) continue;
+                        float4 x = *reinterpret_cast<const float4*>(sb + r * 36 + 4 * (lane & 7));
+                        if (a.relu) { x.x = fmaxf(x.x, 0.f); x.y = fmaxf(x.y, 0.f); x.z = fmaxf(x.z, 0.f); x.w = fmaxf(x.w, 0.f); }
+                        float* o = out + ((size_t)img * a.co + co) * hw + (size_t)ho0 * a.wo + px;
+                        if (v4 && px + 4 <= valid) {
+                            *reinterpret_cast<float4*>(o) = x;
+                        } else {
+                            const float xv[4] = {x.x, x.y, x.z, x.w};
+                            for (int t = 0; t < 4 && px + t < valid; t++) o[t] = xv[t];
+                        }
                     }
-                    if (vec && c + 32 <= valid) {
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(orow + c + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                    } else {
-                        for (int j = 0; j < 32 && c + j < valid; j++) orow[c + j] = v[j];
-                    }
+                    __syncwarp();
                 }
             }
         }

@@ -112,25 +112,35 @@ k_gemm_i8(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtens
         if (ok) tc::mma_commit(&sm->accum);
     }
     __syncwarp();
-    // epilogue: every warp reads its 32 TMEM lanes (= rows)
+    // epilogue: every warp reads its 32 TMEM lanes (= rows), stages each 32x32 int32 block
+    // in the drained pipeline smem and stores it by rows (lane j: column j), coalesced
     if (tc::mbar_wait(&sm->accum, 0, abort, &g_i8_watchdog, 3)) {
         tc::tc_fence_after();
         const double scale = act_scale(amax, scale_w);
-        for (int half = 0; half < 2; half++)
-        for (int c = 0; c < BN; c += 32) {
-            const int row = m0 + half * 128 + 32 * warp + lane;
-            if (n0 + c >= N || m0 + half * 128 >= M) break;   // warp-uniform
-            float v[32];
-            tc::tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(half * BN + c), v);
-            if (row >= M) continue;
+        int* sb = reinterpret_cast<int*>(tiles) + (size_t)warp * 32 * 33;
+        for (int half = 0; half < 2; half++) {
+            const int row0 = m0 + half * 128 + 32 * warp;
+            if (m0 + half * 128 >= M) break;                   // warp-uniform
+            for (int c = 0; c < BN; c += 32) {
+                if (n0 + c >= N) break;                        // warp-uniform
+                float v[32];
+                tc::tmem_ld32(tmem + ((uint32_t)(32 * warp) << 16) + (uint32_t)(half * BN + c), v);
 #pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const int col = n0 + c + j;
-                if (col >= N) break;
-                float x = (float)((double)__float_as_int(v[j]) * scale);
-                if (relu && x < 0.f) x = 0.f;
-                if (conv_hw) out[(size_t)(col / conv_hw) * M * conv_hw + (size_t)row * conv_hw + col % conv_hw] = x;
-                else out[(size_t)row * N + col] = x;
+                for (int j = 0; j < 32; j++) sb[lane * 33 + j] = __float_as_int(v[j]);
+                __syncwarp();
+                const int col = n0 + c + lane;
+                if (col < N) {
+#pragma unroll 4
+                    for (int r = 0; r < 32; r++) {
+                        const int row = row0 + r;
+                        if (row >= M) break;
+                        float x = (float)((double)sb[r * 33 + lane] * scale);
+                        if (relu && x < 0.f) x = 0.f;
+                        if (conv_hw) out[(size_t)(col / conv_hw) * M * conv_hw + (size_t)row * conv_hw + col % conv_hw] = x;
+                        else out[(size_t)row * N + col] = x;
+                    }
+                }
+                __syncwarp();
             }
         }
     }
