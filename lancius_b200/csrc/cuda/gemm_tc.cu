@@ -160,11 +160,27 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
             const bool v4 = N % 4 == 0 && !conv_hw && ((reinterpret_cast<uintptr_t>(gr.c) | reinterpret_cast<uintptr_t>(gr.resid) |
                                                         reinterpret_cast<uintptr_t>(gr.bias)) & 15) == 0 &&
                             (!DST || (dst.ldc % 4 == 0 && dst.col_off % 4 == 0));
+            // residual rows of a chunk, 8 per lane (the float4 path's lane mapping); the next
+            // chunk's are fetched while this one is stored, so HBM latency is paid once per half
+            auto load_res = [&](int row0, int cc, float4 (&rv)[8]) {
+                const int col = n0 + cc + 4 * (lane & 7);
+#pragma unroll
+                for (int it = 0; it < 8; it++) {
+                    const int row = row0 + 4 * it + (lane >> 3);
+                    rv[it] = (gr.resid && v4 && row < M && col < N)
+                                 ? *reinterpret_cast<const float4*>(gr.resid + (size_t)row * N + col)
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            };
             for (int half = 0; half < 2; half++) {
                 const int row0 = m0 + half * 128 + 32 * q;
                 if (m0 + half * 128 >= M) break;       // warp-uniform
+                float4 rv[8];
+                load_res(row0, 0, rv);
                 for (int c = 0; c < BN; c += 32) {
                     if (n0 + c >= N) break;            // warp-uniform
+                    float4 rn[8];
+                    load_res(row0, c + 32, rn);        // next chunk's residuals in flight
                     float v[32];
                     tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * BN + c), v);
 #pragma unroll
@@ -177,17 +193,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
                         if (col < N) {
                             const float4 bv = gr.bias ? __ldg(reinterpret_cast<const float4*>(gr.bias + col))
                                                       : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 2
+#pragma unroll
                             for (int it = 0; it < 8; it++) {
                                 const int r = 4 * it + (lane >> 3), row = row0 + r;
                                 if (row >= M) break;
                                 float4 x = *reinterpret_cast<const float4*>(sb + r * 36 + 4 * (lane & 7));
                                 x.x = lcu_apply_epi(x.x + bv.x, epi_here); x.y = lcu_apply_epi(x.y + bv.y, epi_here);
                                 x.z = lcu_apply_epi(x.z + bv.z, epi_here); x.w = lcu_apply_epi(x.w + bv.w, epi_here);
-                                if (gr.resid) {
-                                    const float4 rv = *reinterpret_cast<const float4*>(gr.resid + (size_t)row * N + col);
-                                    x.x += rv.x; x.y += rv.y; x.z += rv.z; x.w += rv.w;
-                                }
+                                x.x += rv[it].x; x.y += rv[it].y; x.z += rv[it].z; x.w += rv[it].w;   // zeros without a residual
                                 if (DST && splits == 1) {
                                     const size_t o = (size_t)row * dst.ldc + dst.col_off + col;
                                     for (int k = 0; k < dst.n_dst; k++) *reinterpret_cast<float4*>(dst.ptr[k] + o) = x;
@@ -222,6 +235,8 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
                         }
                     }
                     __syncwarp();
+#pragma unroll
+                    for (int it = 0; it < 8; it++) rv[it] = rn[it];
                 }
             }
             if (DST) __threadfence_system();   // peer stores complete before the kernel does
