@@ -264,20 +264,36 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
     }
 }
 
-// hi/lo split of `count` row-major [rows, cols] operands into pitched scratch
+// hi/lo split of `count` row-major [rows, cols] operands into pitched scratch. Rows are
+// walked by the grid and columns by the block: float4 in and out when cols % 4 == 0 and
+// the source is 16-byte aligned (the pitch always is), no per-element division.
 __global__ void k_split(const LcuGemmGroup* __restrict__ groups, int which, size_t rows, size_t cols, size_t pitch,
                         float* __restrict__ hi, float* __restrict__ lo) {
     const LcuGemmGroup& gr = groups[blockIdx.y];
     if (which == 0 ? gr.adup : gr.bdup) return;          // an earlier group already split this operand
     const float* src = which == 0 ? gr.a : gr.b;
-    size_t base = (size_t)(which == 0 ? gr.aidx : gr.bidx) * rows * pitch;
-    size_t n = rows * cols;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
-        size_t r = i / cols, c = i % cols;
-        float x = src[i];
-        float h = tc::tf32_rna(x);
-        hi[base + r * pitch + c] = h;
-        if (lo) lo[base + r * pitch + c] = tc::tf32_rna(x - h);   // TF32-exact: no truncation bias in the MMA
+    const size_t base = (size_t)(which == 0 ? gr.aidx : gr.bidx) * rows * pitch;
+    const bool v4 = cols % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+    for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
+        const float* s_row = src + r * cols;
+        float* h_row = hi + base + r * pitch;
+        float* l_row = lo ? lo + base + r * pitch : nullptr;
+        if (v4) {
+            for (size_t c = 4 * threadIdx.x; c < cols; c += 4 * blockDim.x) {
+                const float4 x = __ldg(reinterpret_cast<const float4*>(s_row + c));
+                const float4 h = make_float4(tc::tf32_rna(x.x), tc::tf32_rna(x.y), tc::tf32_rna(x.z), tc::tf32_rna(x.w));
+                *reinterpret_cast<float4*>(h_row + c) = h;
+                if (l_row)   // TF32-exact: no truncation bias in the MMA
+                    *reinterpret_cast<float4*>(l_row + c) = make_float4(tc::tf32_rna(x.x - h.x), tc::tf32_rna(x.y - h.y),
+                                                                        tc::tf32_rna(x.z - h.z), tc::tf32_rna(x.w - h.w));
+            }
+        } else {
+            for (size_t c = threadIdx.x; c < cols; c += blockDim.x) {
+                const float x = s_row[c], h = tc::tf32_rna(x);
+                h_row[c] = h;
+                if (l_row) l_row[c] = tc::tf32_rna(x - h);
+            }
+        }
     }
 }
 
@@ -428,13 +444,13 @@ extern "C" lancius_error lcu_gemm_tc_run_dst(const LcuTcGemmPlan* p, const LcuGe
     float* lo_a = p->passes > 1 ? p->s_alo : nullptr;
     float* lo_b = p->passes > 1 ? p->s_blo : nullptr;
     if (p->K > 0) {
-        k_split<<<dim3(lcu_blocks(p->M * p->K, 256 * 8, 148 * 4), p->G), 256, 0, st>>>(d_groups, 0, p->M, p->K, p->Kp, p->s_ahi, lo_a);
+        k_split<<<dim3((unsigned)(p->M < 65535 ? p->M : 65535), p->G), 256, 0, st>>>(d_groups, 0, p->M, p->K, p->Kp, p->s_ahi, lo_a);
         lcu_note_launch();
         if (p->conv.n)
             k_im2col_split<<<dim3((unsigned)((p->N + 1023) / 1024 < 64 ? (p->N + 1023) / 1024 : 64), (unsigned)p->K), 256, 0, st>>>(
                 d_groups, p->conv, p->Np, p->s_bhi, lo_b);
         else
-            k_split<<<dim3(lcu_blocks(p->K * p->N, 256 * 8, 148 * 4), p->G), 256, 0, st>>>(d_groups, 1, p->K, p->N, p->Np, p->s_bhi, lo_b);
+            k_split<<<dim3((unsigned)(p->K < 65535 ? p->K : 65535), p->G), 256, 0, st>>>(d_groups, 1, p->K, p->N, p->Np, p->s_bhi, lo_b);
         lcu_note_launch();
     }
     dim3 grid((unsigned)((p->N + BN - 1) / BN), (unsigned)((p->M + BM - 1) / BM), (unsigned)(p->G * p->splits));
