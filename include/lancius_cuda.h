@@ -69,6 +69,11 @@ lancius_error lcu_download_async(lcu_ctx* ctx, const lancius_node* n, void* host
 /* Uploads every INPUT node whose runtime_data (FP64) is bound on the host. */
 lancius_error lcu_upload_bound_inputs(lcu_ctx* ctx);
 float* lcu_node_device_ptr(lcu_ctx* ctx, const lancius_node* n);
+/* Tensor-core MATMULs whose weights are INPUT nodes read TF32 hi/lo copies made once
+ * per lcu_upload of the weight (not per run). After writing a weight slot through
+ * lcu_node_device_ptr, call this to remake the copies. No reference counterpart:
+ * the reference's CPU kernels read the FP64 weights directly. */
+lancius_error lcu_refresh_weights(lcu_ctx* ctx);
 
 /* Runs every wave of the bound schedule on the context's stream (asynchronous;
  * lcu_synchronize() or a download waits). Same shape as the reference's

@@ -121,6 +121,7 @@ B200_FUNCS = {
     "lcu_watchdog_selftest": (C.c_int, [P]),
     "lcu_upload_bound_inputs": (C.c_int, [P]),
     "lcu_node_device_ptr": (P, [P, NODE_P]),
+    "lcu_refresh_weights": (C.c_int, [P]),
     "lancius_schedule_execute_cuda": (None, [SCHED_P, P]),
     "lcu_last_launch_count": (C.c_int, [P]),
     "lcu_last_cuda_error": (C.c_char_p, []),

@@ -44,6 +44,7 @@ struct Step {
     int lop = 0;               // lancius opcode (S_MISC); LANCIUS_OP_MATMUL / CONV2D* mean the INT8-weight forms
     double dscale = 1.0;       // INT8 weight scale
     size_t packed_off = (size_t)-1;   // INT8 MATMUL: K-major copy of the weights in ctx->packed
+    size_t wsplit_off = (size_t)-1;   // tensor-core MATMUL on INPUT weights: hi/lo copies in ctx->wsplit
     float eps = 1e-5f;
 };
 
@@ -77,6 +78,12 @@ struct lcu_ctx {
     std::vector<Pack> packs;
     int8_t* packed = nullptr;
     size_t packed_bytes = 0;
+    // FP32 weights (INPUT nodes) feeding tensor-core MATMULs, kept as TF32 hi/lo copies
+    // ([Gb][K][pad4(N)] per step, lo after hi) and refreshed by every upload of the node
+    struct WSplit { uint32_t node; size_t hi_off, lo_off, K, N, Np; };
+    std::vector<WSplit> wsplits;
+    float* wsplit = nullptr;
+    size_t wsplit_floats = 0;
     std::vector<LcuTcGemmPlan> tc_plans;
     std::vector<size_t> off;            // node id -> byte offset in dmem (NPOS: no storage)
     std::vector<Step> steps;
@@ -96,6 +103,8 @@ static void release_binding(lcu_ctx* c) {
     if (c->scratch) { cudaFree(c->scratch); c->scratch = nullptr; }
     if (c->packed) { cudaFree(c->packed); c->packed = nullptr; }
     c->packs.clear(); c->packed_bytes = 0;
+    if (c->wsplit) { cudaFree(c->wsplit); c->wsplit = nullptr; }
+    c->wsplits.clear(); c->wsplit_floats = 0;
     c->dmem_bytes = 0; c->staging_elems = 0; c->scratch_bytes = 0;
     c->tc_plans.clear();
     c->off.clear(); c->steps.clear();
@@ -389,6 +398,20 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                         if (need > c->scratch_bytes) c->scratch_bytes = need;
                         st.plan_idx = (int)c->tc_plans.size();
                         c->tc_plans.push_back(LcuTcGemmPlan());
+                        // weights that only uploads write are split once per upload, not per run
+                        bool all_inputs = true;
+                        for (const lancius_node* x : ns)
+                            all_inputs = all_inputs && x->inputs[1]->op == LANCIUS_OP_INPUT &&
+                                         x->inputs[1]->dtype != LANCIUS_DTYPE_INT8;
+                        if (all_inputs && !lcu_no_weight_cache()) {
+                            const size_t Np = (st.N + 3) & ~size_t(3), mat = st.K * Np;
+                            st.wsplit_off = c->wsplit_floats;
+                            for (size_t i = 0; i < ns.size(); i++)
+                                if (!bdup[i])
+                                    c->wsplits.push_back({ns[i]->inputs[1]->id, st.wsplit_off + bidx[i] * mat,
+                                                          st.wsplit_off + (st.gb + bidx[i]) * mat, st.K, st.N, Np});
+                            c->wsplit_floats += align_up(2 * st.gb * mat, 64);
+                        }
                     }
                     if (n->inputs[1]->dtype == LANCIUS_DTYPE_INT8 && n->inputs[1]->runtime_data_int8) {
                         // INT8 weights: dynamic per-tensor quantisation of A (scheduler.c:195-220)
@@ -664,6 +687,13 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
         ce = cudaMalloc(&c->packed, c->packed_bytes);
         if (ce != cudaSuccess) { cudaGetLastError(); release_binding(c); return fail(LANCIUS_ERROR_OOM); }
     }
+    if (c->wsplit_floats) {
+        ce = cudaMalloc(&c->wsplit, c->wsplit_floats * sizeof(float));
+        if (ce != cudaSuccess) { cudaGetLastError(); release_binding(c); return fail(LANCIUS_ERROR_OOM); }
+        // zero until the first upload, like the node slots of never-uploaded inputs
+        ce = cudaMemsetAsync(c->wsplit, 0, c->wsplit_floats * sizeof(float), c->stream);
+        if (ce != cudaSuccess) { release_binding(c); return cuda_fail(ce); }
+    }
     ce = cudaMalloc(&c->staging, (max_io ? max_io : 1) * sizeof(double));
     if (ce != cudaSuccess) { cudaGetLastError(); release_binding(c); return fail(LANCIUS_ERROR_OOM); }
     c->staging_elems = max_io;
@@ -692,13 +722,26 @@ static bool node_slot(lcu_ctx* c, const lancius_node* n, float** p, size_t* E) {
     return true;
 }
 
+// re-split every TF32 hi/lo weight copy made from node `id` (device data at d), in stream order
+static lancius_error refresh_weight_splits(lcu_ctx* c, uint32_t id, const float* d) {
+    for (const auto& w : c->wsplits)
+        if (w.node == id) {
+            lancius_error e = lcu_tf32_split_rows(d, w.K, w.N, w.Np, c->wsplit + w.hi_off, c->wsplit + w.lo_off, c->stream);
+            if (e != LANCIUS_ERROR_OK) return e;
+        }
+    return LANCIUS_ERROR_OK;
+}
+
 extern "C" lancius_error lcu_upload(lcu_ctx* c, const lancius_node* n, const void* host, lancius_dtype dt) {
     float* d; size_t E;
     if (!host) return fail(LANCIUS_ERROR_NULL_PTR);
     if (!node_slot(c, n, &d, &E)) return fail(LANCIUS_ERROR_NULL_PTR);
     cudaSetDevice(c->device);
-    if (dt == LANCIUS_DTYPE_FP32)
-        return cuda_fail(cudaMemcpyAsync(d, host, E * 4, cudaMemcpyHostToDevice, c->stream));
+    if (dt == LANCIUS_DTYPE_FP32) {
+        cudaError_t ce = cudaMemcpyAsync(d, host, E * 4, cudaMemcpyHostToDevice, c->stream);
+        if (ce != cudaSuccess) return cuda_fail(ce);
+        return refresh_weight_splits(c, n->id, d);
+    }
     if (dt == LANCIUS_DTYPE_INT8) {     // INT8 weights are stored as bytes in the node's slot
         cudaError_t ce = cudaMemcpyAsync(d, host, E, cudaMemcpyHostToDevice, c->stream);
         if (ce != cudaSuccess) return cuda_fail(ce);
@@ -714,7 +757,19 @@ extern "C" lancius_error lcu_upload(lcu_ctx* c, const lancius_node* n, const voi
     if (E > c->staging_elems) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
     cudaError_t ce = cudaMemcpyAsync(c->staging, host, E * 8, cudaMemcpyHostToDevice, c->stream);
     if (ce != cudaSuccess) return cuda_fail(ce);
-    return lcu_convert_f64_to_f32(d, c->staging, E, c->stream);
+    lancius_error e = lcu_convert_f64_to_f32(d, c->staging, E, c->stream);
+    if (e != LANCIUS_ERROR_OK) return e;
+    return refresh_weight_splits(c, n->id, d);
+}
+
+extern "C" lancius_error lcu_refresh_weights(lcu_ctx* c) {
+    if (!c || !c->g) return fail(LANCIUS_ERROR_NULL_PTR);
+    cudaSetDevice(c->device);
+    for (const auto& w : c->wsplits) {
+        lancius_error e = refresh_weight_splits(c, w.node, reinterpret_cast<const float*>(c->dmem + c->off[w.node]));
+        if (e != LANCIUS_ERROR_OK) return e;
+    }
+    return LANCIUS_ERROR_OK;
 }
 
 // FP32 device -> host copy queued on the context's stream; returns at once (the data is
@@ -820,6 +875,12 @@ static lancius_error run_steps(lcu_ctx* c) {
                     if (p.passes != passes || p.M != s.M) {
                         e = lcu_gemm_tc_prepare(&p, c->scratch, s.M, s.N, s.K, s.count, s.ga, s.gb, passes);
                         if (e != LANCIUS_ERROR_OK) break;
+                        if (s.wsplit_off != NPOS) {
+                            const size_t mat = s.K * ((s.N + 3) & ~size_t(3));
+                            float* hi = c->wsplit + s.wsplit_off;
+                            e = lcu_gemm_tc_use_presplit_b(&p, hi, hi + s.gb * mat);
+                            if (e != LANCIUS_ERROR_OK) break;
+                        }
                     }
                     e = lcu_gemm_tc_run(&p, (const LcuGemmGroup*)(base + s.table_off), s.epi, st);
                 } else {

@@ -267,17 +267,13 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
 // hi/lo split of `count` row-major [rows, cols] operands into pitched scratch. Rows are
 // walked by the grid and columns by the block: float4 in and out when cols % 4 == 0 and
 // the source is 16-byte aligned (the pitch always is), no per-element division.
-__global__ void k_split(const LcuGemmGroup* __restrict__ groups, int which, size_t rows, size_t cols, size_t pitch,
-                        float* __restrict__ hi, float* __restrict__ lo) {
-    const LcuGemmGroup& gr = groups[blockIdx.y];
-    if (which == 0 ? gr.adup : gr.bdup) return;          // an earlier group already split this operand
-    const float* src = which == 0 ? gr.a : gr.b;
-    const size_t base = (size_t)(which == 0 ? gr.aidx : gr.bidx) * rows * pitch;
+__device__ __forceinline__ void split_rows(const float* __restrict__ src, size_t rows, size_t cols, size_t pitch,
+                                           float* __restrict__ hi, float* __restrict__ lo) {
     const bool v4 = cols % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
     for (size_t r = blockIdx.x; r < rows; r += gridDim.x) {
         const float* s_row = src + r * cols;
-        float* h_row = hi + base + r * pitch;
-        float* l_row = lo ? lo + base + r * pitch : nullptr;
+        float* h_row = hi + r * pitch;
+        float* l_row = lo ? lo + r * pitch : nullptr;
         if (v4) {
             for (size_t c = 4 * threadIdx.x; c < cols; c += 4 * blockDim.x) {
                 const float4 x = __ldg(reinterpret_cast<const float4*>(s_row + c));
@@ -295,6 +291,19 @@ __global__ void k_split(const LcuGemmGroup* __restrict__ groups, int which, size
             }
         }
     }
+}
+
+__global__ void k_split(const LcuGemmGroup* __restrict__ groups, int which, size_t rows, size_t cols, size_t pitch,
+                        float* __restrict__ hi, float* __restrict__ lo) {
+    const LcuGemmGroup& gr = groups[blockIdx.y];
+    if (which == 0 ? gr.adup : gr.bdup) return;          // an earlier group already split this operand
+    const size_t base = (size_t)(which == 0 ? gr.aidx : gr.bidx) * rows * pitch;
+    split_rows(which == 0 ? gr.a : gr.b, rows, cols, pitch, hi + base, lo ? lo + base : nullptr);
+}
+
+__global__ void k_split_one(const float* __restrict__ src, size_t rows, size_t cols, size_t pitch, float* __restrict__ hi,
+                            float* __restrict__ lo) {
+    split_rows(src, rows, cols, pitch, hi, lo);
 }
 
 // hi/lo im2col of an NCHW input into pitched [K = Ci*Kh*Kw][P = N*Ho*Wo] scratch
@@ -404,6 +413,7 @@ extern "C" lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, si
                                              int Ga, int Gb, int passes) {
     p->M = M; p->N = N; p->K = K; p->Kp = pad4(K); p->Np = pad4(N); p->G = G; p->Ga = Ga; p->Gb = Gb; p->passes = passes;
     p->conv = LcuConvShape{};
+    p->b_presplit = 0;
     size_t a = al256((size_t)Ga * M * p->Kp * 4), b = al256((size_t)Gb * K * p->Np * 4);
     char* s = static_cast<char*>(scratch);
     p->s_ahi = (float*)s; s += a;
@@ -421,6 +431,24 @@ extern "C" lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, si
     else if (ok) { p->a_lo = p->a_hi; p->b_lo = p->b_hi; }
     if (!ok) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
     return LANCIUS_ERROR_OK;
+}
+
+extern "C" lancius_error lcu_gemm_tc_use_presplit_b(LcuTcGemmPlan* p, float* b_hi, float* b_lo) {
+    if (p->conv.n || !b_hi || (p->passes > 1 && !b_lo)) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    bool ok = make_map(&p->b_hi, b_hi, p->N, p->K, p->Gb, p->Np, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    if (ok && p->passes > 1) ok = make_map(&p->b_lo, b_lo, p->N, p->K, p->Gb, p->Np, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+    else if (ok) p->b_lo = p->b_hi;
+    if (!ok) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    p->s_bhi = b_hi; p->s_blo = p->passes > 1 ? b_lo : nullptr;
+    p->b_presplit = 1;
+    return LANCIUS_ERROR_OK;
+}
+
+extern "C" lancius_error lcu_tf32_split_rows(const float* src, size_t rows, size_t cols, size_t pitch, float* hi, float* lo,
+                                             void* stream) {
+    if (!rows || !cols) return LANCIUS_ERROR_OK;
+    k_split_one<<<(unsigned)(rows < 65535 ? rows : 65535), 256, 0, lcu_as_stream(stream)>>>(src, rows, cols, pitch, hi, lo);
+    return lcu_launch_status();
 }
 
 extern "C" lancius_error lcu_gemm_tc_run(const LcuTcGemmPlan* p, const LcuGemmGroup* d_groups, int epi, void* stream) {
@@ -449,9 +477,9 @@ extern "C" lancius_error lcu_gemm_tc_run_dst(const LcuTcGemmPlan* p, const LcuGe
         if (p->conv.n)
             k_im2col_split<<<dim3((unsigned)((p->N + 1023) / 1024 < 64 ? (p->N + 1023) / 1024 : 64), (unsigned)p->K), 256, 0, st>>>(
                 d_groups, p->conv, p->Np, p->s_bhi, lo_b);
-        else
+        else if (!p->b_presplit)
             k_split<<<dim3((unsigned)(p->K < 65535 ? p->K : 65535), p->G), 256, 0, st>>>(d_groups, 1, p->K, p->N, p->Np, p->s_bhi, lo_b);
-        lcu_note_launch();
+        if (p->conv.n || !p->b_presplit) lcu_note_launch();
     }
     dim3 grid((unsigned)((p->N + BN - 1) / BN), (unsigned)((p->M + BM - 1) / BM), (unsigned)(p->G * p->splits));
     if (dst.n_dst > 0)

@@ -35,12 +35,19 @@ struct LcuTcGemmPlan {
     int splits, kchunk;          // K cut into `splits` chunks of kchunk (multiple of 16)
     float* partial;              // [G][splits][M][N] partial sums when splits > 1
     LcuConvShape conv;           // conv.n > 0: B is the im2col of groups[0].b, C is stored NCHW
+    int b_presplit;              // 1: b maps point at persistent hi/lo weight copies; no B split per run
 };
 
 extern "C" {
 size_t lcu_gemm_tc_scratch_bytes(size_t M, size_t N, size_t K, int G, int Ga, int Gb, int passes);
 lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, size_t M, size_t N, size_t K, int G, int Ga, int Gb,
                                   int passes);
+// Points a prepared plan's B maps at persistent [Gb][K][pad4(N)] hi/lo copies (made by
+// lcu_tf32_split_rows) so runs skip the per-call B split; undone by the next prepare.
+lancius_error lcu_gemm_tc_use_presplit_b(LcuTcGemmPlan* p, float* b_hi, float* b_lo);
+// hi = rna_tf32(x), lo = rna_tf32(x - hi) of a row-major [rows, cols] matrix into rows of `pitch` floats
+lancius_error lcu_tf32_split_rows(const float* src, size_t rows, size_t cols, size_t pitch, float* hi, float* lo,
+                                  void* stream);
 lancius_error lcu_gemm_tc_run(const LcuTcGemmPlan* p, const LcuGemmGroup* d_groups, int epi, void* stream);
 lancius_error lcu_gemm_tc_run_dst(const LcuTcGemmPlan* p, const LcuGemmGroup* d_groups, int epi, LcuColDest dst,
                                   void* stream);
@@ -64,6 +71,7 @@ int lcu_gemm_watchdog_read_and_clear(void);
 int lcu_use_tensor_cores(size_t M, size_t N, size_t K);
 int lcu_attention_tc_supported(size_t D);
 int lcu_force_simt(void);
+int lcu_no_weight_cache(void);
 lancius_error lcu_conv2d_tc(float* out, const float* in, const float* w, LcuConvShape cs, int relu, int mode, void* stream);
 // direct implicit-GEMM conv over NHWC hi/lo copies (conv_tc.cu); scratch of
 // lcu_conv_nhwc_scratch_bytes(cs, passes) bytes

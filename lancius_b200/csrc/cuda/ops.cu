@@ -28,6 +28,12 @@ static int force_mode() {
 extern "C" int lcu_force_simt(void) { return force_mode() == 0; }
 // LCU_FORCE_TC=1 also sends short-reduction convs to the tensor cores (tests)
 extern "C" int lcu_force_tc_conv(void) { return force_mode() == 1; }
+// LCU_NO_WEIGHT_CACHE=1: split MATMUL weights into TF32 hi/lo on every run instead of once
+// per upload (read at each bind, so tests can compare both paths in one process)
+extern "C" int lcu_no_weight_cache(void) {
+    const char* e = getenv("LCU_NO_WEIGHT_CACHE");
+    return e && e[0] == '1';
+}
 extern "C" int lcu_conv_force_im2col(void) {
     static int f = -1;
     if (f < 0) { const char* e = getenv("LCU_CONV_IM2COL"); f = e && e[0] == '1'; }

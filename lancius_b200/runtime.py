@@ -78,6 +78,10 @@ class Device:
     def device_ptr(self, node):
         return self.lib.lcu_node_device_ptr(self.ptr, node.ptr)
 
+    def refresh_weights(self):
+        """Remakes the TF32 hi/lo weight copies after writes through device_ptr()."""
+        _ok(self.lib.lcu_refresh_weights(self.ptr), "lcu_refresh_weights")
+
     def execute(self, schedule=None):
         s = schedule or self.sched
         self.lib.lancius_clear_error()

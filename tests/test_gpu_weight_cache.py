@@ -1,0 +1,90 @@
+"""TF32 hi/lo weight copies kept across runs: MATMULs whose weights are INPUT nodes read
+copies made at upload time. Checks that a re-upload and lcu_refresh_weights remake them,
+that grouped waves (distinct and shared weights) index them correctly, and that the cached
+path gives the same bytes as splitting per run (LCU_NO_WEIGHT_CACHE=1)."""
+import os
+
+import numpy as np
+import pytest
+
+from conftest import assert_close
+import lancius_b200 as L
+
+pytestmark = pytest.mark.gpu
+torch = pytest.importorskip("torch")
+
+M, K, N = 256, 512, 384          # 50M multiply-adds: tensor-core path
+
+
+@pytest.fixture(scope="module")
+def device():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    d = L.Device(0)
+    yield d
+    d.close()
+
+
+def rnd(seed, *shape):
+    return np.random.default_rng(seed).standard_normal(shape)
+
+
+def test_reupload_and_refresh(device):
+    g = L.Graph()
+    x, w = g.input(M, K), g.input(K, N)
+    y = g.matmul(x, w)
+    s = g.schedule()
+    device.bind(s)
+    xa, w1, w2 = rnd(1, M, K), rnd(2, K, N), rnd(3, K, N)
+    device.upload(x, xa)
+    device.upload(w, w1)
+    device.execute(s)
+    assert_close(device.download(y), xa @ w1, 1e-4)
+    device.upload(w, w2)                      # a new upload re-splits the weight
+    device.execute(s)
+    assert_close(device.download(y), xa @ w2, 1e-4)
+    # a write through the device pointer needs an explicit refresh
+    assert device.lib.lcu_fill(device.device_ptr(w), 0.5, K * N, device.stream) == 0
+    device.refresh_weights()
+    device.execute(s)
+    assert_close(device.download(y), xa @ np.full((K, N), 0.5), 1e-4)
+
+
+def test_grouped_distinct_and_shared_weights(device):
+    g = L.Graph()
+    x1, x2 = g.input(M, K), g.input(M, K)
+    wq, wk, wv = g.input(K, N), g.input(K, N), g.input(K, N)
+    outs = [g.matmul(x1, wq), g.matmul(x1, wk), g.matmul(x1, wv), g.matmul(x2, wq)]
+    s = g.schedule()
+    device.bind(s)
+    arrs = {n: rnd(10 + i, *n.shape) for i, n in enumerate([x1, x2, wq, wk, wv])}
+    for n, a in arrs.items():
+        device.upload(n, a)
+    device.execute(s)
+    refs = [arrs[x1] @ arrs[wq], arrs[x1] @ arrs[wk], arrs[x1] @ arrs[wv], arrs[x2] @ arrs[wq]]
+    for o, r in zip(outs, refs):
+        assert_close(device.download(o), r, 1e-4)
+
+
+def test_cached_equals_per_run_split(device):
+    g = L.Graph()
+    x, w, bias = g.input(M, K), g.input(K, N), g.input(1, N)
+    y = g.relu(g.add(g.matmul(x, w), g.broadcast(bias, M, N)))
+    s = g.schedule()
+    xa, wa, ba = rnd(21, M, K), rnd(22, K, N), rnd(23, 1, N)
+
+    def run():
+        device.bind(s)
+        for n, a in ((x, xa), (w, wa), (bias, ba)):
+            device.upload(n, a)
+        device.execute(s)
+        return device.download(y, np.float32)
+
+    cached = run()
+    os.environ["LCU_NO_WEIGHT_CACHE"] = "1"
+    try:
+        per_run = run()
+    finally:
+        del os.environ["LCU_NO_WEIGHT_CACHE"]
+    assert np.array_equal(cached, per_run)
+    assert_close(cached, np.maximum(xa @ wa + ba, 0), 1e-4)
