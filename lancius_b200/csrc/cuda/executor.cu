@@ -45,6 +45,7 @@ struct Step {
     double dscale = 1.0;       // INT8 weight scale
     size_t packed_off = (size_t)-1;   // INT8 MATMUL: K-major copy of the weights in ctx->packed
     size_t wsplit_off = (size_t)-1;   // tensor-core MATMUL on INPUT weights: hi/lo copies in ctx->wsplit
+    int amap_idx = -1;                // tensor-core MATMUL in raw-A mode: first of its maps in ctx->amaps
     float eps = 1e-5f;
 };
 
@@ -84,6 +85,8 @@ struct lcu_ctx {
     std::vector<WSplit> wsplits;
     float* wsplit = nullptr;
     size_t wsplit_floats = 0;
+    std::vector<CUtensorMap> amaps_host;  // raw-A tensor maps of every step, uploaded to amaps at bind
+    CUtensorMap* amaps = nullptr;
     std::vector<LcuTcGemmPlan> tc_plans;
     std::vector<size_t> off;            // node id -> byte offset in dmem (NPOS: no storage)
     std::vector<Step> steps;
@@ -105,6 +108,8 @@ static void release_binding(lcu_ctx* c) {
     c->packs.clear(); c->packed_bytes = 0;
     if (c->wsplit) { cudaFree(c->wsplit); c->wsplit = nullptr; }
     c->wsplits.clear(); c->wsplit_floats = 0;
+    if (c->amaps) { cudaFree(c->amaps); c->amaps = nullptr; }
+    c->amaps_host.clear();
     c->dmem_bytes = 0; c->staging_elems = 0; c->scratch_bytes = 0;
     c->tc_plans.clear();
     c->off.clear(); c->steps.clear();
@@ -663,6 +668,26 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
             for (int i = 0; i < st.count; i++) {
                 patch(t[i].a); patch(t[i].b); patch((const float*&)t[i].c); patch(t[i].bias); patch(t[i].resid);
             }
+            if (st.kind == S_GEMM && st.tc && !lcu_no_raw_a()) {
+                // raw-A mode: the GEMM reads each distinct A in place and splits it on chip.
+                // Needs K % 4 == 0, aligned A, and no C of the wave overlapping any A (the
+                // groups' CTAs read A while others already store C).
+                std::vector<CUtensorMap> maps(st.ga);
+                bool ok = true;
+                for (int i = 0; i < st.count && ok; i++) {
+                    const char* a0 = (const char*)t[i].a;
+                    const char* a1 = a0 + st.M * st.K * 4;
+                    for (int j = 0; j < st.count && ok; j++) {
+                        const char* c0 = (const char*)t[j].c;
+                        ok = c0 + st.M * st.N * 4 <= a0 || a1 <= c0;
+                    }
+                    if (ok && !t[i].adup) ok = lcu_gemm_tc_make_raw_a_map(&maps[t[i].aidx], t[i].a, st.M, st.K);
+                }
+                if (ok) {
+                    st.amap_idx = (int)c->amaps_host.size();
+                    c->amaps_host.insert(c->amaps_host.end(), maps.begin(), maps.end());
+                }
+            }
         } else if (st.kind == S_ATTN) {
             LcuAttnGroup* t = (LcuAttnGroup*)base;
             for (int i = 0; i < st.count; i++) { patch(t[i].q); patch(t[i].k); patch(t[i].v); patch((const float*&)t[i].o); }
@@ -692,6 +717,13 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
         if (ce != cudaSuccess) { cudaGetLastError(); release_binding(c); return fail(LANCIUS_ERROR_OOM); }
         // zero until the first upload, like the node slots of never-uploaded inputs
         ce = cudaMemsetAsync(c->wsplit, 0, c->wsplit_floats * sizeof(float), c->stream);
+        if (ce != cudaSuccess) { release_binding(c); return cuda_fail(ce); }
+    }
+    if (!c->amaps_host.empty()) {
+        const size_t bytes = c->amaps_host.size() * sizeof(CUtensorMap);
+        ce = cudaMalloc(&c->amaps, bytes);
+        if (ce != cudaSuccess) { cudaGetLastError(); release_binding(c); return fail(LANCIUS_ERROR_OOM); }
+        ce = cudaMemcpyAsync(c->amaps, c->amaps_host.data(), bytes, cudaMemcpyHostToDevice, c->stream);
         if (ce != cudaSuccess) { release_binding(c); return cuda_fail(ce); }
     }
     ce = cudaMalloc(&c->staging, (max_io ? max_io : 1) * sizeof(double));
@@ -881,6 +913,7 @@ static lancius_error run_steps(lcu_ctx* c) {
                             e = lcu_gemm_tc_use_presplit_b(&p, hi, hi + s.gb * mat);
                             if (e != LANCIUS_ERROR_OK) break;
                         }
+                        if (s.amap_idx >= 0 && (e = lcu_gemm_tc_use_raw_a(&p, c->amaps + s.amap_idx)) != LANCIUS_ERROR_OK) break;
                     }
                     e = lcu_gemm_tc_run(&p, (const LcuGemmGroup*)(base + s.table_off), s.epi, st);
                 } else {

@@ -37,6 +37,7 @@ __device__ int g_gemm_watchdog = 0;
 struct Smem {
     uint64_t full[STAGES];
     uint64_t empty[STAGES];
+    uint64_t conv[STAGES];     // raw-A mode: the stage's A tile has been split in place
     uint64_t accum;
     uint64_t drain;
     uint32_t tmem_base;
@@ -49,7 +50,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
           const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
           const LcuGemmGroup* __restrict__ groups, int M, int N, int K, int epi, int passes,
-          int splits, int kchunk, float* __restrict__ partial, int conv_hw, LcuColDest dst) {
+          int splits, int kchunk, float* __restrict__ partial, int conv_hw, LcuColDest dst,
+          const CUtensorMap* __restrict__ a_maps) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Smem* sm = reinterpret_cast<Smem*>(tiles + STAGES * STAGE_BYTES);
@@ -64,14 +66,18 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
     volatile int* abort = &sm->abort;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; s++) { tc::mbar_init(&sm->full[s], 1); tc::mbar_init(&sm->empty[s], 1); }
+        for (int s = 0; s < STAGES; s++) {
+            tc::mbar_init(&sm->full[s], 1); tc::mbar_init(&sm->empty[s], 1); tc::mbar_init(&sm->conv[s], 4);
+        }
         tc::mbar_init(&sm->accum, 1);
         tc::mbar_init(&sm->drain, 1);
         sm->abort = 0;
         sm->consumed = 0;
         tc::fence_barrier_init();
-        tc::prefetch_tmap(&ta_hi); tc::prefetch_tmap(&tb_hi);
-        if (passes > 1) { tc::prefetch_tmap(&ta_lo); tc::prefetch_tmap(&tb_lo); }
+        if (a_maps) { tc::tmap_acquire(a_maps + groups[g].aidx); tc::prefetch_tmap(a_maps + groups[g].aidx); }
+        else { tc::prefetch_tmap(&ta_hi); if (passes > 1) tc::prefetch_tmap(&ta_lo); }
+        tc::prefetch_tmap(&tb_hi);
+        if (passes > 1) tc::prefetch_tmap(&tb_lo);
     }
     if (warp == 1) tc::tmem_alloc(&sm->tmem_base, TMEM_COLS);
     tc::tc_fence_before();
@@ -82,19 +88,22 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
 
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer ----------------
-        const uint32_t tx = passes > 1 ? STAGE_BYTES : A_TILE + B_TILE;
+        // raw-A mode: only the FP32 A tile arrives; warps 2-5 split it into hi/lo in place
+        const uint32_t tx = a_maps ? (passes > 1 ? A_TILE + 2 * B_TILE : A_TILE + B_TILE)
+                                   : (passes > 1 ? STAGE_BYTES : A_TILE + B_TILE);
         const int ga = groups[g].aidx, gb = groups[g].bidx;      // scratch slots of this group's operands
+        const CUtensorMap* ma = a_maps ? a_maps + ga : &ta_hi;
         for (int kt = 0; kt < KT; kt++) {
             int s = kt % STAGES;
             if (kt >= STAGES && !tc::mbar_wait(&sm->empty[s], ((kt / STAGES) - 1) & 1, abort, &g_gemm_watchdog, 1)) break;
             uint8_t* st = tiles + s * STAGE_BYTES;
             tc::mbar_expect_tx(&sm->full[s], tx);
             int k0 = k_begin + kt * BK;
-            tc::tma_load_3d(st, &ta_hi, &sm->full[s], k0, m0, ga);
+            tc::tma_load_3d(st, ma, &sm->full[s], k0, m0, a_maps ? 0 : ga);
             for (int j = 0; j < BN / 32; j++)
                 tc::tma_load_3d(st + 2 * A_TILE + j * B_CHUNK, &tb_hi, &sm->full[s], n0 + 32 * j, k0, gb);
             if (passes > 1) {
-                tc::tma_load_3d(st + A_TILE, &ta_lo, &sm->full[s], k0, m0, ga);
+                if (!a_maps) tc::tma_load_3d(st + A_TILE, &ta_lo, &sm->full[s], k0, m0, ga);
                 for (int j = 0; j < BN / 32; j++)
                     tc::tma_load_3d(st + 2 * A_TILE + B_TILE + j * B_CHUNK, &tb_lo, &sm->full[s], n0 + 32 * j, k0, gb);
             }
@@ -106,7 +115,9 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
         bool ok = true;
         for (int kt = 0; kt < KT && ok; kt++) {
             int s = kt % STAGES;
-            if (!tc::mbar_wait(&sm->full[s], (kt / STAGES) & 1, abort, &g_gemm_watchdog, 2)) { ok = false; break; }
+            if (!tc::mbar_wait(a_maps ? &sm->conv[s] : &sm->full[s], (kt / STAGES) & 1, abort, &g_gemm_watchdog, 2)) {
+                ok = false; break;
+            }
             tc::tc_fence_after();
             if (LCU_GEMM_DEBUG && blockIdx.x == 0 && blockIdx.y == 0 && kt == 0) {
                 const float* fa = reinterpret_cast<const float*>(tiles + s * STAGE_BYTES);
@@ -140,6 +151,29 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
         }
         if (ok) tc::mma_commit(&sm->accum);
     } else if (warp >= 2) {
+        if (a_maps) {
+            // ---------------- A splitter (raw-A mode) ----------------
+            // hi = rna_tf32(x) in place, lo = rna_tf32(x - hi) into the stage's lo slot. The
+            // swizzle permutes 16-byte chunks identically in both slots, so the split is a
+            // flat elementwise pass over the tile's bytes.
+            for (int kt = 0; kt < KT; kt++) {
+                const int s = kt % STAGES;
+                if (!tc::mbar_wait(&sm->full[s], (kt / STAGES) & 1, abort, &g_gemm_watchdog, 4)) break;
+                float4* a4 = reinterpret_cast<float4*>(tiles + s * STAGE_BYTES);
+#pragma unroll 4
+                for (int i = threadIdx.x - 64; i < A_TILE / 16; i += 128) {
+                    const float4 x = a4[i];
+                    const float4 h = make_float4(tc::tf32_rna(x.x), tc::tf32_rna(x.y), tc::tf32_rna(x.z), tc::tf32_rna(x.w));
+                    a4[i] = h;
+                    if (passes > 1)
+                        a4[i + A_TILE / 16] = make_float4(tc::tf32_rna(x.x - h.x), tc::tf32_rna(x.y - h.y),
+                                                          tc::tf32_rna(x.z - h.z), tc::tf32_rna(x.w - h.w));
+                }
+                tc::fence_proxy_async();           // generic-proxy writes -> visible to the tensor core
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&sm->conv[s]);
+            }
+        }
         // ---------------- epilogue ----------------
         if (tc::mbar_wait(&sm->accum, 0, abort, &g_gemm_watchdog, 3)) {
             tc::tc_fence_after();
@@ -414,6 +448,7 @@ extern "C" lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, si
     p->M = M; p->N = N; p->K = K; p->Kp = pad4(K); p->Np = pad4(N); p->G = G; p->Ga = Ga; p->Gb = Gb; p->passes = passes;
     p->conv = LcuConvShape{};
     p->b_presplit = 0;
+    p->d_amaps = nullptr;
     size_t a = al256((size_t)Ga * M * p->Kp * 4), b = al256((size_t)Gb * K * p->Np * 4);
     char* s = static_cast<char*>(scratch);
     p->s_ahi = (float*)s; s += a;
@@ -441,6 +476,17 @@ extern "C" lancius_error lcu_gemm_tc_use_presplit_b(LcuTcGemmPlan* p, float* b_h
     if (!ok) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
     p->s_bhi = b_hi; p->s_blo = p->passes > 1 ? b_lo : nullptr;
     p->b_presplit = 1;
+    return LANCIUS_ERROR_OK;
+}
+
+extern "C" bool lcu_gemm_tc_make_raw_a_map(CUtensorMap* m, const float* a, size_t M, size_t K) {
+    if (K % 4 || (reinterpret_cast<uintptr_t>(a) & 15) || !M || !K) return false;
+    return make_map(m, a, K, M, 1, K, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
+extern "C" lancius_error lcu_gemm_tc_use_raw_a(LcuTcGemmPlan* p, const CUtensorMap* d_maps) {
+    if (p->conv.n || !d_maps) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    p->d_amaps = d_maps;
     return LANCIUS_ERROR_OK;
 }
 
@@ -472,8 +518,10 @@ extern "C" lancius_error lcu_gemm_tc_run_dst(const LcuTcGemmPlan* p, const LcuGe
     float* lo_a = p->passes > 1 ? p->s_alo : nullptr;
     float* lo_b = p->passes > 1 ? p->s_blo : nullptr;
     if (p->K > 0) {
-        k_split<<<dim3((unsigned)(p->M < 65535 ? p->M : 65535), p->G), 256, 0, st>>>(d_groups, 0, p->M, p->K, p->Kp, p->s_ahi, lo_a);
-        lcu_note_launch();
+        if (!p->d_amaps) {
+            k_split<<<dim3((unsigned)(p->M < 65535 ? p->M : 65535), p->G), 256, 0, st>>>(d_groups, 0, p->M, p->K, p->Kp, p->s_ahi, lo_a);
+            lcu_note_launch();
+        }
         if (p->conv.n)
             k_im2col_split<<<dim3((unsigned)((p->N + 1023) / 1024 < 64 ? (p->N + 1023) / 1024 : 64), (unsigned)p->K), 256, 0, st>>>(
                 d_groups, p->conv, p->Np, p->s_bhi, lo_b);
@@ -485,11 +533,11 @@ extern "C" lancius_error lcu_gemm_tc_run_dst(const LcuTcGemmPlan* p, const LcuGe
     if (dst.n_dst > 0)
         k_gemm_tc<true><<<grid, THREADS, SMEM_BYTES, st>>>(p->a_hi, p->a_lo, p->b_hi, p->b_lo, d_groups, (int)p->M, (int)p->N,
                                                            (int)p->K, epi, p->passes, p->splits, p->kchunk, p->partial,
-                                                           p->conv.n ? p->conv.ho * p->conv.wo : 0, dst);
+                                                           p->conv.n ? p->conv.ho * p->conv.wo : 0, dst, p->d_amaps);
     else
         k_gemm_tc<false><<<grid, THREADS, SMEM_BYTES, st>>>(p->a_hi, p->a_lo, p->b_hi, p->b_lo, d_groups, (int)p->M, (int)p->N,
                                                             (int)p->K, epi, p->passes, p->splits, p->kchunk, p->partial,
-                                                            p->conv.n ? p->conv.ho * p->conv.wo : 0, dst);
+                                                            p->conv.n ? p->conv.ho * p->conv.wo : 0, dst, p->d_amaps);
     lcu_note_launch();
     if (p->splits > 1) {
         k_splitk_reduce<<<dim3(lcu_blocks(p->M * p->N, 256 * 4, 148 * 8), p->G), 256, 0, st>>>(d_groups, p->partial, p->splits,

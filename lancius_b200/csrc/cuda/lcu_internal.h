@@ -36,6 +36,8 @@ struct LcuTcGemmPlan {
     float* partial;              // [G][splits][M][N] partial sums when splits > 1
     LcuConvShape conv;           // conv.n > 0: B is the im2col of groups[0].b, C is stored NCHW
     int b_presplit;              // 1: b maps point at persistent hi/lo weight copies; no B split per run
+    const CUtensorMap* d_amaps;  // raw-A mode: per-distinct-A maps (device memory) over the FP32 operands
+                                 // themselves, split into hi/lo inside the GEMM; no A split pass
 };
 
 extern "C" {
@@ -45,6 +47,10 @@ lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, size_t M, siz
 // Points a prepared plan's B maps at persistent [Gb][K][pad4(N)] hi/lo copies (made by
 // lcu_tf32_split_rows) so runs skip the per-call B split; undone by the next prepare.
 lancius_error lcu_gemm_tc_use_presplit_b(LcuTcGemmPlan* p, float* b_hi, float* b_lo);
+// Raw-A mode: a map over the FP32 A operand itself ([M][K] row-major; K % 4 == 0, 16-byte
+// aligned, false otherwise), one per distinct A, stored in device memory and handed to the plan.
+bool lcu_gemm_tc_make_raw_a_map(CUtensorMap* m, const float* a, size_t M, size_t K);
+lancius_error lcu_gemm_tc_use_raw_a(LcuTcGemmPlan* p, const CUtensorMap* d_maps);
 // hi = rna_tf32(x), lo = rna_tf32(x - hi) of a row-major [rows, cols] matrix into rows of `pitch` floats
 lancius_error lcu_tf32_split_rows(const float* src, size_t rows, size_t cols, size_t pitch, float* hi, float* lo,
                                   void* stream);
@@ -72,6 +78,7 @@ int lcu_use_tensor_cores(size_t M, size_t N, size_t K);
 int lcu_attention_tc_supported(size_t D);
 int lcu_force_simt(void);
 int lcu_no_weight_cache(void);
+int lcu_no_raw_a(void);
 lancius_error lcu_conv2d_tc(float* out, const float* in, const float* w, LcuConvShape cs, int relu, int mode, void* stream);
 // direct implicit-GEMM conv over NHWC hi/lo copies (conv_tc.cu); scratch of
 // lcu_conv_nhwc_scratch_bytes(cs, passes) bytes

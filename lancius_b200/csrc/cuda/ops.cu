@@ -34,6 +34,11 @@ extern "C" int lcu_no_weight_cache(void) {
     const char* e = getenv("LCU_NO_WEIGHT_CACHE");
     return e && e[0] == '1';
 }
+// LCU_NO_RAW_A=1: split tensor-core GEMM A operands in a separate pass (read at each bind)
+extern "C" int lcu_no_raw_a(void) {
+    const char* e = getenv("LCU_NO_RAW_A");
+    return e && e[0] == '1';
+}
 extern "C" int lcu_conv_force_im2col(void) {
     static int f = -1;
     if (f < 0) { const char* e = getenv("LCU_CONV_IM2COL"); f = e && e[0] == '1'; }

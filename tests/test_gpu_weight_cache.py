@@ -1,7 +1,9 @@
-"""TF32 hi/lo weight copies kept across runs: MATMULs whose weights are INPUT nodes read
-copies made at upload time. Checks that a re-upload and lcu_refresh_weights remake them,
+"""TF32 hi/lo operand handling of the tensor-core MATMUL. MATMULs whose weights are INPUT
+nodes read hi/lo copies made at upload time. Checks that a re-upload and lcu_refresh_weights remake them,
 that grouped waves (distinct and shared weights) index them correctly, and that the cached
-path gives the same bytes as splitting per run (LCU_NO_WEIGHT_CACHE=1)."""
+path gives the same bytes as splitting per run (LCU_NO_WEIGHT_CACHE=1). Activations (A) are
+split inside the GEMM (raw-A mode); it must match the separate split pass (LCU_NO_RAW_A=1)
+bit for bit, and shapes it cannot take (K % 4 != 0) fall back to the pass."""
 import os
 
 import numpy as np
@@ -86,5 +88,25 @@ def test_cached_equals_per_run_split(device):
         per_run = run()
     finally:
         del os.environ["LCU_NO_WEIGHT_CACHE"]
+    os.environ["LCU_NO_RAW_A"] = "1"      # A split by a separate pass instead of inside the GEMM
+    try:
+        a_split = run()
+    finally:
+        del os.environ["LCU_NO_RAW_A"]
     assert np.array_equal(cached, per_run)
+    assert np.array_equal(cached, a_split)
     assert_close(cached, np.maximum(xa @ wa + ba, 0), 1e-4)
+
+
+@pytest.mark.parametrize("k", [510, 513, 1000])
+def test_raw_a_shapes(device, k):
+    g = L.Graph()
+    x, w = g.input(300, k), g.input(k, 200)
+    y = g.matmul(x, w)
+    s = g.schedule()
+    device.bind(s)
+    xa, wa = rnd(31, 300, k), rnd(32, k, 200)
+    device.upload(x, xa)
+    device.upload(w, wa)
+    device.execute(s)
+    assert_close(device.download(y), xa @ wa, 1e-4)
