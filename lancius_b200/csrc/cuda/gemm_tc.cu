@@ -7,7 +7,8 @@
 //
 //   warp 0      TMA producer (one elected lane)
 //   warp 1      TMEM allocation + tcgen05.mma issue (one lane)
-//   warps 2-5   epilogue: tcgen05.ld -> +bias -> ReLU/GELU -> +residual -> global
+//   warps 2-9   epilogue: tcgen05.ld -> +bias -> ReLU/GELU -> +residual -> global
+//               (two warps per TMEM lane quadrant; in raw-A mode they also split A)
 //
 // Tile 128 x 256 x 16: A K-major in 64-byte swizzle, B N-major in the 128-byte
 // swizzle with 32-byte atoms (the only N-major layout tcgen05 accepts for TF32;
@@ -19,20 +20,41 @@
 #ifndef LCU_GEMM_DEBUG
 #define LCU_GEMM_DEBUG 0
 #endif
+#include <algorithm>
 #include <mutex>
 #include <vector>
 
 namespace {
 
-constexpr int BM = 256, BN = 256, BK = 16, STAGES = 3, THREADS = 192;
+constexpr int BM = 256, BN = 256, BK = 16, STAGES = 3;
+constexpr int EPI_WARPS = 8;                         // two per TMEM lane quadrant
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int A_TILE = BM * BK * 4;                  // 16 KB (two 128-row halves)
 constexpr int B_CHUNK = BK * 32 * 4;                 // 2 KB: 16 k-rows x 32 n
 constexpr int B_TILE = BN * BK * 4;                  // 16 KB
 constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE; // 64 KB
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + BN * 4 /*bias slice*/;
 constexpr uint32_t TMEM_COLS = 512;   // two 128x256 FP32 accumulators (rows 0-127, 128-255)
 
 __device__ int g_gemm_watchdog = 0;
+
+// Optional per-CTA phase timestamps (%globaltimer) for tuning; compiled out unless built
+// with -DLCU_GEMM_TRACE=1 (then lcu_gemm_trace_dump copies them out).
+#ifndef LCU_GEMM_TRACE
+#define LCU_GEMM_TRACE 0
+#endif
+#if LCU_GEMM_TRACE
+__device__ unsigned long long g_gtrace[2048][8];
+__device__ __forceinline__ unsigned long long gtime() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+#define GTRACE(slot) do { unsigned cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z); \
+    if (cta_ < 2048) g_gtrace[cta_][slot] = gtime(); } while (0)
+#else
+#define GTRACE(slot) do {} while (0)
+#endif
 
 struct Smem {
     uint64_t full[STAGES];
@@ -64,10 +86,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
     const int k_end = min(K, k_begin + kchunk);
     const int KT = (k_end - k_begin + BK - 1) / BK;
     volatile int* abort = &sm->abort;
+    if (threadIdx.x == 0) GTRACE(0);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            tc::mbar_init(&sm->full[s], 1); tc::mbar_init(&sm->empty[s], 1); tc::mbar_init(&sm->conv[s], 4);
+            tc::mbar_init(&sm->full[s], 1); tc::mbar_init(&sm->empty[s], 1); tc::mbar_init(&sm->conv[s], EPI_WARPS);
         }
         tc::mbar_init(&sm->accum, 1);
         tc::mbar_init(&sm->drain, 1);
@@ -88,7 +111,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
 
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer ----------------
-        // raw-A mode: only the FP32 A tile arrives; warps 2-5 split it into hi/lo in place
+        // raw-A mode: only the FP32 A tile arrives; the epilogue warps split it into hi/lo in place
         const uint32_t tx = a_maps ? (passes > 1 ? A_TILE + 2 * B_TILE : A_TILE + B_TILE)
                                    : (passes > 1 ? STAGE_BYTES : A_TILE + B_TILE);
         const int ga = groups[g].aidx, gb = groups[g].bidx;      // scratch slots of this group's operands
@@ -99,11 +122,15 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
             uint8_t* st = tiles + s * STAGE_BYTES;
             tc::mbar_expect_tx(&sm->full[s], tx);
             int k0 = k_begin + kt * BK;
-            tc::tma_load_3d(st, ma, &sm->full[s], k0, m0, a_maps ? 0 : ga);
+            tc::tma_load_3d(st, ma, &sm->full[s], k0, m0, a_maps ? 0 : ga);               // A: two 128-row boxes
+            tc::tma_load_3d(st + A_TILE / 2, ma, &sm->full[s], k0, m0 + 128, a_maps ? 0 : ga);
             for (int j = 0; j < BN / 32; j++)
                 tc::tma_load_3d(st + 2 * A_TILE + j * B_CHUNK, &tb_hi, &sm->full[s], n0 + 32 * j, k0, gb);
             if (passes > 1) {
-                if (!a_maps) tc::tma_load_3d(st + A_TILE, &ta_lo, &sm->full[s], k0, m0, ga);
+                if (!a_maps) {
+                    tc::tma_load_3d(st + A_TILE, &ta_lo, &sm->full[s], k0, m0, ga);
+                    tc::tma_load_3d(st + A_TILE + A_TILE / 2, &ta_lo, &sm->full[s], k0, m0 + 128, ga);
+                }
                 for (int j = 0; j < BN / 32; j++)
                     tc::tma_load_3d(st + 2 * A_TILE + B_TILE + j * B_CHUNK, &tb_lo, &sm->full[s], n0 + 32 * j, k0, gb);
             }
@@ -118,6 +145,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
             if (!tc::mbar_wait(a_maps ? &sm->conv[s] : &sm->full[s], (kt / STAGES) & 1, abort, &g_gemm_watchdog, 2)) {
                 ok = false; break;
             }
+            if (kt == 0) GTRACE(1);
             tc::tc_fence_after();
             if (LCU_GEMM_DEBUG && blockIdx.x == 0 && blockIdx.y == 0 && kt == 0) {
                 const float* fa = reinterpret_cast<const float*>(tiles + s * STAGE_BYTES);
@@ -161,7 +189,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
                 if (!tc::mbar_wait(&sm->full[s], (kt / STAGES) & 1, abort, &g_gemm_watchdog, 4)) break;
                 float4* a4 = reinterpret_cast<float4*>(tiles + s * STAGE_BYTES);
 #pragma unroll 4
-                for (int i = threadIdx.x - 64; i < A_TILE / 16; i += 128) {
+                for (int i = threadIdx.x - 64; i < A_TILE / 16; i += 32 * EPI_WARPS) {
                     const float4 x = a4[i];
                     const float4 h = make_float4(tc::tf32_rna(x.x), tc::tf32_rna(x.y), tc::tf32_rna(x.z), tc::tf32_rna(x.w));
                     a4[i] = h;
@@ -175,105 +203,126 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
             }
         }
         // ---------------- epilogue ----------------
-        if (tc::mbar_wait(&sm->accum, 0, abort, &g_gemm_watchdog, 3)) {
-            tc::tc_fence_after();
-            LcuGemmGroup gr = groups[g];
-            if (splits > 1) {   // raw partial sums; the reduction applies the epilogue
-                gr.c = partial + (size_t)blockIdx.z * M * N;
-                gr.bias = nullptr; gr.resid = nullptr;
+        // Set-up that needs no accumulator runs while the last MMAs retire: the tile's bias
+        // slice goes to shared memory and the first residual rows are put in flight.
+        LcuGemmGroup gr = groups[g];
+        if (splits > 1) {   // raw partial sums; the reduction applies the epilogue
+            gr.c = partial + (size_t)blockIdx.z * M * N;
+            gr.bias = nullptr; gr.resid = nullptr;
+        }
+        const int epi_here = splits > 1 ? LCU_EPI_NONE : epi;
+        float* sbias = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(sm) + 256);
+        for (int i = threadIdx.x - 64; i < BN; i += 32 * EPI_WARPS)
+            sbias[i] = (gr.bias && n0 + i < N) ? __ldg(gr.bias + n0 + i) : 0.f;
+        asm volatile("bar.sync 1, %0;" ::"n"(32 * EPI_WARPS) : "memory");      // the epilogue warps
+        // Each warp owns 32 TMEM lanes (rows) and every other 32-column chunk of them (two
+        // warps per lane quadrant). Per chunk it stages the 32x32 block in shared memory
+        // (the drained pipeline buffers) and writes it back by rows: every store
+        // instruction covers whole 128-byte row segments (coalesced). The warp's next
+        // chunk's TMEM load and residual rows are in flight meanwhile.
+        const int q = warp & 3;                    // TMEM lane quadrant of this warp
+        constexpr int PARTS = EPI_WARPS / 4;       // warps sharing a quadrant
+        const int part = (warp - 2) >> 2;
+        // float4 path: every pointer 16-byte aligned and rows a multiple of 4 floats
+        const bool v4 = N % 4 == 0 && !conv_hw && ((reinterpret_cast<uintptr_t>(gr.c) | reinterpret_cast<uintptr_t>(gr.resid) |
+                                                    reinterpret_cast<uintptr_t>(gr.bias)) & 15) == 0 &&
+                        (!DST || (dst.ldc % 4 == 0 && dst.col_off % 4 == 0));
+        // residual rows of a chunk, 8 per lane (the float4 path's lane mapping)
+        auto load_res = [&](int row0, int cc, float4 (&rv)[8]) {
+            const int col = n0 + cc + 4 * (lane & 7);
+#pragma unroll
+            for (int it = 0; it < 8; it++) {
+                const int row = row0 + 4 * it + (lane >> 3);
+                rv[it] = (gr.resid && v4 && row < M && col < N)
+                             ? *reinterpret_cast<const float4*>(gr.resid + (size_t)row * N + col)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            const int epi_here = splits > 1 ? LCU_EPI_NONE : epi;
-            // Each warp owns 32 TMEM lanes (rows). Per 32-column chunk it stages the 32x32
-            // block in shared memory (the drained pipeline buffers) and writes it back by
-            // rows: every store instruction covers whole 128-byte row segments (coalesced),
-            // and the loop body (bias, activation, residual, destination) stays small
-            // instead of being unrolled 32-fold.
-            const int q = warp & 3;                    // TMEM lane quadrant of this warp
-            float* sb = reinterpret_cast<float*>(tiles) + (size_t)q * 32 * 36;
-            // float4 path: every pointer 16-byte aligned and rows a multiple of 4 floats
-            const bool v4 = N % 4 == 0 && !conv_hw && ((reinterpret_cast<uintptr_t>(gr.c) | reinterpret_cast<uintptr_t>(gr.resid) |
-                                                        reinterpret_cast<uintptr_t>(gr.bias)) & 15) == 0 &&
-                            (!DST || (dst.ldc % 4 == 0 && dst.col_off % 4 == 0));
-            // residual rows of a chunk, 8 per lane (the float4 path's lane mapping); the next
-            // chunk's are fetched while this one is stored, so HBM latency is paid once per half
-            auto load_res = [&](int row0, int cc, float4 (&rv)[8]) {
-                const int col = n0 + cc + 4 * (lane & 7);
-#pragma unroll
-                for (int it = 0; it < 8; it++) {
-                    const int row = row0 + 4 * it + (lane >> 3);
-                    rv[it] = (gr.resid && v4 && row < M && col < N)
-                                 ? *reinterpret_cast<const float4*>(gr.resid + (size_t)row * N + col)
-                                 : make_float4(0.f, 0.f, 0.f, 0.f);
-                }
+        };
+        const int nh = m0 + 128 < M ? 2 : 1;                         // row halves present
+        const int nc = (min(BN, N - n0) + 31) / 32;                   // 32-column chunks present
+        float4 rv[8];
+        if (part < nh * nc) load_res(m0 + (part / nc) * 128 + 32 * q, (part % nc) * 32, rv);
+        if (threadIdx.x == 64) GTRACE(2);
+        if (tc::mbar_wait(&sm->accum, 0, abort, &g_gemm_watchdog, 3)) {
+            if (threadIdx.x == 64) GTRACE(3);
+            tc::tc_fence_after();
+            float* sb = reinterpret_cast<float*>(tiles) + (size_t)(warp - 2) * 32 * 36;
+            auto taddr = [&](int i) {
+                return tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((i / nc) * BN + (i % nc) * 32);
             };
-            for (int half = 0; half < 2; half++) {
+            const int total = nh * nc;
+            uint32_t va[32];
+            if (part < total) tc::tmem_ld32_issue(taddr(part), va);
+            for (int i = part; i < total; i += PARTS) {
+                const int half = i / nc, c = (i % nc) * 32;
                 const int row0 = m0 + half * 128 + 32 * q;
-                if (m0 + half * 128 >= M) break;       // warp-uniform
-                float4 rv[8];
-                load_res(row0, 0, rv);
-                for (int c = 0; c < BN; c += 32) {
-                    if (n0 + c >= N) break;            // warp-uniform
-                    float4 rn[8];
-                    load_res(row0, c + 32, rn);        // next chunk's residuals in flight
-                    float v[32];
-                    tc::tmem_ld32(tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)(half * BN + c), v);
+                tc::tmem_ld_wait(va);
 #pragma unroll
-                    for (int j = 0; j < 32; j += 4)
-                        *reinterpret_cast<float4*>(sb + lane * 36 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                    __syncwarp();
-                    if (v4) {
-                        // 8 lanes per row, 4 columns each: 4 rows (128-byte segments) per step
-                        const int col = n0 + c + 4 * (lane & 7);
-                        if (col < N) {
-                            const float4 bv = gr.bias ? __ldg(reinterpret_cast<const float4*>(gr.bias + col))
-                                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(sb + lane * 36 + j) =
+                        make_float4(__uint_as_float(va[j]), __uint_as_float(va[j + 1]), __uint_as_float(va[j + 2]),
+                                    __uint_as_float(va[j + 3]));
+                __syncwarp();
+                float4 rn[8];
+                const int nx = i + PARTS;
+                if (nx < total) {
+                    tc::tmem_ld32_issue(taddr(nx), va);
+                    load_res(m0 + (nx / nc) * 128 + 32 * q, (nx % nc) * 32, rn);
+                }
+                if (v4) {
+                    // 8 lanes per row, 4 columns each: 4 rows (128-byte segments) per step
+                    const int cl = c + 4 * (lane & 7), col = n0 + cl;
+                    if (col < N) {
+                        const float4 bv = *reinterpret_cast<const float4*>(sbias + cl);
 #pragma unroll
-                            for (int it = 0; it < 8; it++) {
-                                const int r = 4 * it + (lane >> 3), row = row0 + r;
-                                if (row >= M) break;
-                                float4 x = *reinterpret_cast<const float4*>(sb + r * 36 + 4 * (lane & 7));
-                                x.x = lcu_apply_epi(x.x + bv.x, epi_here); x.y = lcu_apply_epi(x.y + bv.y, epi_here);
-                                x.z = lcu_apply_epi(x.z + bv.z, epi_here); x.w = lcu_apply_epi(x.w + bv.w, epi_here);
-                                x.x += rv[it].x; x.y += rv[it].y; x.z += rv[it].z; x.w += rv[it].w;   // zeros without a residual
-                                if (DST && splits == 1) {
-                                    const size_t o = (size_t)row * dst.ldc + dst.col_off + col;
-                                    for (int k = 0; k < dst.n_dst; k++) *reinterpret_cast<float4*>(dst.ptr[k] + o) = x;
-                                } else {
-                                    *reinterpret_cast<float4*>(gr.c + (size_t)row * N + col) = x;
-                                }
-                            }
-                        }
-                    } else {
-                        // any shape: lane j takes column j of each row (coalesced per row)
-                        const int col = n0 + c + lane;
-                        if (col < N) {
-                            const float bv = gr.bias ? __ldg(gr.bias + col) : 0.f;
-#pragma unroll 4
-                            for (int r = 0; r < 32; r++) {
-                                const int row = row0 + r;
-                                if (row >= M) break;
-                                float x = lcu_apply_epi(sb[r * 36 + lane] + bv, epi_here);
-                                if (conv_hw && splits == 1) {
-                                    // implicit-GEMM conv: row = output channel, column = n*HoWo + pixel -> NCHW
-                                    gr.c[(size_t)(col / conv_hw) * M * conv_hw + (size_t)row * conv_hw + col % conv_hw] = x;
-                                    continue;
-                                }
-                                if (gr.resid) x += gr.resid[(size_t)row * N + col];
-                                if (DST && splits == 1) {   // fused all-gather: straight into every rank's C
-                                    const size_t o = (size_t)row * dst.ldc + dst.col_off + col;
-                                    for (int k = 0; k < dst.n_dst; k++) dst.ptr[k][o] = x;
-                                } else {
-                                    gr.c[(size_t)row * N + col] = x;
-                                }
+                        for (int it = 0; it < 8; it++) {
+                            const int r = 4 * it + (lane >> 3), row = row0 + r;
+                            if (row >= M) break;
+                            float4 x = *reinterpret_cast<const float4*>(sb + r * 36 + 4 * (lane & 7));
+                            x.x = lcu_apply_epi(x.x + bv.x, epi_here); x.y = lcu_apply_epi(x.y + bv.y, epi_here);
+                            x.z = lcu_apply_epi(x.z + bv.z, epi_here); x.w = lcu_apply_epi(x.w + bv.w, epi_here);
+                            x.x += rv[it].x; x.y += rv[it].y; x.z += rv[it].z; x.w += rv[it].w;   // zeros without a residual
+                            if (DST && splits == 1) {
+                                const size_t o = (size_t)row * dst.ldc + dst.col_off + col;
+                                for (int k = 0; k < dst.n_dst; k++) *reinterpret_cast<float4*>(dst.ptr[k] + o) = x;
+                            } else {
+                                *reinterpret_cast<float4*>(gr.c + (size_t)row * N + col) = x;
                             }
                         }
                     }
-                    __syncwarp();
+                } else {
+                    // any shape: lane j takes column j of each row (coalesced per row)
+                    const int col = n0 + c + lane;
+                    if (col < N) {
+                        const float bv = sbias[c + lane];
+#pragma unroll 4
+                        for (int r = 0; r < 32; r++) {
+                            const int row = row0 + r;
+                            if (row >= M) break;
+                            float x = lcu_apply_epi(sb[r * 36 + lane] + bv, epi_here);
+                            if (conv_hw && splits == 1) {
+                                // implicit-GEMM conv: row = output channel, column = n*HoWo + pixel -> NCHW
+                                gr.c[(size_t)(col / conv_hw) * M * conv_hw + (size_t)row * conv_hw + col % conv_hw] = x;
+                                continue;
+                            }
+                            if (gr.resid) x += gr.resid[(size_t)row * N + col];
+                            if (DST && splits == 1) {   // fused all-gather: straight into every rank's C
+                                const size_t o = (size_t)row * dst.ldc + dst.col_off + col;
+                                for (int k = 0; k < dst.n_dst; k++) dst.ptr[k][o] = x;
+                            } else {
+                                gr.c[(size_t)row * N + col] = x;
+                            }
+                        }
+                    }
+                }
+                __syncwarp();
+                if (nx < total) {
 #pragma unroll
                     for (int it = 0; it < 8; it++) rv[it] = rn[it];
                 }
             }
             if (DST) __threadfence_system();   // peer stores complete before the kernel does
+            if (threadIdx.x == 64) GTRACE(4);
         }
     }
 
@@ -296,7 +345,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem, TMEM_COLS);
     }
+    if (threadIdx.x == 0) GTRACE(5);
 }
+
+
+
 
 // hi/lo split of `count` row-major [rows, cols] operands into pitched scratch. Rows are
 // walked by the grid and columns by the block: float4 in and out when cols % 4 == 0 and
@@ -458,10 +511,10 @@ extern "C" lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, si
     p->splits = split_count(K);
     p->kchunk = p->splits > 1 ? (int)(((K + p->splits - 1) / p->splits + BK - 1) / BK * BK) : (int)(K ? K : 1);
     p->partial = p->splits > 1 ? (float*)s : nullptr;
-    bool ok = make_map(&p->a_hi, p->s_ahi, K, M, Ga, p->Kp, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B) &&
+    bool ok = make_map(&p->a_hi, p->s_ahi, K, M, Ga, p->Kp, BK, 128, CU_TENSOR_MAP_SWIZZLE_64B) &&
               make_map(&p->b_hi, p->s_bhi, N, K, Gb, p->Np, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     if (ok && passes > 1)
-        ok = make_map(&p->a_lo, p->s_alo, K, M, Ga, p->Kp, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B) &&
+        ok = make_map(&p->a_lo, p->s_alo, K, M, Ga, p->Kp, BK, 128, CU_TENSOR_MAP_SWIZZLE_64B) &&
              make_map(&p->b_lo, p->s_blo, N, K, Gb, p->Np, 32, BK, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
     else if (ok) { p->a_lo = p->a_hi; p->b_lo = p->b_hi; }
     if (!ok) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
@@ -481,7 +534,7 @@ extern "C" lancius_error lcu_gemm_tc_use_presplit_b(LcuTcGemmPlan* p, float* b_h
 
 extern "C" bool lcu_gemm_tc_make_raw_a_map(CUtensorMap* m, const float* a, size_t M, size_t K) {
     if (K % 4 || (reinterpret_cast<uintptr_t>(a) & 15) || !M || !K) return false;
-    return make_map(m, a, K, M, 1, K, BK, BM, CU_TENSOR_MAP_SWIZZLE_64B);
+    return make_map(m, a, K, M, 1, K, BK, 128, CU_TENSOR_MAP_SWIZZLE_64B);   // 128-row boxes
 }
 
 extern "C" lancius_error lcu_gemm_tc_use_raw_a(LcuTcGemmPlan* p, const CUtensorMap* d_maps) {
@@ -489,6 +542,12 @@ extern "C" lancius_error lcu_gemm_tc_use_raw_a(LcuTcGemmPlan* p, const CUtensorM
     p->d_amaps = d_maps;
     return LANCIUS_ERROR_OK;
 }
+
+#if LCU_GEMM_TRACE
+extern "C" int lcu_gemm_trace_dump(unsigned long long* host, int ctas) {
+    return cudaMemcpyFromSymbol(host, g_gtrace, (size_t)ctas * 8 * sizeof(unsigned long long)) == cudaSuccess ? 0 : -1;
+}
+#endif
 
 extern "C" lancius_error lcu_tf32_split_rows(const float* src, size_t rows, size_t cols, size_t pitch, float* hi, float* lo,
                                              void* stream) {

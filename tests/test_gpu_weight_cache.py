@@ -110,3 +110,33 @@ def test_raw_a_shapes(device, k):
     device.upload(w, wa)
     device.execute(s)
     assert_close(device.download(y), xa @ wa, 1e-4)
+
+
+# grouped waves, ragged edges (M, N not multiples of the 256x256 tile, odd chunk counts per
+# epilogue warp) and the fused bias/ReLU/residual epilogue, against FP64
+EPI_SHAPES = [(256, 8192, 256, 1), (1000, 4096, 1000, 1), (512, 768, 768, 16), (300, 1000, 200, 3), (8192, 3072, 768, 1),
+              (130, 64, 40, 2)]
+
+
+@pytest.mark.parametrize("m,k,n,groups", EPI_SHAPES)
+def test_gemm_epilogue_shapes(device, m, k, n, groups):
+    g = L.Graph()
+    w, bias = g.input(k, n), g.input(1, n)
+    xs = [g.input(m, k) for _ in range(groups)]
+    rs = [g.input(m, n) for _ in range(groups)]
+    ys = [g.add(g.relu(g.add(g.matmul(x, w), g.broadcast(bias, m, n))), r) for x, r in zip(xs, rs)]
+    s = g.schedule()
+    wa, ba = rnd(41, k, n), rnd(42, 1, n)
+    xa = [rnd(50 + i, m, k) for i in range(groups)]
+    ra = [rnd(70 + i, m, n) for i in range(groups)]
+    device.bind(s)
+    device.upload(w, wa)
+    device.upload(bias, ba)
+    for node, a in zip(xs + rs, xa + ra):
+        device.upload(node, a)
+    device.execute(s)
+    out = [device.download(y) for y in ys]
+    for i in range(groups):
+        assert_close(out[i], np.maximum(xa[i] @ wa + ba, 0) + ra[i], 1e-4)
+    device.execute(s)                         # a rerun gives the same bytes
+    assert all(np.array_equal(device.download(y), a) for y, a in zip(ys, out))
