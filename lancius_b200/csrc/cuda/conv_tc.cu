@@ -5,8 +5,9 @@
 //
 //   C[Co][P] = W'[Co][K'] . X'[P][K']^T,  P = N*Ho*Wo,  K' = (kh, kw, ci)
 //
-// The input is rewritten once as NHWC TF32 hi/lo copies (one pass over it, instead
-// of the Kh*Kw-times larger im2col). For one k-step (kh, kw, 16 channels) the B tile
+// The input is rewritten once as NHWC FP32 (one pass over it, instead of the
+// Kh*Kw-times larger im2col); the epilogue warps split each loaded tile into TF32
+// hi/lo in shared memory while the MMAs of earlier stages run. For one k-step (kh, kw, 16 channels) the B tile
 // of r whole output rows (r * Wo <= 256 pixels of one image) is ONE 4-D TMA load at
 // (c, kw - pad, ho0*s - pad + kh, n) with both spatial traversal strides set to the
 // conv stride, so the hardware performs the gather and the padding (out-of-range
@@ -21,6 +22,8 @@
 // r with r * Wo % 16 == 0, K' <= 8192.
 // Every mbarrier wait is bounded; a timeout sets the watchdog word and unwinds.
 #include "tc_common.cuh"
+#include <algorithm>
+#include <cstdlib>
 #include <mutex>
 
 namespace {
@@ -35,7 +38,7 @@ constexpr uint32_t TMEM_COLS = 512;
 __device__ int g_conv_watchdog = 0;
 
 struct Smem {
-    uint64_t full[STAGES], empty[STAGES], accum, drain;
+    uint64_t full[STAGES], empty[STAGES], conv[STAGES], accum, drain;
     uint32_t tmem;
     int abort, consumed;
 };
@@ -45,6 +48,7 @@ struct ConvArgs {
     int rows;        // output rows per tile: the tile is rows x Wo pixels of one image
     int halves;      // 1 when Co <= 128
     int passes, relu;
+    int raw_b;       // 1: the input map covers plain FP32 NHWC; the epilogue warps split it on chip
 };
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
@@ -73,14 +77,16 @@ k_conv_tc(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
     volatile int* abort = &sm->abort;
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < STAGES; s++) { tc::mbar_init(&sm->full[s], 1); tc::mbar_init(&sm->empty[s], 1); }
+        for (int s = 0; s < STAGES; s++) {
+            tc::mbar_init(&sm->full[s], 1); tc::mbar_init(&sm->empty[s], 1); tc::mbar_init(&sm->conv[s], 4);
+        }
         tc::mbar_init(&sm->accum, 1);
         tc::mbar_init(&sm->drain, 1);
         sm->abort = 0;
         sm->consumed = 0;
         tc::fence_barrier_init();
         tc::prefetch_tmap(&tw_hi); tc::prefetch_tmap(&tx_hi);
-        if (a.passes > 1) { tc::prefetch_tmap(&tw_lo); tc::prefetch_tmap(&tx_lo); }
+        if (a.passes > 1) { tc::prefetch_tmap(&tw_lo); if (!a.raw_b) tc::prefetch_tmap(&tx_lo); }
     }
     if (warp == 1) tc::tmem_alloc(&sm->tmem, TMEM_COLS);
     tc::tc_fence_before();
@@ -92,7 +98,8 @@ k_conv_tc(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer ----------------
         // a box counts all of its bytes, the zero-filled out-of-range part included
-        const uint32_t tx = (a.passes > 1 ? 2u : 1u) * (uint32_t)(A_TILE + bn * BK * 4);
+        const uint32_t tx = a.raw_b ? (a.passes > 1 ? 2u : 1u) * (uint32_t)A_TILE + (uint32_t)(bn * BK * 4)
+                                    : (a.passes > 1 ? 2u : 1u) * (uint32_t)(A_TILE + bn * BK * 4);
         for (int kt = 0; kt < KT; kt++) {
             const int s = kt % STAGES;
             if (kt >= STAGES && !tc::mbar_wait(&sm->empty[s], ((kt / STAGES) - 1) & 1, abort, &g_conv_watchdog, 1)) break;
@@ -105,7 +112,7 @@ k_conv_tc(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
             const int ix = -a.pad + kw, iy = ho0 * a.stride - a.pad + kh;
             uint8_t* dst = st + 2 * A_TILE;
             tma_load_4d(dst, &tx_hi, &sm->full[s], cb * BK, ix, iy, img);
-            if (a.passes > 1) tma_load_4d(dst + B_TILE, &tx_lo, &sm->full[s], cb * BK, ix, iy, img);
+            if (a.passes > 1 && !a.raw_b) tma_load_4d(dst + B_TILE, &tx_lo, &sm->full[s], cb * BK, ix, iy, img);
             issued = kt + 1;
         }
     } else if (warp == 1 && lane == 0) {
@@ -114,7 +121,9 @@ k_conv_tc(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
         bool ok = true;
         for (int kt = 0; kt < KT; kt++) {
             const int s = kt % STAGES;
-            if (!tc::mbar_wait(&sm->full[s], (kt / STAGES) & 1, abort, &g_conv_watchdog, 2)) { ok = false; break; }
+            if (!tc::mbar_wait(a.raw_b ? &sm->conv[s] : &sm->full[s], (kt / STAGES) & 1, abort, &g_conv_watchdog, 2)) {
+                ok = false; break;
+            }
             tc::tc_fence_after();
             const uint32_t st = tc::smem_u32(tiles + s * STAGE_BYTES);
             const uint32_t a_hi = st, a_lo = st + A_TILE, b_hi = st + 2 * A_TILE, b_lo = b_hi + B_TILE;
@@ -141,6 +150,29 @@ k_conv_tc(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
         }
         if (ok) tc::mma_commit(&sm->accum);
     } else if (warp >= 2) {
+        if (a.raw_b) {
+            // ---------------- input splitter (raw-B mode) ----------------
+            // hi = rna_tf32(x) in place, lo = rna_tf32(x - hi) into the stage's lo slot; the
+            // swizzle permutes 16-byte chunks identically in both, so a flat pass suffices
+            const int n4 = bn * BK / 4;
+            for (int kt = 0; kt < KT; kt++) {
+                const int s = kt % STAGES;
+                if (!tc::mbar_wait(&sm->full[s], (kt / STAGES) & 1, abort, &g_conv_watchdog, 4)) break;
+                float4* b4 = reinterpret_cast<float4*>(tiles + s * STAGE_BYTES + 2 * A_TILE);
+#pragma unroll 4
+                for (int i = threadIdx.x - 64; i < n4; i += 128) {
+                    const float4 x = b4[i];
+                    const float4 h = make_float4(tc::tf32_rna(x.x), tc::tf32_rna(x.y), tc::tf32_rna(x.z), tc::tf32_rna(x.w));
+                    b4[i] = h;
+                    if (a.passes > 1)
+                        b4[i + B_TILE / 16] = make_float4(tc::tf32_rna(x.x - h.x), tc::tf32_rna(x.y - h.y),
+                                                          tc::tf32_rna(x.z - h.z), tc::tf32_rna(x.w - h.w));
+                }
+                tc::fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&sm->conv[s]);
+            }
+        }
         // ---------------- epilogue: rows = output channels, columns = pixels ----------------
         if (tc::mbar_wait(&sm->accum, 0, abort, &g_conv_watchdog, 3)) {
             tc::tc_fence_after();
@@ -202,10 +234,199 @@ k_conv_tc(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
     }
 }
 
-// NCHW -> NHWC TF32 hi / lo (lo = 0 pointer: TF32 mode): per (n, h) tiles of 32
-// channels x 64 columns through shared memory, float4 on both sides (C % 4 == 0).
+// Persistent variant for output-channel tiles of 128: one CTA per SM walks the tiles
+// (pixel tile x 128-channel tile) round-robin; the accumulator of one tile takes 256
+// TMEM columns, so two of them alternate and the epilogue of a tile (TMEM -> ReLU ->
+// NCHW) overlaps the MMAs of the next. Roles as in k_conv_tc; the epilogue stages its
+// blocks in a dedicated XOR-swizzled buffer because the ring already holds the next
+// tile's stages. The input comes as NHWC TF32 hi/lo (pre-split).
+constexpr int PT_BM = 128, PT_STAGES = 4;
+constexpr int PT_A_TILE = PT_BM * BK * 4;                       // 8 KB
+constexpr int PT_STAGE_BYTES = 2 * PT_A_TILE + 2 * B_TILE;      // 48 KB
+constexpr int PT_SMEM_BYTES = PT_STAGES * PT_STAGE_BYTES + 4 * 32 * 32 * 4 + 1024 + 256;
+
+struct SmemPT {
+    uint64_t full[PT_STAGES], empty[PT_STAGES], acc_full[2], acc_empty[2], drain;
+    uint32_t tmem;
+    int abort, consumed;
+};
+
+__global__ void __launch_bounds__(THREADS, 1)
+k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap tw_lo,
+          const __grid_constant__ CUtensorMap tx_hi, const __grid_constant__ CUtensorMap tx_lo, float* __restrict__ out,
+          ConvArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float* stage_f = reinterpret_cast<float*>(tiles + PT_STAGES * PT_STAGE_BYTES);
+    SmemPT* sm = reinterpret_cast<SmemPT*>(stage_f + 4 * 32 * 32);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int hw = a.ho * a.wo;
+    const int tiles_per_img = (a.ho + a.rows - 1) / a.rows;
+    const int ct = (a.co + PT_BM - 1) / PT_BM;
+    const int T = a.n * tiles_per_img * ct;
+    const int bn = a.rows * a.wo;                    // pixels (MMA N) of a tile
+    const int CB = a.ci / BK, KT = a.kh * a.kw * CB;
+    volatile int* abort = &sm->abort;
+    auto coords = [&](int t, int& img, int& ho0, int& m0) {
+        const int pt = t / ct;
+        m0 = (t - pt * ct) * PT_BM;
+        img = pt / tiles_per_img;
+        ho0 = (pt - img * tiles_per_img) * a.rows;
+    };
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < PT_STAGES; s++) { tc::mbar_init(&sm->full[s], 1); tc::mbar_init(&sm->empty[s], 1); }
+        for (int b = 0; b < 2; b++) { tc::mbar_init(&sm->acc_full[b], 1); tc::mbar_init(&sm->acc_empty[b], 4); }
+        tc::mbar_init(&sm->drain, 1);
+        sm->abort = 0;
+        sm->consumed = 0;
+        tc::fence_barrier_init();
+        tc::prefetch_tmap(&tw_hi); tc::prefetch_tmap(&tx_hi);
+        if (a.passes > 1) { tc::prefetch_tmap(&tw_lo); tc::prefetch_tmap(&tx_lo); }
+    }
+    if (warp == 1) tc::tmem_alloc(&sm->tmem, TMEM_COLS);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = sm->tmem;
+    int issued = 0;
+
+    if (warp == 0 && lane == 0) {
+        // ---------------- TMA producer ----------------
+        const uint32_t tx = (a.passes > 1 ? 2u : 1u) * (uint32_t)(PT_A_TILE + bn * BK * 4);
+        int it = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < T && ok; t += gridDim.x) {
+            int img, ho0, m0;
+            coords(t, img, ho0, m0);
+            for (int kt = 0; kt < KT; kt++, it++) {
+                const int s = it % PT_STAGES;
+                if (it >= PT_STAGES && !tc::mbar_wait(&sm->empty[s], ((it / PT_STAGES) - 1) & 1, abort, &g_conv_watchdog, 11)) {
+                    ok = false; break;
+                }
+                const int cb = kt % CB, r = kt / CB, kw = r % a.kw, kh = r / a.kw;
+                uint8_t* st = tiles + s * PT_STAGE_BYTES;
+                tc::mbar_expect_tx(&sm->full[s], tx);
+                tc::tma_load_3d(st, &tw_hi, &sm->full[s], kt * BK, m0, 0);
+                if (a.passes > 1) tc::tma_load_3d(st + PT_A_TILE, &tw_lo, &sm->full[s], kt * BK, m0, 0);
+                const int ix = -a.pad + kw, iy = ho0 * a.stride - a.pad + kh;
+                uint8_t* dst = st + 2 * PT_A_TILE;
+                tma_load_4d(dst, &tx_hi, &sm->full[s], cb * BK, ix, iy, img);
+                if (a.passes > 1) tma_load_4d(dst + B_TILE, &tx_lo, &sm->full[s], cb * BK, ix, iy, img);
+                issued = it + 1;
+            }
+        }
+    } else if (warp == 1 && lane == 0) {
+        // ---------------- MMA issuer ----------------
+        const uint32_t idesc = tc::idesc_tf32(128, bn, false, false);
+        int it = 0, j = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; t < T && ok; t += gridDim.x, j++) {
+            const int b = j & 1;
+            if (j >= 2 && !tc::mbar_wait(&sm->acc_empty[b], ((j >> 1) - 1) & 1, abort, &g_conv_watchdog, 12)) break;
+            tc::tc_fence_after();
+            const uint32_t d = tmem + (uint32_t)b * 256;
+            for (int kt = 0; kt < KT; kt++, it++) {
+                const int s = it % PT_STAGES;
+                if (!tc::mbar_wait(&sm->full[s], (it / PT_STAGES) & 1, abort, &g_conv_watchdog, 13)) { ok = false; break; }
+                tc::tc_fence_after();
+                const uint32_t st = tc::smem_u32(tiles + s * PT_STAGE_BYTES);
+                const uint32_t a_hi = st, a_lo = st + PT_A_TILE, b_hi = st + 2 * PT_A_TILE, b_lo = b_hi + B_TILE;
+#pragma unroll
+                for (int kb = 0; kb < BK / 8; kb++) {
+                    const uint64_t dbh = tc::smem_desc(b_hi + kb * 32, 16, 512, tc::SWZ_64B);
+                    const uint64_t dah = tc::smem_desc(a_hi + kb * 32, 16, 512, tc::SWZ_64B);
+                    const uint32_t acc = (kt | kb) ? 1u : 0u;
+                    if (a.passes > 1) {
+                        const uint64_t dbl = tc::smem_desc(b_lo + kb * 32, 16, 512, tc::SWZ_64B);
+                        const uint64_t dal = tc::smem_desc(a_lo + kb * 32, 16, 512, tc::SWZ_64B);
+                        tc::mma_tf32(d, dal, dbh, idesc, acc);      // small terms first
+                        tc::mma_tf32(d, dah, dbl, idesc, 1u);
+                        tc::mma_tf32(d, dah, dbh, idesc, 1u);
+                    } else {
+                        tc::mma_tf32(d, dah, dbh, idesc, acc);
+                    }
+                }
+                tc::mma_commit(&sm->empty[s]);
+                sm->consumed = it + 1;
+            }
+            if (!ok) break;
+            tc::mma_commit(&sm->acc_full[b]);
+        }
+    } else if (warp >= 2) {
+        // ---------------- epilogue: rows = output channels, columns = pixels ----------------
+        const int q = warp & 3;
+        float* sb = stage_f + q * 32 * 32;           // 32x32 block, float4 slots XOR-swizzled by row
+        const bool v4base = hw % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+        int j = 0;
+        for (int t = blockIdx.x; t < T; t += gridDim.x, j++) {
+            const int b = j & 1;
+            int img, ho0, m0;
+            coords(t, img, ho0, m0);
+            if (!tc::mbar_wait(&sm->acc_full[b], (j >> 1) & 1, abort, &g_conv_watchdog, 14)) break;
+            tc::tc_fence_after();
+            const int valid = min(bn, (a.ho - ho0) * a.wo);
+            const bool v4 = v4base && ((size_t)ho0 * a.wo) % 4 == 0;
+            const int co0 = m0 + 32 * q;
+            const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)b * 256;
+            uint32_t va[32];
+            tc::tmem_ld32_issue(tbase, va);
+            for (int c = 0; c < bn; c += 32) {
+                tc::tmem_ld_wait(va);
+#pragma unroll
+                for (int jj = 0; jj < 8; jj++)
+                    *reinterpret_cast<float4*>(sb + lane * 32 + ((jj ^ (lane & 7)) << 2)) =
+                        make_float4(__uint_as_float(va[4 * jj]), __uint_as_float(va[4 * jj + 1]),
+                                    __uint_as_float(va[4 * jj + 2]), __uint_as_float(va[4 * jj + 3]));
+                __syncwarp();
+                if (c + 32 < bn) tc::tmem_ld32_issue(tbase + (uint32_t)(c + 32), va);
+                const int cl4 = lane & 7, px = c + 4 * cl4;
+#pragma unroll 2
+                for (int it = 0; it < 8; it++) {
+                    const int r = 4 * it + (lane >> 3), co = co0 + r;
+                    if (co >= a.co || px >= valid) continue;
+                    float4 x = *reinterpret_cast<const float4*>(sb + r * 32 + ((cl4 ^ (r & 7)) << 2));
+                    if (a.relu) { x.x = fmaxf(x.x, 0.f); x.y = fmaxf(x.y, 0.f); x.z = fmaxf(x.z, 0.f); x.w = fmaxf(x.w, 0.f); }
+                    float* o = out + ((size_t)img * a.co + co) * hw + (size_t)ho0 * a.wo + px;
+                    if (v4 && px + 4 <= valid) {
+                        *reinterpret_cast<float4*>(o) = x;
+                    } else {
+                        const float xv[4] = {x.x, x.y, x.z, x.w};
+                        for (int u = 0; u < 4 && px + u < valid; u++) o[u] = xv[u];
+                    }
+                }
+                __syncwarp();
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&sm->acc_empty[b]);
+        }
+    }
+
+    tc::tc_fence_before();
+    __syncthreads();
+    if (sm->abort) {
+        int never = 0;
+        if (warp == 0 && lane == 0)
+            for (int kt = sm->consumed; kt < issued; kt++)
+                if (!tc::mbar_wait(&sm->full[kt % PT_STAGES], (kt / PT_STAGES) & 1, &never, nullptr, 0)) break;
+        if (warp == 1 && lane == 0) {
+            tc::mma_commit(&sm->drain);
+            tc::mbar_wait(&sm->drain, 0, &never, nullptr, 0);
+        }
+        __syncthreads();
+    }
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, TMEM_COLS);
+    }
+}
+
+// NCHW -> NHWC, as TF32 hi / lo (lo = 0 pointer: TF32 mode) or plain FP32 (round = 0,
+// split later on chip): per (n, h) tiles of 32 channels x 64 columns through shared
+// memory, float4 on both sides (C % 4 == 0).
 __global__ void __launch_bounds__(256) k_nhwc_split(const float* __restrict__ in, float* __restrict__ hi,
-                                                    float* __restrict__ lo, int C, int H, int W) {
+                                                    float* __restrict__ lo, int C, int H, int W, int round) {
     __shared__ float t[32][65];
     const int nh = blockIdx.z, n = nh / H, h = nh % H;
     const int c0 = blockIdx.y * 32, w0 = blockIdx.x * 64;
@@ -231,7 +452,10 @@ __global__ void __launch_bounds__(256) k_nhwc_split(const float* __restrict__ in
         if (w0 + w >= W || c0 + c >= C) continue;
         float x[4] = {t[c][w], t[c + 1][w], t[c + 2][w], t[c + 3][w]}, xh[4], xl[4];
 #pragma unroll
-        for (int j = 0; j < 4; j++) { xh[j] = tc::tf32_rna(x[j]); xl[j] = tc::tf32_rna(x[j] - xh[j]); }
+        for (int j = 0; j < 4; j++) {
+            xh[j] = round ? tc::tf32_rna(x[j]) : x[j];
+            xl[j] = tc::tf32_rna(x[j] - xh[j]);
+        }
         const size_t o = (((size_t)n * H + h) * W + w0 + w) * C + c0 + c;
         *reinterpret_cast<float4*>(hi + o) = make_float4(xh[0], xh[1], xh[2], xh[3]);
         if (lo) *reinterpret_cast<float4*>(lo + o) = make_float4(xl[0], xl[1], xl[2], xl[3]);
@@ -286,7 +510,8 @@ bool configure() {
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev >= 0 && dev < 64 && done[dev]) return true;
-    if (cudaFuncSetAttribute(k_conv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+    if (cudaFuncSetAttribute(k_conv_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess ||
+        cudaFuncSetAttribute(k_conv_pt, cudaFuncAttributeMaxDynamicSharedMemorySize, PT_SMEM_BYTES) != cudaSuccess)
         return false;
     if (dev >= 0 && dev < 64) done[dev] = true;
     return true;
@@ -311,13 +536,20 @@ extern "C" lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const f
     cudaStream_t st = lcu_as_stream(stream);
     const size_t xe = (size_t)cs.n * cs.h * cs.w * cs.ci, K = (size_t)cs.ci * cs.kh * cs.kw, we = (size_t)cs.co * K;
     char* s = static_cast<char*>(scratch);
+    // persistent kernel (128-channel tiles, pre-split NHWC input) unless disabled; the
+    // one-launch-per-tile kernel takes the input NHWC as plain FP32 and splits it on chip
+    static int n_sm = 0;
+    if (!n_sm) { int dev = 0; cudaGetDevice(&dev); cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev); }
+    const char* nopt = getenv("LCU_CONV_NO_PT");
+    const bool pt = !(nopt && nopt[0] == '1') && n_sm > 0;
+    const int raw = (pt || lcu_no_raw_a()) ? 0 : 1;
     float* xh = reinterpret_cast<float*>(s); s += al256(xe * 4);
-    float* xl = passes > 1 ? reinterpret_cast<float*>(s) : nullptr; if (passes > 1) s += al256(xe * 4);
+    float* xl = passes > 1 && !raw ? reinterpret_cast<float*>(s) : nullptr; if (passes > 1) s += al256(xe * 4);
     float* wh = reinterpret_cast<float*>(s); s += al256(we * 4);
     float* wl = passes > 1 ? reinterpret_cast<float*>(s) : nullptr;
 
     k_nhwc_split<<<dim3((unsigned)((cs.w + 63) / 64), (unsigned)((cs.ci + 31) / 32), (unsigned)(cs.n * cs.h)), 256, 0, st>>>(
-        in, xh, xl, cs.ci, cs.h, cs.w);
+        in, xh, xl, cs.ci, cs.h, cs.w, raw ? 0 : 1);
     lcu_note_launch();
     k_weight_khwc_split<<<lcu_blocks(we, 256), 256, 0, st>>>(w, wh, wl, cs.co, cs.ci, cs.kh, cs.kw);
     lcu_note_launch();
@@ -329,10 +561,10 @@ extern "C" lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const f
     const int rows = pick_rows(cs.wo, cs.ho, cs.stride);
     CUtensorMap mw_hi, mw_lo, mx_hi, mx_lo;
     bool ok = true;
-    {   // weights: [1][Co][K] rows of K floats, box {16, 256}
+    {   // weights: [1][Co][K] rows of K floats, box {16, 256} (128 rows for the persistent kernel)
         cuuint64_t dims[3] = {K, (cuuint64_t)cs.co, 1};
         cuuint64_t strides[2] = {K * 4, we * 4};
-        cuuint32_t box[3] = {BK, BM, 1}, es[3] = {1, 1, 1};
+        cuuint32_t box[3] = {BK, pt ? (cuuint32_t)PT_BM : (cuuint32_t)BM, 1}, es[3] = {1, 1, 1};
         ok = ok && fn(&mw_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, wh, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                       CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
         if (passes > 1)
@@ -347,13 +579,19 @@ extern "C" lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const f
         cuuint32_t es[4] = {1, (cuuint32_t)cs.stride, (cuuint32_t)cs.stride, 1};
         ok = ok && fn(&mx_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xh, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                       CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-        if (passes > 1)
+        if (xl)
             ok = ok && fn(&mx_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xl, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
                           CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
         else mx_lo = mx_hi;
     }
     if (!ok) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
-    ConvArgs a{cs.n, cs.ci, cs.co, cs.kh, cs.kw, cs.stride, cs.pad, cs.ho, cs.wo, rows, cs.co > 128 ? 2 : 1, passes, relu};
+    ConvArgs a{cs.n, cs.ci, cs.co, cs.kh, cs.kw, cs.stride, cs.pad, cs.ho, cs.wo, rows, cs.co > 128 ? 2 : 1, passes, relu, raw};
+    if (pt) {
+        const long long T = (long long)cs.n * ((cs.ho + rows - 1) / rows) * ((cs.co + PT_BM - 1) / PT_BM);
+        k_conv_pt<<<(unsigned)std::min<long long>(T, n_sm), THREADS, PT_SMEM_BYTES, st>>>(mw_hi, mw_lo, mx_hi, mx_lo, out, a);
+        lcu_note_launch();
+        return lcu_launch_status();
+    }
     dim3 grid((unsigned)(cs.n * ((cs.ho + rows - 1) / rows)), (unsigned)((cs.co + BM - 1) / BM));
     k_conv_tc<<<grid, THREADS, SMEM_BYTES, st>>>(mw_hi, mw_lo, mx_hi, mx_lo, out, a);
     lcu_note_launch();

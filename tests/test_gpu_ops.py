@@ -123,6 +123,26 @@ def test_conv2d(lib, orc, shape, relu):
     assert_close(out.cpu().numpy(), ref, 1e-4)
 
 
+@pytest.mark.parametrize("shape", [(2, 64, 32, 32, 128, 3, 3, 1, 1), (2, 16, 64, 64, 48, 5, 5, 2, 2)])
+def test_conv2d_split_on_chip_matches_split_pass(lib, shape):
+    """The direct conv splits its NHWC input tiles into TF32 hi/lo on chip; the result is
+    bit-identical to splitting the whole input first (LCU_NO_RAW_A=1)."""
+    import os
+    N, Ci, H, W, Co, Kh, Kw, s, p = shape
+    x, w = dev(data.normal(23, (N, Ci, H, W))), dev(data.normal(24, (Co, Ci, Kh, Kw)))
+    Ho, Wo = (H + 2 * p - Kh) // s + 1, (W + 2 * p - Kw) // s + 1
+    outs = []
+    for flag in ("0", "1"):
+        os.environ["LCU_NO_RAW_A"] = flag
+        try:
+            out = torch.empty((N, Co, Ho, Wo), device="cuda")
+            run(lib.lcu_conv2d(P(out), P(x), P(w), N, Ci, H, W, Co, Kh, Kw, s, p, 1, MODE_FP32_EXACT, None))
+            outs.append(out.cpu().numpy())
+        finally:
+            del os.environ["LCU_NO_RAW_A"]
+    assert np.array_equal(outs[0], outs[1])
+
+
 @pytest.mark.parametrize("rows,hidden", [(8192, 768), (3, 10), (17, 2048), (5, 3000)])
 def test_layernorm(lib, orc, rows, hidden):
     x = data.normal(31, (rows, hidden), 0.5, 2.0)
