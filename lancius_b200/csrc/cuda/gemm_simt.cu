@@ -1,6 +1,8 @@
 // CUDA-core FP32 GEMM and implicit-GEMM conv launchers (see gemm_simt.cuh).
 #include "gemm_simt.cuh"
 
+#include <algorithm>
+
 using namespace lcu_simt;
 
 __global__ void __launch_bounds__(THREADS) k_gemm_simt(const LcuGemmGroup* __restrict__ groups, size_t M, size_t N,
@@ -156,6 +158,79 @@ __global__ void __launch_bounds__(256) k_conv_smallk(float* __restrict__ out, co
     }
 }
 
+// Short-reduction conv with compile-time geometry: a thread computes 4 consecutive
+// output pixels of one row (Wo % 4 == 0) for 16 output channels. Its input patch
+// (CI x KH x (3*S + KW) values) sits in registers and serves all 16 channels; weights
+// are stored [K][Co] in shared memory, so one float4 broadcast load feeds 16 FMAs
+// (4 channels x 4 pixels). The warps of a block cover the same 32 pixel quads for
+// different 16-channel groups (the patch loads hit L1), and each channel row is stored
+// as float4 (a warp writes 512 contiguous bytes). Per output the reduction runs in k
+// order, as in k_conv_smallk: the same bits.
+template <int CI, int KH, int KW, int S>
+__global__ void __launch_bounds__(256) k_conv_smallk_q(float* __restrict__ out, const float* __restrict__ in,
+                                                       const float* __restrict__ w, int N, int H, int W, int Co,
+                                                       int pad, int Ho, int Wo, int relu) {
+    constexpr int K = CI * KH * KW, PW = 3 * S + KW;
+    extern __shared__ float4 wt4[];                      // [K][Co / 4]
+    float* wt = reinterpret_cast<float*>(wt4);
+    for (int i = threadIdx.x; i < K * Co; i += blockDim.x) {
+        const int k = i / Co, co = i - k * Co;
+        wt[i] = w[(size_t)co * K + k];
+    }
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int groups = Co / 16, quads_per_img = Ho * Wo / 4;
+    const long long Q = (long long)N * quads_per_img;
+    // warp job: (32 quads, one 16-channel group); blocks stride over the jobs
+    const long long jobs = ((Q + 31) / 32) * groups;
+    for (long long job = (long long)blockIdx.x * 8 + warp; job < jobs; job += (long long)gridDim.x * 8) {
+        const int g = (int)(job % groups);
+        const long long qi = (job / groups) * 32 + lane;
+        if (qi >= Q) continue;
+        const int n = (int)(qi / quads_per_img);
+        const int r = (int)(qi - (long long)n * quads_per_img) * 4;
+        const int ho = r / Wo, wo0 = r - ho * Wo;
+        const int y0 = ho * S - pad, x0 = wo0 * S - pad;
+        float x[CI][KH][PW];
+        const float* base = in + (size_t)n * CI * H * W;
+#pragma unroll
+        for (int ci = 0; ci < CI; ci++)
+#pragma unroll
+            for (int kh = 0; kh < KH; kh++)
+#pragma unroll
+                for (int c = 0; c < PW; c++) {
+                    const int iy = y0 + kh, ix = x0 + c;
+                    x[ci][kh][c] = (iy >= 0 && ix >= 0 && iy < H && ix < W) ? __ldg(base + ((size_t)ci * H + iy) * W + ix) : 0.f;
+                }
+        float* obase = out + ((size_t)n * Co + g * 16) * Ho * Wo + (size_t)ho * Wo + wo0;
+#pragma unroll 1
+        for (int cq = 0; cq < 4; cq++) {
+            float acc[4][4] = {};
+            const float4* wk = wt4 + (g * 16 + cq * 4) / 4;
+#pragma unroll
+            for (int ci = 0; ci < CI; ci++)
+#pragma unroll
+                for (int kh = 0; kh < KH; kh++)
+#pragma unroll
+                    for (int kw = 0; kw < KW; kw++) {
+                        const int k = (ci * KH + kh) * KW + kw;
+                        const float4 wv = wk[k * (Co / 4)];
+                        const float wc[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                        for (int c = 0; c < 4; c++)
+#pragma unroll
+                            for (int j = 0; j < 4; j++) acc[c][j] = fmaf(wc[c], x[ci][kh][j * S + kw], acc[c][j]);
+                    }
+#pragma unroll
+            for (int c = 0; c < 4; c++) {
+                float4 v = make_float4(acc[c][0], acc[c][1], acc[c][2], acc[c][3]);
+                if (relu) { v.x = fmaxf(v.x, 0.f); v.y = fmaxf(v.y, 0.f); v.z = fmaxf(v.z, 0.f); v.w = fmaxf(v.w, 0.f); }
+                *reinterpret_cast<float4*>(obase + (size_t)(cq * 4 + c) * Ho * Wo) = v;
+            }
+        }
+    }
+}
+
 extern "C" {
 
 int lcu_conv_smallk_supported(size_t Ci, size_t Kh, size_t Kw, size_t Co) {
@@ -172,10 +247,27 @@ lancius_error lcu_conv2d_smallk(float* out, const float* in, const float* w, siz
     if (P == 0 || Co == 0) return LANCIUS_ERROR_OK;
     if (!smallk_fits_int(N, Ci, H, W, Co, Ho, Wo))
         return lcu_conv2d_simt(out, in, w, N, Ci, H, W, Co, Kh, Kw, stride, pad, relu, stream);
+    cudaStream_t st = lcu_as_stream(stream);
+    // register-blocked variants for common stems (4 pixels x 16 channels per thread)
+    const bool qshape = Wo % 4 == 0 && Co % 16 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+                        (Ho * Wo) % 4 == 0 && Co * K * 4 <= 48 * 1024;
+    if (qshape) {
+        const size_t jobs = ((N * Ho * Wo / 4 + 31) / 32) * (Co / 16);
+        const unsigned qgrid = (unsigned)std::min<size_t>((jobs + 7) / 8, 148u * 16u);
+        const size_t qsmem = Co * K * 4;
+#define LCU_SMALLKQ(ci, kh, kw, s)                                                                                    \
+        if (Ci == ci && Kh == kh && Kw == kw && stride == s) {                                                        \
+            k_conv_smallk_q<ci, kh, kw, s><<<qgrid, 256, qsmem, st>>>(out, in, w, (int)N, (int)H, (int)W, (int)Co,   \
+                                                                       (int)pad, (int)Ho, (int)Wo, relu);             \
+            lcu_note_launch();                                                                                        \
+            return lcu_launch_status();                                                                               \
+        }
+        LCU_SMALLKQ(3, 3, 3, 1) LCU_SMALLKQ(3, 3, 3, 2) LCU_SMALLKQ(1, 3, 3, 1) LCU_SMALLKQ(3, 1, 1, 1)
+#undef LCU_SMALLKQ
+    }
     const int K4 = (int)((K + 3) / 4);
     const size_t smem = Co * K4 * sizeof(float4);
     const unsigned grid = lcu_blocks(P, 256, 148u * 8u);
-    cudaStream_t st = lcu_as_stream(stream);
 #define LCU_SMALLK(k4)                                                                                                \
     case k4:                                                                                                          \
         if (smem > 48 * 1024 && cudaFuncSetAttribute(k_conv_smallk<k4>, cudaFuncAttributeMaxDynamicSharedMemorySize,  \

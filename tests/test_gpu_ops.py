@@ -111,7 +111,9 @@ def test_attention(lib, orc, B, S, H, D, causal):
                                    # direct NHWC implicit-GEMM path (Ci % 16 == 0, Wo % 8 == 0)
                                    (2, 64, 32, 32, 128, 3, 3, 1, 1), (4, 32, 64, 64, 64, 3, 3, 2, 1),
                                    (3, 16, 24, 24, 200, 3, 3, 1, 1), (2, 64, 48, 48, 96, 1, 1, 1, 0),
-                                   (2, 16, 64, 64, 48, 5, 5, 2, 2)])
+                                   (2, 16, 64, 64, 48, 5, 5, 2, 2),
+                                   # register-blocked short-reduction stems (4 pixels x 16 channels a thread)
+                                   (2, 3, 30, 32, 32, 3, 3, 2, 1), (1, 1, 16, 16, 16, 3, 3, 1, 1), (2, 3, 20, 24, 48, 1, 1, 1, 0)])
 @pytest.mark.parametrize("relu", [0, 1])
 def test_conv2d(lib, orc, shape, relu):
     N, Ci, H, W, Co, Kh, Kw, s, p = shape
