@@ -49,6 +49,7 @@ struct ConvArgs {
     int halves;      // 1 when Co <= 128
     int passes, relu;
     int raw_b;       // 1: the input map covers plain FP32 NHWC; the epilogue warps split it on chip
+    int out_nhwc;    // 1 (persistent kernel only): store the output NHWC for a conv that reads it next
 };
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
@@ -239,19 +240,22 @@ k_conv_tc(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
 // TMEM columns, so two of them alternate and the epilogue of a tile (TMEM -> ReLU ->
 // NCHW) overlaps the MMAs of the next. Roles as in k_conv_tc; the epilogue stages its
 // blocks in a dedicated XOR-swizzled buffer because the ring already holds the next
-// tile's stages. The input comes as NHWC TF32 hi/lo (pre-split).
+// tile's stages. The input comes as NHWC TF32 hi/lo (pre-split) or, in raw-B mode, as
+// plain FP32 that warps 6-9 split on chip.
 constexpr int PT_BM = 128, PT_STAGES = 4;
 constexpr int PT_A_TILE = PT_BM * BK * 4;                       // 8 KB
 constexpr int PT_STAGE_BYTES = 2 * PT_A_TILE + 2 * B_TILE;      // 48 KB
 constexpr int PT_SMEM_BYTES = PT_STAGES * PT_STAGE_BYTES + 4 * 32 * 32 * 4 + 1024 + 256;
 
+constexpr int PT_THREADS = 320;
+
 struct SmemPT {
-    uint64_t full[PT_STAGES], empty[PT_STAGES], acc_full[2], acc_empty[2], drain;
+    uint64_t full[PT_STAGES], empty[PT_STAGES], conv[PT_STAGES], acc_full[2], acc_empty[2], drain;
     uint32_t tmem;
     int abort, consumed;
 };
 
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(PT_THREADS, 1)
 k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap tw_lo,
           const __grid_constant__ CUtensorMap tx_hi, const __grid_constant__ CUtensorMap tx_lo, float* __restrict__ out,
           ConvArgs a) {
@@ -275,14 +279,16 @@ k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
     };
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < PT_STAGES; s++) { tc::mbar_init(&sm->full[s], 1); tc::mbar_init(&sm->empty[s], 1); }
+        for (int s = 0; s < PT_STAGES; s++) {
+            tc::mbar_init(&sm->full[s], 1); tc::mbar_init(&sm->empty[s], 1); tc::mbar_init(&sm->conv[s], 4);
+        }
         for (int b = 0; b < 2; b++) { tc::mbar_init(&sm->acc_full[b], 1); tc::mbar_init(&sm->acc_empty[b], 4); }
         tc::mbar_init(&sm->drain, 1);
         sm->abort = 0;
         sm->consumed = 0;
         tc::fence_barrier_init();
         tc::prefetch_tmap(&tw_hi); tc::prefetch_tmap(&tx_hi);
-        if (a.passes > 1) { tc::prefetch_tmap(&tw_lo); tc::prefetch_tmap(&tx_lo); }
+        if (a.passes > 1) { tc::prefetch_tmap(&tw_lo); if (!a.raw_b) tc::prefetch_tmap(&tx_lo); }
     }
     if (warp == 1) tc::tmem_alloc(&sm->tmem, TMEM_COLS);
     tc::tc_fence_before();
@@ -293,7 +299,8 @@ k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
 
     if (warp == 0 && lane == 0) {
         // ---------------- TMA producer ----------------
-        const uint32_t tx = (a.passes > 1 ? 2u : 1u) * (uint32_t)(PT_A_TILE + bn * BK * 4);
+        const uint32_t tx = a.raw_b ? (a.passes > 1 ? 2u : 1u) * (uint32_t)PT_A_TILE + (uint32_t)(bn * BK * 4)
+                                    : (a.passes > 1 ? 2u : 1u) * (uint32_t)(PT_A_TILE + bn * BK * 4);
         int it = 0;
         bool ok = true;
         for (int t = blockIdx.x; t < T && ok; t += gridDim.x) {
@@ -312,7 +319,7 @@ k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
                 const int ix = -a.pad + kw, iy = ho0 * a.stride - a.pad + kh;
                 uint8_t* dst = st + 2 * PT_A_TILE;
                 tma_load_4d(dst, &tx_hi, &sm->full[s], cb * BK, ix, iy, img);
-                if (a.passes > 1) tma_load_4d(dst + B_TILE, &tx_lo, &sm->full[s], cb * BK, ix, iy, img);
+                if (a.passes > 1 && !a.raw_b) tma_load_4d(dst + B_TILE, &tx_lo, &sm->full[s], cb * BK, ix, iy, img);
                 issued = it + 1;
             }
         }
@@ -328,7 +335,9 @@ k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
             const uint32_t d = tmem + (uint32_t)b * 256;
             for (int kt = 0; kt < KT; kt++, it++) {
                 const int s = it % PT_STAGES;
-                if (!tc::mbar_wait(&sm->full[s], (it / PT_STAGES) & 1, abort, &g_conv_watchdog, 13)) { ok = false; break; }
+                if (!tc::mbar_wait(a.raw_b ? &sm->conv[s] : &sm->full[s], (it / PT_STAGES) & 1, abort, &g_conv_watchdog, 13)) {
+                    ok = false; break;
+                }
                 tc::tc_fence_after();
                 const uint32_t st = tc::smem_u32(tiles + s * PT_STAGE_BYTES);
                 const uint32_t a_hi = st, a_lo = st + PT_A_TILE, b_hi = st + 2 * PT_A_TILE, b_lo = b_hi + B_TILE;
@@ -352,6 +361,32 @@ k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
             }
             if (!ok) break;
             tc::mma_commit(&sm->acc_full[b]);
+        }
+    } else if (warp >= 6) {
+        // ---------------- input splitter (raw-B mode) ----------------
+        if (a.raw_b) {
+            const int n4 = bn * BK / 4;
+            int it = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < T && ok; t += gridDim.x) {
+                for (int kt = 0; kt < KT; kt++, it++) {
+                    const int s = it % PT_STAGES;
+                    if (!tc::mbar_wait(&sm->full[s], (it / PT_STAGES) & 1, abort, &g_conv_watchdog, 15)) { ok = false; break; }
+                    float4* b4 = reinterpret_cast<float4*>(tiles + s * PT_STAGE_BYTES + 2 * PT_A_TILE);
+#pragma unroll 4
+                    for (int i = threadIdx.x - 192; i < n4; i += 128) {
+                        const float4 x = b4[i];
+                        const float4 h = make_float4(tc::tf32_rna(x.x), tc::tf32_rna(x.y), tc::tf32_rna(x.z), tc::tf32_rna(x.w));
+                        b4[i] = h;
+                        if (a.passes > 1)
+                            b4[i + B_TILE / 16] = make_float4(tc::tf32_rna(x.x - h.x), tc::tf32_rna(x.y - h.y),
+                                                              tc::tf32_rna(x.z - h.z), tc::tf32_rna(x.w - h.w));
+                    }
+                    tc::fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&sm->conv[s]);
+                }
+            }
         }
     } else if (warp >= 2) {
         // ---------------- epilogue: rows = output channels, columns = pixels ----------------
@@ -380,6 +415,18 @@ k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
                                     __uint_as_float(va[4 * jj + 2]), __uint_as_float(va[4 * jj + 3]));
                 __syncwarp();
                 if (c + 32 < bn) tc::tmem_ld32_issue(tbase + (uint32_t)(c + 32), va);
+                if (a.out_nhwc) {
+                    // NHWC: lane = channel, one 128-byte channel run per pixel and store
+                    const int co = co0 + lane;
+                    float* o = out + ((size_t)img * hw + (size_t)ho0 * a.wo + c) * a.co + co;
+                    for (int pxi = 0; pxi < 32 && c + pxi < valid; pxi++) {
+                        float x = sb[lane * 32 + ((((pxi >> 2) ^ (lane & 7))) << 2) + (pxi & 3)];
+                        if (a.relu) x = fmaxf(x, 0.f);
+                        if (co < a.co) o[(size_t)pxi * a.co] = x;
+                    }
+                    __syncwarp();
+                    continue;
+                }
                 const int cl4 = lane & 7, px = c + 4 * cl4;
 #pragma unroll 2
                 for (int it = 0; it < 8; it++) {
@@ -462,6 +509,25 @@ __global__ void __launch_bounds__(256) k_nhwc_split(const float* __restrict__ in
     }
 }
 
+// NHWC -> NCHW (the layout a download hands back for a conv output kept NHWC between
+// two convs), FP32 or FP64 out: per (n, h) tiles of 64 columns x 32 channels.
+template <typename T>
+__global__ void __launch_bounds__(256) k_nhwc_to_nchw(T* __restrict__ out, const float* __restrict__ in, int C, int H,
+                                                      int W) {
+    __shared__ float t[64][33];
+    const int nh = blockIdx.z, n = nh / H, h = nh % H;
+    const int c0 = blockIdx.y * 32, w0 = blockIdx.x * 64;
+    for (int idx = threadIdx.x; idx < 64 * 32; idx += 256) {
+        const int w = idx >> 5, c = idx & 31;
+        t[w][c] = (w0 + w < W && c0 + c < C) ? in[(((size_t)n * H + h) * W + w0 + w) * C + c0 + c] : 0.f;
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < 32 * 64; idx += 256) {
+        const int c = idx >> 6, w = idx & 63;
+        if (w0 + w < W && c0 + c < C) out[(((size_t)n * C + c0 + c) * H + h) * W + w0 + w] = (T)t[w][c];
+    }
+}
+
 // OIHW -> [Co][Kh][Kw][Ci] TF32 hi / lo
 __global__ void k_weight_khwc_split(const float* __restrict__ w, float* __restrict__ hi, float* __restrict__ lo, int Co,
                                     int Ci, int Kh, int Kw) {
@@ -531,6 +597,27 @@ extern "C" size_t lcu_conv_nhwc_scratch_bytes(LcuConvShape cs, int passes) {
 
 extern "C" lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const float* w, LcuConvShape cs, int relu,
                                             int mode, void* scratch, void* stream) {
+    return lcu_conv2d_tc_nhwc_ex(out, in, w, cs, relu, mode, scratch, stream, 0, 0);
+}
+
+static bool conv_pt_enabled() {
+    const char* e = getenv("LCU_CONV_NO_PT");
+    return !(e && e[0] == '1');
+}
+
+extern "C" int lcu_conv_nhwc_out_ok(LcuConvShape cs) { return lcu_conv_nhwc_supported(cs) && conv_pt_enabled(); }
+
+extern "C" lancius_error lcu_nhwc_to_nchw(void* out, const float* in, int n, int c, int h, int w, int f64, void* stream) {
+    const dim3 grid((unsigned)((w + 63) / 64), (unsigned)((c + 31) / 32), (unsigned)(n * h));
+    if (f64) k_nhwc_to_nchw<double><<<grid, 256, 0, lcu_as_stream(stream)>>>(static_cast<double*>(out), in, c, h, w);
+    else k_nhwc_to_nchw<float><<<grid, 256, 0, lcu_as_stream(stream)>>>(static_cast<float*>(out), in, c, h, w);
+    return lcu_launch_status();
+}
+
+// in_nhwc: `in` already holds the input as NHWC FP32 (written by the previous conv);
+// out_nhwc: store the output NHWC (persistent kernel only).
+extern "C" lancius_error lcu_conv2d_tc_nhwc_ex(float* out, const float* in, const float* w, LcuConvShape cs, int relu,
+                                               int mode, void* scratch, void* stream, int in_nhwc, int out_nhwc) {
     const int passes = mode == LCU_MODE_TF32 ? 1 : 3;
     if (!lcu_conv_nhwc_supported(cs) || !scratch) { lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP; }
     cudaStream_t st = lcu_as_stream(stream);
@@ -540,17 +627,24 @@ extern "C" lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const f
     // one-launch-per-tile kernel takes the input NHWC as plain FP32 and splits it on chip
     static int n_sm = 0;
     if (!n_sm) { int dev = 0; cudaGetDevice(&dev); cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev); }
-    const char* nopt = getenv("LCU_CONV_NO_PT");
-    const bool pt = !(nopt && nopt[0] == '1') && n_sm > 0;
-    const int raw = (pt || lcu_no_raw_a()) ? 0 : 1;
+    const bool pt = conv_pt_enabled() && n_sm > 0;
+    if (out_nhwc && !pt) {
+        lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP;
+    }
+    const char* ptraw = getenv("LCU_CONV_PT_RAW");
+    const int raw = in_nhwc ? 1 : lcu_no_raw_a() ? 0 : pt ? (ptraw && ptraw[0] == '1') : 1;
     float* xh = reinterpret_cast<float*>(s); s += al256(xe * 4);
     float* xl = passes > 1 && !raw ? reinterpret_cast<float*>(s) : nullptr; if (passes > 1) s += al256(xe * 4);
     float* wh = reinterpret_cast<float*>(s); s += al256(we * 4);
     float* wl = passes > 1 ? reinterpret_cast<float*>(s) : nullptr;
 
-    k_nhwc_split<<<dim3((unsigned)((cs.w + 63) / 64), (unsigned)((cs.ci + 31) / 32), (unsigned)(cs.n * cs.h)), 256, 0, st>>>(
-        in, xh, xl, cs.ci, cs.h, cs.w, raw ? 0 : 1);
-    lcu_note_launch();
+    if (in_nhwc) {
+        xh = const_cast<float*>(in);                  // read in place, split on chip
+    } else {
+        k_nhwc_split<<<dim3((unsigned)((cs.w + 63) / 64), (unsigned)((cs.ci + 31) / 32), (unsigned)(cs.n * cs.h)), 256, 0, st>>>(
+            in, xh, xl, cs.ci, cs.h, cs.w, raw ? 0 : 1);
+        lcu_note_launch();
+    }
     k_weight_khwc_split<<<lcu_blocks(we, 256), 256, 0, st>>>(w, wh, wl, cs.co, cs.ci, cs.kh, cs.kw);
     lcu_note_launch();
     lancius_error e = lcu_launch_status();
@@ -585,10 +679,11 @@ extern "C" lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const f
         else mx_lo = mx_hi;
     }
     if (!ok) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
-    ConvArgs a{cs.n, cs.ci, cs.co, cs.kh, cs.kw, cs.stride, cs.pad, cs.ho, cs.wo, rows, cs.co > 128 ? 2 : 1, passes, relu, raw};
+    ConvArgs a{cs.n, cs.ci, cs.co, cs.kh, cs.kw, cs.stride, cs.pad, cs.ho, cs.wo, rows, cs.co > 128 ? 2 : 1, passes, relu, raw,
+               out_nhwc};
     if (pt) {
         const long long T = (long long)cs.n * ((cs.ho + rows - 1) / rows) * ((cs.co + PT_BM - 1) / PT_BM);
-        k_conv_pt<<<(unsigned)std::min<long long>(T, n_sm), THREADS, PT_SMEM_BYTES, st>>>(mw_hi, mw_lo, mx_hi, mx_lo, out, a);
+        k_conv_pt<<<(unsigned)std::min<long long>(T, n_sm), PT_THREADS, PT_SMEM_BYTES, st>>>(mw_hi, mw_lo, mx_hi, mx_lo, out, a);
         lcu_note_launch();
         return lcu_launch_status();
     }

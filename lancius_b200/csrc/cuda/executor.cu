@@ -47,6 +47,10 @@ struct Step {
     size_t wsplit_off = (size_t)-1;   // tensor-core MATMUL on INPUT weights: hi/lo copies in ctx->wsplit
     int amap_idx = -1;                // tensor-core MATMUL in raw-A mode: first of its maps in ctx->amaps
     float eps = 1e-5f;
+    uint32_t node_id = 0;      // S_CONV: the conv node (its output)
+    uint32_t in_id = 0;        // S_CONV: the input node
+    int in_nhwc = 0;           // S_CONV: the input slot holds NHWC (written by the previous conv)
+    int out_nhwc = 0;          // S_CONV: store the output NHWC for the convs that read it
 };
 
 struct Chain {          // a MATMUL and the epilogue nodes folded into it
@@ -87,6 +91,7 @@ struct lcu_ctx {
     size_t wsplit_floats = 0;
     std::vector<CUtensorMap> amaps_host;  // raw-A tensor maps of every step, uploaded to amaps at bind
     CUtensorMap* amaps = nullptr;
+    std::vector<uint8_t> nhwc;          // node id -> 1: a conv output stored NHWC (only convs read it)
     std::vector<LcuTcGemmPlan> tc_plans;
     std::vector<size_t> off;            // node id -> byte offset in dmem (NPOS: no storage)
     std::vector<Step> steps;
@@ -112,6 +117,7 @@ static void release_binding(lcu_ctx* c) {
     c->amaps_host.clear();
     c->dmem_bytes = 0; c->staging_elems = 0; c->scratch_bytes = 0;
     c->tc_plans.clear();
+    c->nhwc.clear();
     c->off.clear(); c->steps.clear();
     c->g = nullptr; c->s = nullptr;
 }
@@ -502,6 +508,7 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                 case LANCIUS_OP_CONV2D: case LANCIUS_OP_CONV2D_RELU_FUSED: {
                     const lancius_node *in = n->inputs[0], *wt = n->inputs[1];
                     st.kind = S_CONV; st.relu = n->op == LANCIUS_OP_CONV2D_RELU_FUSED;
+                    st.node_id = n->id; st.in_id = n->inputs[0]->id;
                     st.cn = in->shape[0]; st.ci = in->shape[1]; st.h = in->shape[2]; st.w = in->shape[3];
                     st.co = wt->shape[0]; st.kh = wt->shape[2]; st.kw = wt->shape[3]; st.stride = n->stride; st.pad = n->pad;
                     if (in->ndim != 4 || wt->ndim != 4 || wt->shape[1] != st.ci || st.stride == 0) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
@@ -591,6 +598,46 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
     return LANCIUS_ERROR_OK;
 }
 
+static LcuConvShape conv_shape(const Step& s) {
+    const size_t ho = (s.h + 2 * s.pad - s.kh) / s.stride + 1, wo = (s.w + 2 * s.pad - s.kw) / s.stride + 1;
+    return LcuConvShape{(int)s.cn, (int)s.ci, (int)s.h, (int)s.w, (int)s.co, (int)s.kh, (int)s.kw, (int)s.stride,
+                        (int)s.pad, (int)ho, (int)wo};
+}
+
+// A conv step that reads its input through the NHWC tensor-core path
+static bool reads_nhwc_path(const Step& s) {
+    return s.kind == S_CONV && s.tc && lcu_conv_nhwc_supported(conv_shape(s)) && !lcu_conv_force_im2col();
+}
+
+// A conv output read only by convs on the NHWC path is stored NHWC by its producer and read
+// in place by them: no NCHW store and no NCHW -> NHWC pass in between. Downloads of such a
+// node transpose back to NCHW. LCU_NO_NHWC_HANDOFF=1 turns this off.
+static void plan_nhwc_handoff(lcu_ctx* c, const Builder& b) {
+    const char* env = getenv("LCU_NO_NHWC_HANDOFF");
+    if (env && env[0] == '1') return;
+    c->nhwc.assign(b.g->next_id, 0);
+    for (Step& p : c->steps) {
+        if (p.kind != S_CONV) continue;
+        const bool can_write = p.tc ? (reads_nhwc_path(p) && lcu_conv_nhwc_out_ok(conv_shape(p)))
+                                    : lcu_conv_smallk_nhwc_ok(p.cn, p.ci, p.h, p.w, p.co, p.kh, p.kw, p.stride, p.pad) != 0;
+        if (!can_write) continue;
+        const std::vector<const lancius_node*>& users = b.users[p.node_id];
+        if (users.empty()) continue;
+        bool ok = true;
+        for (const lancius_node* u : users) {
+            bool found = false;
+            for (const Step& q : c->steps)
+                if (q.kind == S_CONV && q.node_id == u->id && q.in_id == p.node_id && reads_nhwc_path(q)) found = true;
+            ok = ok && found && u->inputs[1] && u->inputs[1]->id != p.node_id;
+        }
+        if (!ok) continue;
+        p.out_nhwc = 1;
+        c->nhwc[p.node_id] = 1;
+        for (Step& q : c->steps)
+            if (q.kind == S_CONV && q.in_id == p.node_id) q.in_nhwc = 1;
+    }
+}
+
 extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_graph* g, const lancius_memory_plan* plan) {
     if (!c || !s || !g) return fail(LANCIUS_ERROR_NULL_PTR);
     cudaSetDevice(c->device);
@@ -653,6 +700,7 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
     lancius_error e = build_steps(b, off, fused);
     if (own) lancius_memory_plan_destroy(own);
     if (e != LANCIUS_ERROR_OK) { c->steps.clear(); return e; }
+    if (fused) plan_nhwc_handoff(c, b);
 
     size_t table_base = align_up(cursor, SLOT_ALIGN);
     size_t total = table_base + align_up(b.tables.size(), SLOT_ALIGN);
@@ -807,11 +855,23 @@ extern "C" lancius_error lcu_refresh_weights(lcu_ctx* c) {
 // FP32 device -> host copy queued on the context's stream; returns at once (the data is
 // there after lcu_synchronize). With page-locked `host` the copy overlaps other streams'
 // work, e.g. the next request's uploads on a second context.
+// A node kept NHWC between two convs: transpose it to NCHW (FP32 or FP64) in the staging
+// buffer, in stream order; returns the buffer to copy from, or null.
+static const void* nchw_view(lcu_ctx* c, const lancius_node* n, const float* d, int f64) {
+    if (n->id >= c->nhwc.size() || !c->nhwc[n->id]) return nullptr;
+    if (lcu_nhwc_to_nchw(c->staging, d, (int)n->shape[0], (int)n->shape[1], (int)n->shape[2], (int)n->shape[3], f64,
+                         c->stream) != LANCIUS_ERROR_OK)
+        return nullptr;
+    return c->staging;
+}
+
 extern "C" lancius_error lcu_download_async(lcu_ctx* c, const lancius_node* n, void* host) {
     float* d; size_t E;
     if (!host) return fail(LANCIUS_ERROR_NULL_PTR);
     if (!node_slot(c, n, &d, &E)) return fail(LANCIUS_ERROR_NULL_PTR);
     cudaSetDevice(c->device);
+    if (const void* v = nchw_view(c, n, d, 0))
+        return cuda_fail(cudaMemcpyAsync(host, v, E * 4, cudaMemcpyDeviceToHost, c->stream));
     return cuda_fail(cudaMemcpyAsync(host, d, E * 4, cudaMemcpyDeviceToHost, c->stream));
 }
 
@@ -821,12 +881,20 @@ extern "C" lancius_error lcu_download(lcu_ctx* c, const lancius_node* n, void* h
     if (!node_slot(c, n, &d, &E)) return fail(LANCIUS_ERROR_NULL_PTR);
     cudaSetDevice(c->device);
     cudaError_t ce;
+    const bool nhwc = n->id < c->nhwc.size() && c->nhwc[n->id];
+    if (nhwc && E > c->staging_elems) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
     if (dt == LANCIUS_DTYPE_FP32) {
-        ce = cudaMemcpyAsync(host, d, E * 4, cudaMemcpyDeviceToHost, c->stream);
+        const void* v = nhwc ? nchw_view(c, n, d, 0) : d;
+        if (!v) return fail(LANCIUS_ERROR_INTERNAL);
+        ce = cudaMemcpyAsync(host, v, E * 4, cudaMemcpyDeviceToHost, c->stream);
     } else if (dt == LANCIUS_DTYPE_FP64) {
         if (E > c->staging_elems) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
-        lancius_error e = lcu_convert_f32_to_f64(c->staging, d, E, c->stream);
-        if (e != LANCIUS_ERROR_OK) return e;
+        if (nhwc) {
+            if (!nchw_view(c, n, d, 1)) return fail(LANCIUS_ERROR_INTERNAL);
+        } else {
+            lancius_error e = lcu_convert_f32_to_f64(c->staging, d, E, c->stream);
+            if (e != LANCIUS_ERROR_OK) return e;
+        }
         ce = cudaMemcpyAsync(host, c->staging, E * 8, cudaMemcpyDeviceToHost, c->stream);
     } else {
         return fail(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
@@ -944,7 +1012,8 @@ static lancius_error run_steps(lcu_ctx* c) {
                     const LcuConvShape cs{(int)s.cn, (int)s.ci, (int)s.h, (int)s.w, (int)s.co, (int)s.kh, (int)s.kw,
                                           (int)s.stride, (int)s.pad, (int)ho, (int)wo};
                     if (lcu_conv_nhwc_supported(cs) && !lcu_conv_force_im2col()) {
-                        e = lcu_conv2d_tc_nhwc(F(s.out), F(s.in0), F(s.in1), cs, s.relu, c->mode, c->scratch, st);
+                        e = lcu_conv2d_tc_nhwc_ex(F(s.out), F(s.in0), F(s.in1), cs, s.relu, c->mode, c->scratch, st,
+                                                  s.in_nhwc, s.out_nhwc);
                         break;
                     }
                     LcuTcGemmPlan& p = c->tc_plans[s.plan_idx];
@@ -959,8 +1028,12 @@ static lancius_error run_steps(lcu_ctx* c) {
                     e = lcu_gemm_tc_run(&p, (const LcuGemmGroup*)(base + s.table_off), s.relu ? LCU_EPI_RELU : LCU_EPI_NONE, st);
                     break;
                 }
-                e = lcu_conv2d(F(s.out), F(s.in0), F(s.in1), s.cn, s.ci, s.h, s.w, s.co, s.kh, s.kw, s.stride, s.pad,
-                               s.relu, c->mode, st);
+                if (s.out_nhwc)
+                    e = lcu_conv2d_smallk_ex(F(s.out), F(s.in0), F(s.in1), s.cn, s.ci, s.h, s.w, s.co, s.kh, s.kw, s.stride,
+                                             s.pad, s.relu, 1, st);
+                else
+                    e = lcu_conv2d(F(s.out), F(s.in0), F(s.in1), s.cn, s.ci, s.h, s.w, s.co, s.kh, s.kw, s.stride, s.pad,
+                                   s.relu, c->mode, st);
                 break;
             case S_MAXPOOL: e = lcu_maxpool2d(F(s.out), F(s.in0), s.cn, s.ci, s.h, s.w, s.kh, s.stride, st); break;
             case S_MISC: e = run_misc(s, base, c->scratch, c->packed, st); break;

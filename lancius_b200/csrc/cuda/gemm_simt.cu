@@ -165,8 +165,9 @@ __global__ void __launch_bounds__(256) k_conv_smallk(float* __restrict__ out, co
 // (4 channels x 4 pixels). The warps of a block cover the same 32 pixel quads for
 // different 16-channel groups (the patch loads hit L1), and each channel row is stored
 // as float4 (a warp writes 512 contiguous bytes). Per output the reduction runs in k
-// order, as in k_conv_smallk: the same bits.
-template <int CI, int KH, int KW, int S>
+// order, as in k_conv_smallk: the same bits. NHWC = true stores the output NHWC (4
+// channels of one pixel per float4) for a conv that reads it next.
+template <int CI, int KH, int KW, int S, bool NHWC>
 __global__ void __launch_bounds__(256) k_conv_smallk_q(float* __restrict__ out, const float* __restrict__ in,
                                                        const float* __restrict__ w, int N, int H, int W, int Co,
                                                        int pad, int Ho, int Wo, int relu) {
@@ -221,11 +222,21 @@ __global__ void __launch_bounds__(256) k_conv_smallk_q(float* __restrict__ out, 
 #pragma unroll
                             for (int j = 0; j < 4; j++) acc[c][j] = fmaf(wc[c], x[ci][kh][j * S + kw], acc[c][j]);
                     }
+            if (NHWC) {
+                float* o = out + ((size_t)n * Ho * Wo + r) * Co + g * 16 + cq * 4;
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                float4 v = make_float4(acc[c][0], acc[c][1], acc[c][2], acc[c][3]);
-                if (relu) { v.x = fmaxf(v.x, 0.f); v.y = fmaxf(v.y, 0.f); v.z = fmaxf(v.z, 0.f); v.w = fmaxf(v.w, 0.f); }
-                *reinterpret_cast<float4*>(obase + (size_t)(cq * 4 + c) * Ho * Wo) = v;
+                for (int j = 0; j < 4; j++) {
+                    float4 v = make_float4(acc[0][j], acc[1][j], acc[2][j], acc[3][j]);
+                    if (relu) { v.x = fmaxf(v.x, 0.f); v.y = fmaxf(v.y, 0.f); v.z = fmaxf(v.z, 0.f); v.w = fmaxf(v.w, 0.f); }
+                    *reinterpret_cast<float4*>(o + (size_t)j * Co) = v;
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    float4 v = make_float4(acc[c][0], acc[c][1], acc[c][2], acc[c][3]);
+                    if (relu) { v.x = fmaxf(v.x, 0.f); v.y = fmaxf(v.y, 0.f); v.z = fmaxf(v.z, 0.f); v.w = fmaxf(v.w, 0.f); }
+                    *reinterpret_cast<float4*>(obase + (size_t)(cq * 4 + c) * Ho * Wo) = v;
+                }
             }
         }
     }
@@ -240,8 +251,31 @@ static bool smallk_fits_int(size_t N, size_t Ci, size_t H, size_t W, size_t Co, 
     return N * Co * Ho * Wo < (1u << 31) && Ci * H * W < (1u << 31);
 }
 
+// the register-blocked geometries (Ci, Kh, Kw, stride) instantiated below
+static bool smallk_q_geometry(size_t Ci, size_t Kh, size_t Kw, size_t stride) {
+    return (Ci == 3 && Kh == 3 && Kw == 3 && (stride == 1 || stride == 2)) || (Ci == 1 && Kh == 3 && Kw == 3 && stride == 1) ||
+           (Ci == 3 && Kh == 1 && Kw == 1 && stride == 1);
+}
+static bool smallk_q_shape(size_t N, size_t Ci, size_t H, size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride,
+                           size_t pad) {
+    const size_t Ho = (H + 2 * pad - Kh) / stride + 1, Wo = (W + 2 * pad - Kw) / stride + 1;
+    return smallk_q_geometry(Ci, Kh, Kw, stride) && Wo % 4 == 0 && Co % 16 == 0 && Co * Ci * Kh * Kw * 4 <= 48 * 1024 &&
+           smallk_fits_int(N, Ci, H, W, Co, Ho, Wo);
+}
+
+int lcu_conv_smallk_nhwc_ok(size_t N, size_t Ci, size_t H, size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride,
+                            size_t pad) {
+    return smallk_q_shape(N, Ci, H, W, Co, Kh, Kw, stride, pad);
+}
+
 lancius_error lcu_conv2d_smallk(float* out, const float* in, const float* w, size_t N, size_t Ci, size_t H, size_t W,
                                 size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu, void* stream) {
+    return lcu_conv2d_smallk_ex(out, in, w, N, Ci, H, W, Co, Kh, Kw, stride, pad, relu, 0, stream);
+}
+
+lancius_error lcu_conv2d_smallk_ex(float* out, const float* in, const float* w, size_t N, size_t Ci, size_t H, size_t W,
+                                   size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu, int out_nhwc,
+                                   void* stream) {
     const size_t Ho = (H + 2 * pad - Kh) / stride + 1, Wo = (W + 2 * pad - Kw) / stride + 1;
     const size_t P = N * Ho * Wo, K = Ci * Kh * Kw;
     if (P == 0 || Co == 0) return LANCIUS_ERROR_OK;
@@ -249,16 +283,22 @@ lancius_error lcu_conv2d_smallk(float* out, const float* in, const float* w, siz
         return lcu_conv2d_simt(out, in, w, N, Ci, H, W, Co, Kh, Kw, stride, pad, relu, stream);
     cudaStream_t st = lcu_as_stream(stream);
     // register-blocked variants for common stems (4 pixels x 16 channels per thread)
-    const bool qshape = Wo % 4 == 0 && Co % 16 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
-                        (Ho * Wo) % 4 == 0 && Co * K * 4 <= 48 * 1024;
+    const bool qshape = smallk_q_shape(N, Ci, H, W, Co, Kh, Kw, stride, pad) && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+    if (out_nhwc && !qshape) { lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP; }
     if (qshape) {
         const size_t jobs = ((N * Ho * Wo / 4 + 31) / 32) * (Co / 16);
         const unsigned qgrid = (unsigned)std::min<size_t>((jobs + 7) / 8, 148u * 16u);
         const size_t qsmem = Co * K * 4;
 #define LCU_SMALLKQ(ci, kh, kw, s)                                                                                    \
         if (Ci == ci && Kh == kh && Kw == kw && stride == s) {                                                        \
-            k_conv_smallk_q<ci, kh, kw, s><<<qgrid, 256, qsmem, st>>>(out, in, w, (int)N, (int)H, (int)W, (int)Co,   \
-                                                                       (int)pad, (int)Ho, (int)Wo, relu);             \
+            if (out_nhwc)                                                                                             \
+                k_conv_smallk_q<ci, kh, kw, s, true><<<qgrid, 256, qsmem, st>>>(out, in, w, (int)N, (int)H, (int)W,  \
+                                                                               (int)Co, (int)pad, (int)Ho, (int)Wo,  \
+                                                                               relu);                                \
+            else                                                                                                      \
+                k_conv_smallk_q<ci, kh, kw, s, false><<<qgrid, 256, qsmem, st>>>(out, in, w, (int)N, (int)H, (int)W, \
+                                                                                (int)Co, (int)pad, (int)Ho, (int)Wo, \
+                                                                                relu);                               \
             lcu_note_launch();                                                                                        \
             return lcu_launch_status();                                                                               \
         }

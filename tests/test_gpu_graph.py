@@ -173,3 +173,53 @@ def test_watchdog_reported_by_synchronize(device):
     assert lib.lcu_synchronize(device.ptr) == 0
     b = configs.mlp(L.Graph(), batch=8, seed=5)
     run_gpu(device, b)
+
+
+def test_conv_chain_nhwc_handoff(device, orc):
+    """A conv output read only by the next conv stays NHWC between them (producer stores
+    NHWC, consumer reads it in place). Same bytes as with the handoff off, and downloads of
+    an NHWC-kept output (FP64 and FP32) come back NCHW. The first conv's output is dead
+    after the second conv and its slot is reused by the third, so only the last two conv
+    outputs are compared (the second is kept NHWC and read in the last wave)."""
+    import os
+    from lancius_b200 import data
+
+    def build():
+        g = L.Graph()
+        x = g.input_4d(2, 3, 64, 64)
+        w1, w2, w3 = g.input_4d(32, 3, 3, 3), g.input_4d(64, 32, 3, 3), g.input_4d(64, 64, 3, 3)
+        h1 = g.relu(g.conv2d(x, w1, 1, 1))
+        h2 = g.relu(g.conv2d(h1, w2, 2, 1))
+        y = g.conv2d(h2, w3, 1, 1)
+        g.optimize_fusion()
+        arrs = [(x, data.normal(61, (2, 3, 64, 64))), (w1, data.normal(62, (32, 3, 3, 3), 0, 0.3)),
+                (w2, data.normal(63, (64, 32, 3, 3), 0, 0.06)), (w3, data.normal(64, (64, 64, 3, 3), 0, 0.04))]
+        return g, arrs, [y]
+
+    def run():
+        g, arrs, outs = build()
+        s = g.schedule()
+        device.bind(s)
+        for n, a in arrs:
+            device.upload(n, a)
+        device.execute(s)
+        # every conv node's output, intermediate ones included, through both download paths
+        convs = [n for n in g.nodes() if n.op in ("CONV2D", "CONV2D_RELU_FUSED")][1:]
+        return [device.download(n) for n in convs], [device.download(n, np.float32) for n in convs], (g, arrs, convs)
+
+    y64, y32, (g, arrs, convs) = run()
+    os.environ["LCU_NO_NHWC_HANDOFF"] = "1"
+    try:
+        r64, r32, _ = run()
+    finally:
+        del os.environ["LCU_NO_NHWC_HANDOFF"]
+    assert len(convs) == 2
+    for a, b in zip(y64, r64):
+        assert np.array_equal(a, b)
+    for a, b in zip(y32, r32):
+        assert np.array_equal(a, b)
+    for n, a in arrs:
+        g.bind(n, a)
+    ref = orc.run_graph(g, convs)
+    for n, y in zip(convs, y64):
+        assert_close(y, ref[n.id], 1e-4)
