@@ -153,22 +153,17 @@ k_conv_tc(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
     } else if (warp >= 2) {
         if (a.raw_b) {
             // ---------------- input splitter (raw-B mode) ----------------
-            // hi = rna_tf32(x) in place, lo = rna_tf32(x - hi) into the stage's lo slot; the
-            // swizzle permutes 16-byte chunks identically in both, so a flat pass suffices
+            // the FP32 tile serves as hi as it is (the MMA reads it truncated to TF32);
+            // lo = rna_tf32(x - tf32_hi(x)) goes to the stage's lo slot; the swizzle permutes
+            // 16-byte chunks identically in both, so a flat pass suffices
             const int n4 = bn * BK / 4;
             for (int kt = 0; kt < KT; kt++) {
                 const int s = kt % STAGES;
                 if (!tc::mbar_wait(&sm->full[s], (kt / STAGES) & 1, abort, &g_conv_watchdog, 4)) break;
                 float4* b4 = reinterpret_cast<float4*>(tiles + s * STAGE_BYTES + 2 * A_TILE);
 #pragma unroll 4
-                for (int i = threadIdx.x - 64; i < n4; i += 128) {
-                    const float4 x = b4[i];
-                    const float4 h = make_float4(tc::tf32_rna(x.x), tc::tf32_rna(x.y), tc::tf32_rna(x.z), tc::tf32_rna(x.w));
-                    b4[i] = h;
-                    if (a.passes > 1)
-                        b4[i + B_TILE / 16] = make_float4(tc::tf32_rna(x.x - h.x), tc::tf32_rna(x.y - h.y),
-                                                          tc::tf32_rna(x.z - h.z), tc::tf32_rna(x.w - h.w));
-                }
+                for (int i = threadIdx.x - 64; i < n4 && a.passes > 1; i += 128)
+                    b4[i + B_TILE / 16] = tc::tf32_lo4(b4[i]);
                 tc::fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&sm->conv[s]);
@@ -374,14 +369,8 @@ k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
                     if (!tc::mbar_wait(&sm->full[s], (it / PT_STAGES) & 1, abort, &g_conv_watchdog, 15)) { ok = false; break; }
                     float4* b4 = reinterpret_cast<float4*>(tiles + s * PT_STAGE_BYTES + 2 * PT_A_TILE);
 #pragma unroll 4
-                    for (int i = threadIdx.x - 192; i < n4; i += 128) {
-                        const float4 x = b4[i];
-                        const float4 h = make_float4(tc::tf32_rna(x.x), tc::tf32_rna(x.y), tc::tf32_rna(x.z), tc::tf32_rna(x.w));
-                        b4[i] = h;
-                        if (a.passes > 1)
-                            b4[i + B_TILE / 16] = make_float4(tc::tf32_rna(x.x - h.x), tc::tf32_rna(x.y - h.y),
-                                                              tc::tf32_rna(x.z - h.z), tc::tf32_rna(x.w - h.w));
-                    }
+                    for (int i = threadIdx.x - 192; i < n4 && a.passes > 1; i += 128)
+                        b4[i + B_TILE / 16] = tc::tf32_lo4(b4[i]);
                     tc::fence_proxy_async();
                     __syncwarp();
                     if (lane == 0) tc::mbar_arrive(&sm->conv[s]);
@@ -500,8 +489,8 @@ __global__ void __launch_bounds__(256) k_nhwc_split(const float* __restrict__ in
         float x[4] = {t[c][w], t[c + 1][w], t[c + 2][w], t[c + 3][w]}, xh[4], xl[4];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
-            xh[j] = round ? tc::tf32_rna(x[j]) : x[j];
-            xl[j] = tc::tf32_rna(x[j] - xh[j]);
+            xh[j] = round ? tc::tf32_hi(x[j]) : x[j];
+            xl[j] = tc::tf32_lo(x[j]);
         }
         const size_t o = (((size_t)n * H + h) * W + w0 + w) * C + c0 + c;
         *reinterpret_cast<float4*>(hi + o) = make_float4(xh[0], xh[1], xh[2], xh[3]);
@@ -538,9 +527,9 @@ __global__ void k_weight_khwc_split(const float* __restrict__ w, float* __restri
         const int kw = (int)(r % Kw); r /= Kw;
         const int kh = (int)(r % Kh);
         const int co = (int)(r / Kh);
-        const float x = w[(((size_t)co * Ci + ci) * Kh + kh) * Kw + kw], xh = tc::tf32_rna(x);
-        hi[i] = xh;
-        if (lo) lo[i] = tc::tf32_rna(x - xh);
+        const float x = w[(((size_t)co * Ci + ci) * Kh + kh) * Kw + kw];
+        hi[i] = tc::tf32_hi(x);
+        if (lo) lo[i] = tc::tf32_lo(x);
     }
 }
 

@@ -1,6 +1,6 @@
 // FP32 GEMM on the 5th-generation tensor cores (tcgen05, kind::tf32) with the
 // 3xTF32 split for FP32-exact results:
-//     A*B ~= Ahi*Bhi + Ahi*Blo + Alo*Bhi,   hi = rna_tf32(x), lo = x - hi,
+//     A*B ~= Ahi*Bhi + Ahi*Blo + Alo*Bhi,   hi = x truncated to TF32, lo = rna_tf32(x - hi),
 // accumulated in FP32 in TMEM. A split pass writes hi/lo copies of both operands
 // into scratch with 16-byte-aligned row pitches (any M, N, K is then TMA-legal);
 // the GEMM kernel streams them with TMA through a 4-stage mbarrier ring:
@@ -181,21 +181,17 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
     } else if (warp >= 2) {
         if (a_maps) {
             // ---------------- A splitter (raw-A mode) ----------------
-            // hi = rna_tf32(x) in place, lo = rna_tf32(x - hi) into the stage's lo slot. The
-            // swizzle permutes 16-byte chunks identically in both slots, so the split is a
-            // flat elementwise pass over the tile's bytes.
+            // The FP32 tile serves as hi as it is (the MMA reads it truncated to TF32);
+            // lo = rna_tf32(x - tf32_hi(x)) goes to the stage's lo slot. The swizzle permutes
+            // 16-byte chunks identically in both slots, so this is a flat elementwise pass.
             for (int kt = 0; kt < KT; kt++) {
                 const int s = kt % STAGES;
                 if (!tc::mbar_wait(&sm->full[s], (kt / STAGES) & 1, abort, &g_gemm_watchdog, 4)) break;
                 float4* a4 = reinterpret_cast<float4*>(tiles + s * STAGE_BYTES);
+                if (passes > 1) {
 #pragma unroll 4
-                for (int i = threadIdx.x - 64; i < A_TILE / 16; i += 32 * EPI_WARPS) {
-                    const float4 x = a4[i];
-                    const float4 h = make_float4(tc::tf32_rna(x.x), tc::tf32_rna(x.y), tc::tf32_rna(x.z), tc::tf32_rna(x.w));
-                    a4[i] = h;
-                    if (passes > 1)
-                        a4[i + A_TILE / 16] = make_float4(tc::tf32_rna(x.x - h.x), tc::tf32_rna(x.y - h.y),
-                                                          tc::tf32_rna(x.z - h.z), tc::tf32_rna(x.w - h.w));
+                    for (int i = threadIdx.x - 64; i < A_TILE / 16; i += 32 * EPI_WARPS)
+                        a4[i + A_TILE / 16] = tc::tf32_lo4(a4[i]);
                 }
                 tc::fence_proxy_async();           // generic-proxy writes -> visible to the tensor core
                 __syncwarp();
@@ -364,17 +360,15 @@ __device__ __forceinline__ void split_rows(const float* __restrict__ src, size_t
         if (v4) {
             for (size_t c = 4 * threadIdx.x; c < cols; c += 4 * blockDim.x) {
                 const float4 x = __ldg(reinterpret_cast<const float4*>(s_row + c));
-                const float4 h = make_float4(tc::tf32_rna(x.x), tc::tf32_rna(x.y), tc::tf32_rna(x.z), tc::tf32_rna(x.w));
-                *reinterpret_cast<float4*>(h_row + c) = h;
-                if (l_row)   // TF32-exact: no truncation bias in the MMA
-                    *reinterpret_cast<float4*>(l_row + c) = make_float4(tc::tf32_rna(x.x - h.x), tc::tf32_rna(x.y - h.y),
-                                                                        tc::tf32_rna(x.z - h.z), tc::tf32_rna(x.w - h.w));
+                *reinterpret_cast<float4*>(h_row + c) = make_float4(tc::tf32_hi(x.x), tc::tf32_hi(x.y), tc::tf32_hi(x.z),
+                                                                    tc::tf32_hi(x.w));
+                if (l_row) *reinterpret_cast<float4*>(l_row + c) = tc::tf32_lo4(x);
             }
         } else {
             for (size_t c = threadIdx.x; c < cols; c += blockDim.x) {
-                const float x = s_row[c], h = tc::tf32_rna(x);
-                h_row[c] = h;
-                if (l_row) l_row[c] = tc::tf32_rna(x - h);
+                const float x = s_row[c];
+                h_row[c] = tc::tf32_hi(x);
+                if (l_row) l_row[c] = tc::tf32_lo(x);
             }
         }
     }
@@ -411,9 +405,8 @@ __global__ void k_im2col_split(const LcuGemmGroup* __restrict__ groups, LcuConvS
         float x = 0.f;
         if (ih >= 0 && iw >= 0 && ih < cs.h && iw < cs.w)
             x = __ldg(in + (((size_t)n * cs.ci + ci) * cs.h + ih) * (size_t)cs.w + iw);
-        const float h = tc::tf32_rna(x);
-        hrow[p] = h;
-        if (lrow) lrow[p] = tc::tf32_rna(x - h);
+        hrow[p] = tc::tf32_hi(x);
+        if (lrow) lrow[p] = tc::tf32_lo(x);
     }
 }
 

@@ -183,5 +183,15 @@ __device__ __forceinline__ float tf32_rna(float x) {
     asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
     return __uint_as_float(r);
 }
+// 3xTF32 split used by the GEMM and conv kernels: hi = x with the low 13 mantissa bits
+// cleared (what kind::tf32 reads from a full FP32 word: measured, the MMA ignores those
+// bits), lo = the remainder x - hi (exact in FP32) rounded to TF32. Because the MMA
+// truncates by itself, a plain FP32 tile can serve as the hi operand unchanged and only
+// lo has to be made.
+__device__ __forceinline__ float tf32_hi(float x) { return __uint_as_float(__float_as_uint(x) & 0xffffe000u); }
+__device__ __forceinline__ float tf32_lo(float x) { return tf32_rna(x - tf32_hi(x)); }
+__device__ __forceinline__ float4 tf32_lo4(float4 x) {
+    return make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+}
 
 }  // namespace tc
