@@ -15,65 +15,100 @@ __global__ void __launch_bounds__(THREADS) k_gemm_simt(const LcuGemmGroup* __res
 }
 
 // Small products (the MLP's 64 x 784 x 256): a 128 x 128 tile grid would leave almost
-// every SM idle, so each CTA takes a 16 x 32 output tile. K is walked in chunks of 128:
-// all 256 threads load the chunk's A (16 x 128) and B (128 x 32) tiles into shared memory
-// at once (one memory round trip per chunk), then warp w accumulates k = 16w .. 16w+15 of
-// the chunk; the eight warps' partial tiles are summed in a fixed order (deterministic)
-// and the epilogue is applied as in DenseC.
+// every SM idle, so each CTA takes a 16 x 32 output tile. K is walked in chunks of 128
+// whose A (16 x 128) and B (128 x 32) tiles are copied into shared memory several chunks
+// ahead; warp w accumulates k = 16w .. 16w+15 of each chunk; the eight warps' partial
+// tiles are summed in a fixed order (deterministic) and the epilogue is applied as in
+// DenseC.
 constexpr int SK_TM = 16, SK_TN = 32, SK_WARPS = 8, SK_KC = 128;
+// K chunks in flight per CTA: each chunk (A 16 x 128, B 128 x 32) is copied global ->
+// shared with cp.async (4-byte copies, zero-filled past the matrix edge) SK_STAGES - 1
+// chunks ahead, so a small product pays about one memory latency instead of one per chunk.
+constexpr int SK_STAGES = 6;
+constexpr int SK_A_FLOATS = SK_TM * (SK_KC + 1), SK_B_FLOATS = SK_KC * SK_TN;
+constexpr int SK_SMEM_BYTES = SK_STAGES * (SK_A_FLOATS + SK_B_FLOATS) * 4 + SK_WARPS * SK_TM * (SK_TN + 1) * 4;
+
+// `src` must be a valid address even when !valid (nothing is read then; the word is zeroed)
+__device__ __forceinline__ void cp_async4(float* dst, const float* src, bool valid) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 __global__ void __launch_bounds__(256) k_gemm_skinny(const LcuGemmGroup* __restrict__ groups, LcuGemmGroup one,
                                                      size_t M, size_t N, size_t K, int epi) {
-    __shared__ float As[SK_TM][SK_KC + 1];
-    __shared__ float Bs[SK_KC][SK_TN];
-    __shared__ float part[SK_WARPS][SK_TM][SK_TN + 1];
+    extern __shared__ float sk_smem[];
+    float* As0 = sk_smem;                                          // [stage][16][129]
+    float* Bs0 = sk_smem + SK_STAGES * SK_A_FLOATS;                // [stage][128][32]
+    float* part = Bs0 + SK_STAGES * SK_B_FLOATS;                   // [warp][16][33]
     const LcuGemmGroup gr = groups ? groups[blockIdx.z] : one;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const size_t m0 = (size_t)blockIdx.y * SK_TM, n0 = (size_t)blockIdx.x * SK_TN;
+    const int chunks = (int)((K + SK_KC - 1) / SK_KC);
+    auto load = [&](int kc) {                                      // chunk kc -> stage kc % SK_STAGES
+        const size_t k0 = (size_t)kc * SK_KC;
+        float* As = As0 + (kc % SK_STAGES) * SK_A_FLOATS;
+        float* Bs = Bs0 + (kc % SK_STAGES) * SK_B_FLOATS;
+#pragma unroll
+        for (int r = 0; r < SK_TM * SK_KC / 256; r++) {           // A: 16 rows x 128 k, coalesced along k
+            const int idx = threadIdx.x + 256 * r, i = idx / SK_KC, kk = idx % SK_KC;
+            const bool v = m0 + i < M && k0 + kk < K;
+            cp_async4(As + i * (SK_KC + 1) + kk, v ? gr.a + (m0 + i) * K + k0 + kk : gr.a, v);
+        }
+#pragma unroll
+        for (int r = 0; r < SK_KC * SK_TN / 256; r++) {           // B: 128 k x 32 n, coalesced along n
+            const int idx = threadIdx.x + 256 * r, kk = idx / SK_TN, j = idx % SK_TN;
+            const bool v = k0 + kk < K && n0 + j < N;
+            cp_async4(Bs + kk * SK_TN + j, v ? gr.b + (k0 + kk) * N + n0 + j : gr.b, v);
+        }
+    };
     float acc[SK_TM];
 #pragma unroll
     for (int i = 0; i < SK_TM; i++) acc[i] = 0.f;
-    for (size_t k0 = 0; k0 < K; k0 += SK_KC) {
-        float av[SK_TM * SK_KC / 256], bv[SK_KC * SK_TN / 256];
 #pragma unroll
-        for (int r = 0; r < SK_TM * SK_KC / 256; r++) {        // A: 16 rows x 128 k, coalesced along k
-            const int idx = threadIdx.x + 256 * r, i = idx / SK_KC, kk = idx % SK_KC;
-            av[r] = (m0 + i < M && k0 + kk < K) ? __ldg(gr.a + (m0 + i) * K + k0 + kk) : 0.f;
-        }
-#pragma unroll
-        for (int r = 0; r < SK_KC * SK_TN / 256; r++) {        // B: 128 k x 32 n, coalesced along n
-            const int idx = threadIdx.x + 256 * r, kk = idx / SK_TN, j = idx % SK_TN;
-            bv[r] = (k0 + kk < K && n0 + j < N) ? __ldg(gr.b + (k0 + kk) * N + n0 + j) : 0.f;
-        }
-        __syncthreads();                                        // the previous chunk is consumed
-#pragma unroll
-        for (int r = 0; r < SK_TM * SK_KC / 256; r++) {
-            const int idx = threadIdx.x + 256 * r;
-            As[idx / SK_KC][idx % SK_KC] = av[r];
-        }
-#pragma unroll
-        for (int r = 0; r < SK_KC * SK_TN / 256; r++) {
-            const int idx = threadIdx.x + 256 * r;
-            Bs[idx / SK_TN][idx % SK_TN] = bv[r];
-        }
-        __syncthreads();
+    for (int kc = 0; kc < SK_STAGES - 1; kc++) {                   // prologue: the first chunks in flight
+        if (kc < chunks) load(kc);
+        cp_async_commit();
+    }
+    for (int kc = 0; kc < chunks; kc++) {
+        cp_async_wait<SK_STAGES - 2>();                            // this thread's copies of chunk kc landed
+        __syncthreads();                                           // everyone's; chunk kc - 1 is consumed
+        if (kc + SK_STAGES - 1 < chunks) load(kc + SK_STAGES - 1);
+        cp_async_commit();
+        const float* As = As0 + (kc % SK_STAGES) * SK_A_FLOATS;
+        const float* Bs = Bs0 + (kc % SK_STAGES) * SK_B_FLOATS;
 #pragma unroll
         for (int kk = warp * (SK_KC / SK_WARPS); kk < (warp + 1) * (SK_KC / SK_WARPS); kk++) {
-            const float b = Bs[kk][lane];
+            const float b = Bs[kk * SK_TN + lane];
 #pragma unroll
-            for (int i = 0; i < SK_TM; i++) acc[i] = fmaf(As[i][kk], b, acc[i]);
+            for (int i = 0; i < SK_TM; i++) acc[i] = fmaf(As[i * (SK_KC + 1) + kk], b, acc[i]);
         }
     }
+    cp_async_wait<0>();
 #pragma unroll
-    for (int i = 0; i < SK_TM; i++) part[warp][i][lane] = acc[i];
+    for (int i = 0; i < SK_TM; i++) part[(warp * SK_TM + i) * (SK_TN + 1) + lane] = acc[i];
     __syncthreads();
     const DenseC C{gr.c, gr.bias, gr.resid, M, N, N, epi};
     for (int o = threadIdx.x; o < SK_TM * SK_TN; o += blockDim.x) {
         const int i = o / SK_TN, j = o % SK_TN;
         float sum = 0.f;
 #pragma unroll
-        for (int w = 0; w < SK_WARPS; w++) sum += part[w][i][j];
+        for (int w = 0; w < SK_WARPS; w++) sum += part[(w * SK_TM + i) * (SK_TN + 1) + j];
         C(m0 + i, n0 + j, sum);
     }
+}
+
+static bool skinny_configured() {
+    static bool done[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return false;
+    if (!done[dev] &&
+        cudaFuncSetAttribute(k_gemm_skinny, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_BYTES) == cudaSuccess)
+        done[dev] = true;
+    return done[dev];
 }
 
 static bool use_skinny(size_t M, size_t N, int count) {
@@ -331,7 +366,8 @@ lancius_error lcu_gemm_simt_grouped(const LcuGemmGroup* d_groups, int count, siz
     if (count <= 0 || M == 0 || N == 0) return LANCIUS_ERROR_OK;
     if (use_skinny(M, N, count)) {
         dim3 g((unsigned)((N + SK_TN - 1) / SK_TN), (unsigned)((M + SK_TM - 1) / SK_TM), (unsigned)count);
-        k_gemm_skinny<<<g, 256, 0, lcu_as_stream(stream)>>>(d_groups, LcuGemmGroup{}, M, N, K, epi);
+        if (!skinny_configured()) return lcu_launch_status();
+        k_gemm_skinny<<<g, 256, SK_SMEM_BYTES, lcu_as_stream(stream)>>>(d_groups, LcuGemmGroup{}, M, N, K, epi);
         lcu_note_launch();
         return lcu_launch_status();
     }
@@ -347,7 +383,8 @@ lancius_error lcu_gemm_simt(float* c, const float* a, const float* b, size_t M, 
     LcuGemmGroup g{a, b, c, bias, nullptr};
     if (use_skinny(M, N, 1)) {
         dim3 gs((unsigned)((N + SK_TN - 1) / SK_TN), (unsigned)((M + SK_TM - 1) / SK_TM), 1);
-        k_gemm_skinny<<<gs, 256, 0, lcu_as_stream(stream)>>>(nullptr, g, M, N, K, epi);
+        if (!skinny_configured()) return lcu_launch_status();
+        k_gemm_skinny<<<gs, 256, SK_SMEM_BYTES, lcu_as_stream(stream)>>>(nullptr, g, M, N, K, epi);
         lcu_note_launch();
         return lcu_launch_status();
     }
