@@ -262,6 +262,16 @@ struct Builder {
                     u = sole_user(tail);
                 }
             }
+            // small classifier heads: MATMUL -> ADD(bias) -> SOFTMAX over N <= 32 columns, the
+            // whole row in one CUDA-core tile
+            if (u && u->op == LANCIUS_OP_SOFTMAX && u->ndim == 2 && u->shape[0] == M && u->shape[1] == N &&
+                lcu_gemm_softmax_fold_ok(M, N, m->inputs[0]->shape[m->inputs[0]->ndim - 1])) {
+                ch.epi = LCU_EPI_SOFTMAX_ROW;
+                alias[u->id] = m->id;
+                chain[m->id] = ch;
+                is_chain_root[m->id] = 1;
+                continue;
+            }
             if (u && (u->op == LANCIUS_OP_RELU || u->op == LANCIUS_OP_GELU)) {
                 ch.epi = u->op == LANCIUS_OP_RELU ? LCU_EPI_RELU : LCU_EPI_GELU;
                 alias[u->id] = m->id;

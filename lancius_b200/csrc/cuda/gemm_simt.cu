@@ -90,6 +90,29 @@ __global__ void __launch_bounds__(256) k_gemm_skinny(const LcuGemmGroup* __restr
 #pragma unroll
     for (int i = 0; i < SK_TM; i++) part[(warp * SK_TM + i) * (SK_TN + 1) + lane] = acc[i];
     __syncthreads();
+    if (epi == LCU_EPI_SOFTMAX_ROW) {
+        // the whole row is in this tile (N <= 32, n0 == 0): + bias, then softmax as k_softmax
+        // computes it for rows of at most 32 (max, exp-sum, scale; same shuffle order)
+        for (int i = warp; i < SK_TM; i += SK_WARPS) {
+            const size_t m = m0 + i;
+            if (m >= M) break;                                  // warp-uniform
+            float v = -INFINITY;
+            if (lane < (int)N) {
+                v = 0.f;
+#pragma unroll
+                for (int w = 0; w < SK_WARPS; w++) v += part[(w * SK_TM + i) * (SK_TN + 1) + lane];
+                if (gr.bias) v += __ldg(gr.bias + lane);
+            }
+            float mx = v;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            float e = lane < (int)N ? expf(v - mx) : 0.f, s = e;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+            if (lane < (int)N) gr.c[m * N + lane] = expf(v - mx) * (1.f / s);
+        }
+        return;
+    }
     const DenseC C{gr.c, gr.bias, gr.resid, M, N, N, epi};
     for (int o = threadIdx.x; o < SK_TM * SK_TN; o += blockDim.x) {
         const int i = o / SK_TN, j = o % SK_TN;
@@ -114,6 +137,10 @@ static bool skinny_configured() {
 static bool use_skinny(size_t M, size_t N, int count) {
     const size_t tiles = ((N + BN - 1) / BN) * ((M + BM - 1) / BM) * (size_t)count;
     return tiles < 64 && M * N <= (1u << 20);
+}
+
+int lcu_gemm_softmax_fold_ok(size_t M, size_t N, size_t K) {
+    return N > 0 && N <= (size_t)SK_TN && M * N <= (1u << 20) && !lcu_use_tensor_cores(M, N, K);
 }
 
 __global__ void __launch_bounds__(THREADS) k_gemm_simt1(LcuGemmGroup gr, size_t M, size_t N, size_t K, int epi) {
@@ -364,7 +391,8 @@ lancius_error lcu_conv2d_smallk_ex(float* out, const float* in, const float* w, 
 lancius_error lcu_gemm_simt_grouped(const LcuGemmGroup* d_groups, int count, size_t M, size_t N, size_t K, int epi,
                                     void* stream) {
     if (count <= 0 || M == 0 || N == 0) return LANCIUS_ERROR_OK;
-    if (use_skinny(M, N, count)) {
+    if (epi == LCU_EPI_SOFTMAX_ROW && N > (size_t)SK_TN) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    if (use_skinny(M, N, count) || epi == LCU_EPI_SOFTMAX_ROW) {
         dim3 g((unsigned)((N + SK_TN - 1) / SK_TN), (unsigned)((M + SK_TM - 1) / SK_TM), (unsigned)count);
         if (!skinny_configured()) return lcu_launch_status();
         k_gemm_skinny<<<g, 256, SK_SMEM_BYTES, lcu_as_stream(stream)>>>(d_groups, LcuGemmGroup{}, M, N, K, epi);

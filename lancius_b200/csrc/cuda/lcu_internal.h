@@ -40,6 +40,11 @@ struct LcuTcGemmPlan {
                                  // themselves, split into hi/lo inside the GEMM; no A split pass
 };
 
+// Internal epilogue of the CUDA-core small-product GEMM: bias, then a row softmax over
+// all N <= 32 columns held by one tile (a MATMUL -> ADD(bias) -> SOFTMAX chain)
+constexpr int LCU_EPI_SOFTMAX_ROW = 16;
+int lcu_gemm_softmax_fold_ok(size_t M, size_t N, size_t K);
+
 extern "C" {
 size_t lcu_gemm_tc_scratch_bytes(size_t M, size_t N, size_t K, int G, int Ga, int Gb, int passes);
 lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, size_t M, size_t N, size_t K, int G, int Ga, int Gb,

@@ -108,10 +108,10 @@ def test_caller_plan_path(device, orc):
 
 
 def test_fused_launch_count(device):
-    """MLP: 2 fused GEMM epilogues + 1 softmax = 3 launches per graph."""
+    """MLP: 2 GEMM launches per graph (bias + ReLU, and bias + softmax, in their epilogues)."""
     b = configs.mlp(L.Graph())
     run_gpu(device, b)
-    assert device.last_launch_count == 3
+    assert device.last_launch_count == 2
 
 
 def test_lenet_model_file_on_gpu(device, orc):
@@ -223,3 +223,21 @@ def test_conv_chain_nhwc_handoff(device, orc):
     ref = orc.run_graph(g, convs)
     for n, y in zip(convs, y64):
         assert_close(y, ref[n.id], 1e-4)
+
+
+def test_mlp_softmax_head_folded(device, orc):
+    """MATMUL -> ADD(bias) -> SOFTMAX over 10 columns runs as one small-product GEMM whose
+    epilogue does the row softmax; the bytes equal the unfused graph's (GEMM, ADD, SOFTMAX
+    launched separately) and match the FP64 reference."""
+    outs = []
+    for fuse in (True, False):
+        device.set_fusion(fuse)
+        try:
+            b = configs.mlp(L.Graph())
+            (y,), _ = run_gpu(device, b)
+            outs.append((y, b))
+        finally:
+            device.set_fusion(True)
+    assert np.array_equal(outs[0][0], outs[1][0])
+    (ref,) = oracle_outputs(orc, outs[0][1])
+    assert_close(outs[0][0], ref, 1e-4)
