@@ -620,8 +620,9 @@ extern "C" lancius_error lcu_conv2d_tc_nhwc_ex(float* out, const float* in, cons
     if (out_nhwc && !pt) {
         lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP;
     }
-    const char* ptraw = getenv("LCU_CONV_PT_RAW");
-    const int raw = in_nhwc ? 1 : lcu_no_raw_a() ? 0 : pt ? (ptraw && ptraw[0] == '1') : 1;
+    // the persistent kernel takes its input pre-split unless it reads a conv's NHWC output
+    // in place (its 128-channel tiles leave little shared-memory bandwidth for a splitter)
+    const int raw = in_nhwc ? 1 : (lcu_no_raw_a() || pt) ? 0 : 1;
     float* xh = reinterpret_cast<float*>(s); s += al256(xe * 4);
     float* xl = passes > 1 && !raw ? reinterpret_cast<float*>(s) : nullptr; if (passes > 1) s += al256(xe * 4);
     float* wh = reinterpret_cast<float*>(s); s += al256(we * 4);
