@@ -234,7 +234,7 @@ __global__ void __launch_bounds__(256) k_conv_smallk_q(float* __restrict__ out, 
                                                        const float* __restrict__ w, int N, int H, int W, int Co,
                                                        int pad, int Ho, int Wo, int relu) {
     constexpr int K = CI * KH * KW, PW = 3 * S + KW;
-    extern __shared__ float4 wt4[];                      // [K][Co / 4]
+    extern __shared__ float4 wt4[];                      // [K][Co / 4], then (NHWC) 8 x [128 px][16 ch]
     float* wt = reinterpret_cast<float*>(wt4);
     for (int i = threadIdx.x; i < K * Co; i += blockDim.x) {
         const int k = i / Co, co = i - k * Co;
@@ -242,16 +242,21 @@ __global__ void __launch_bounds__(256) k_conv_smallk_q(float* __restrict__ out, 
     }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // NHWC: the warp's 128 pixels x 16 channels are staged, float4 slots XOR-swizzled by
+    // pixel quad, and stored as 64-byte channel runs (whole sectors) instead of 16-byte pieces
+    float4* stg = reinterpret_cast<float4*>(wt + K * Co) + warp * 128 * 4;
     const int groups = Co / 16, quads_per_img = Ho * Wo / 4;
     const long long Q = (long long)N * quads_per_img;
     // warp job: (32 quads, one 16-channel group); blocks stride over the jobs
     const long long jobs = ((Q + 31) / 32) * groups;
     for (long long job = (long long)blockIdx.x * 8 + warp; job < jobs; job += (long long)gridDim.x * 8) {
         const int g = (int)(job % groups);
-        const long long qi = (job / groups) * 32 + lane;
-        if (qi >= Q) continue;
-        const int n = (int)(qi / quads_per_img);
-        const int r = (int)(qi - (long long)n * quads_per_img) * 4;
+        const long long q0 = (job / groups) * 32, qi = q0 + lane;
+        const bool active = qi < Q;
+        if (!NHWC && !active) continue;
+        const long long qc = active ? qi : Q - 1;       // inactive lanes compute a valid quad, store nothing
+        const int n = (int)(qc / quads_per_img);
+        const int r = (int)(qc - (long long)n * quads_per_img) * 4;
         const int ho = r / Wo, wo0 = r - ho * Wo;
         const int y0 = ho * S - pad, x0 = wo0 * S - pad;
         float x[CI][KH][PW];
@@ -285,12 +290,11 @@ __global__ void __launch_bounds__(256) k_conv_smallk_q(float* __restrict__ out, 
                             for (int j = 0; j < 4; j++) acc[c][j] = fmaf(wc[c], x[ci][kh][j * S + kw], acc[c][j]);
                     }
             if (NHWC) {
-                float* o = out + ((size_t)n * Ho * Wo + r) * Co + g * 16 + cq * 4;
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
+                for (int j = 0; j < 4; j++) {        // pixel 4*lane + j, channel slot cq
                     float4 v = make_float4(acc[0][j], acc[1][j], acc[2][j], acc[3][j]);
                     if (relu) { v.x = fmaxf(v.x, 0.f); v.y = fmaxf(v.y, 0.f); v.z = fmaxf(v.z, 0.f); v.w = fmaxf(v.w, 0.f); }
-                    *reinterpret_cast<float4*>(o + (size_t)j * Co) = v;
+                    stg[(4 * lane + j) * 4 + (cq ^ (lane & 3))] = v;
                 }
             } else {
 #pragma unroll
@@ -301,8 +305,21 @@ __global__ void __launch_bounds__(256) k_conv_smallk_q(float* __restrict__ out, 
                 }
             }
         }
+        if (NHWC) {
+            __syncwarp();
+            // 4 lanes per pixel write its 64-byte run of this group's 16 channels
+#pragma unroll 4
+            for (int it = 0; it < 16; it++) {
+                const int idx = it * 32 + lane, px = idx >> 2, c4 = idx & 3;
+                if (q0 + (px >> 2) < Q)
+                    *reinterpret_cast<float4*>(out + ((size_t)q0 * 4 + px) * Co + g * 16 + c4 * 4) =
+                        stg[px * 4 + (c4 ^ ((px >> 2) & 3))];
+            }
+            __syncwarp();
+        }
     }
 }
+
 
 extern "C" {
 
@@ -350,9 +367,12 @@ lancius_error lcu_conv2d_smallk_ex(float* out, const float* in, const float* w, 
     if (qshape) {
         const size_t jobs = ((N * Ho * Wo / 4 + 31) / 32) * (Co / 16);
         const unsigned qgrid = (unsigned)std::min<size_t>((jobs + 7) / 8, 148u * 16u);
-        const size_t qsmem = Co * K * 4;
+        const size_t qsmem = Co * K * 4 + (out_nhwc ? 8 * 128 * 16 * 4 : 0);
 #define LCU_SMALLKQ(ci, kh, kw, s)                                                                                    \
         if (Ci == ci && Kh == kh && Kw == kw && stride == s) {                                                        \
+            if (out_nhwc && cudaFuncSetAttribute(k_conv_smallk_q<ci, kh, kw, s, true>,                              \
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)qsmem) != cudaSuccess)\
+                return lcu_launch_status();                                                                           \
             if (out_nhwc)                                                                                             \
                 k_conv_smallk_q<ci, kh, kw, s, true><<<qgrid, 256, qsmem, st>>>(out, in, w, (int)N, (int)H, (int)W,  \
                                                                                (int)Co, (int)pad, (int)Ho, (int)Wo,  \
