@@ -166,7 +166,7 @@ lancius_error lcu_matmul_noalloc(float* out, const float* a, const float* b, siz
                                  const float* bias, int epilogue, int mode, void* stream);
 size_t lcu_noalloc_scratch_capacity(void);
 
-/* ---- training, LLM and INT8 operators (SURVEY-ranked "next" rows) --------- */
+/* ---- training, LLM and INT8 operators (the reference's kernels beyond inference) */
 lancius_error lcu_sum(float* out, const float* a, size_t n, void* stream);                       /* scheduler.c:251-256 */
 lancius_error lcu_sum_axis0(float* out, const float* a, size_t rows, size_t cols, void* stream); /* :257-262 */
 lancius_error lcu_transpose(float* out, const float* a, size_t rows, size_t cols, void* stream); /* :246-250 */
