@@ -50,6 +50,8 @@ struct ConvArgs {
     int passes, relu;
     int raw_b;       // 1: the input map covers plain FP32 NHWC; the epilogue warps split it on chip
     int out_nhwc;    // 1 (persistent kernel only): store the output NHWC for a conv that reads it next
+    float* out_lo;   // with out_nhwc: also store tf32_lo of every output there (NHWC), so the next
+                     // conv loads hi (the value itself) and lo by TMA and needs no splitter
 };
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
@@ -411,7 +413,10 @@ k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
                     for (int pxi = 0; pxi < 32 && c + pxi < valid; pxi++) {
                         float x = sb[lane * 32 + ((((pxi >> 2) ^ (lane & 7))) << 2) + (pxi & 3)];
                         if (a.relu) x = fmaxf(x, 0.f);
-                        if (co < a.co) o[(size_t)pxi * a.co] = x;
+                        if (co < a.co) {
+                            o[(size_t)pxi * a.co] = x;
+                            if (a.out_lo) a.out_lo[(o - out) + (size_t)pxi * a.co] = tc::tf32_lo(x);
+                        }
                     }
                     __syncwarp();
                     continue;
@@ -586,7 +591,7 @@ extern "C" size_t lcu_conv_nhwc_scratch_bytes(LcuConvShape cs, int passes) {
 
 extern "C" lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const float* w, LcuConvShape cs, int relu,
                                             int mode, void* scratch, void* stream) {
-    return lcu_conv2d_tc_nhwc_ex(out, in, w, cs, relu, mode, scratch, stream, 0, 0);
+    return lcu_conv2d_tc_nhwc_ex(out, in, w, cs, relu, mode, scratch, stream, 0, 0, nullptr, nullptr);
 }
 
 static bool conv_pt_enabled() {
@@ -604,9 +609,11 @@ extern "C" lancius_error lcu_nhwc_to_nchw(void* out, const float* in, int n, int
 }
 
 // in_nhwc: `in` already holds the input as NHWC FP32 (written by the previous conv);
-// out_nhwc: store the output NHWC (persistent kernel only).
+// in_lo: with in_nhwc, tf32_lo of that input (NHWC), loaded by TMA instead of split on chip;
+// out_nhwc: store the output NHWC (persistent kernel only); out_lo: also its tf32_lo.
 extern "C" lancius_error lcu_conv2d_tc_nhwc_ex(float* out, const float* in, const float* w, LcuConvShape cs, int relu,
-                                               int mode, void* scratch, void* stream, int in_nhwc, int out_nhwc) {
+                                               int mode, void* scratch, void* stream, int in_nhwc, int out_nhwc,
+                                               const float* in_lo, float* out_lo) {
     const int passes = mode == LCU_MODE_TF32 ? 1 : 3;
     if (!lcu_conv_nhwc_supported(cs) || !scratch) { lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP; }
     cudaStream_t st = lcu_as_stream(stream);
@@ -622,14 +629,15 @@ extern "C" lancius_error lcu_conv2d_tc_nhwc_ex(float* out, const float* in, cons
     }
     // the persistent kernel takes its input pre-split unless it reads a conv's NHWC output
     // in place (its 128-channel tiles leave little shared-memory bandwidth for a splitter)
-    const int raw = in_nhwc ? 1 : (lcu_no_raw_a() || pt) ? 0 : 1;
+    const int raw = in_nhwc ? (in_lo && passes > 1 ? 0 : 1) : (lcu_no_raw_a() || pt) ? 0 : 1;
     float* xh = reinterpret_cast<float*>(s); s += al256(xe * 4);
     float* xl = passes > 1 && !raw ? reinterpret_cast<float*>(s) : nullptr; if (passes > 1) s += al256(xe * 4);
     float* wh = reinterpret_cast<float*>(s); s += al256(we * 4);
     float* wl = passes > 1 ? reinterpret_cast<float*>(s) : nullptr;
 
     if (in_nhwc) {
-        xh = const_cast<float*>(in);                  // read in place, split on chip
+        xh = const_cast<float*>(in);                  // read in place (the MMA truncates it to hi)
+        if (!raw) xl = const_cast<float*>(in_lo);     // lo written by the producer; else split on chip
     } else {
         k_nhwc_split<<<dim3((unsigned)((cs.w + 63) / 64), (unsigned)((cs.ci + 31) / 32), (unsigned)(cs.n * cs.h)), 256, 0, st>>>(
             in, xh, xl, cs.ci, cs.h, cs.w, raw ? 0 : 1);
@@ -670,7 +678,7 @@ extern "C" lancius_error lcu_conv2d_tc_nhwc_ex(float* out, const float* in, cons
     }
     if (!ok) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
     ConvArgs a{cs.n, cs.ci, cs.co, cs.kh, cs.kw, cs.stride, cs.pad, cs.ho, cs.wo, rows, cs.co > 128 ? 2 : 1, passes, relu, raw,
-               out_nhwc};
+               out_nhwc, out_nhwc ? out_lo : nullptr};
     if (pt) {
         const long long T = (long long)cs.n * ((cs.ho + rows - 1) / rows) * ((cs.co + PT_BM - 1) / PT_BM);
         k_conv_pt<<<(unsigned)std::min<long long>(T, n_sm), PT_THREADS, PT_SMEM_BYTES, st>>>(mw_hi, mw_lo, mx_hi, mx_lo, out, a);

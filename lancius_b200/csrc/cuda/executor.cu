@@ -51,6 +51,8 @@ struct Step {
     uint32_t in_id = 0;        // S_CONV: the input node
     int in_nhwc = 0;           // S_CONV: the input slot holds NHWC (written by the previous conv)
     int out_nhwc = 0;          // S_CONV: store the output NHWC for the convs that read it
+    size_t in_lo = (size_t)-1; // S_CONV: tf32_lo of the NHWC input in ctx->lo_buf (float offset)
+    size_t out_lo = (size_t)-1;// S_CONV: where to store tf32_lo of the NHWC output
 };
 
 struct Chain {          // a MATMUL and the epilogue nodes folded into it
@@ -92,6 +94,8 @@ struct lcu_ctx {
     std::vector<CUtensorMap> amaps_host;  // raw-A tensor maps of every step, uploaded to amaps at bind
     CUtensorMap* amaps = nullptr;
     std::vector<uint8_t> nhwc;          // node id -> 1: a conv output stored NHWC (only convs read it)
+    float* lo_buf = nullptr;            // tf32_lo copies of NHWC-kept conv outputs
+    size_t lo_floats = 0;
     std::vector<LcuTcGemmPlan> tc_plans;
     std::vector<size_t> off;            // node id -> byte offset in dmem (NPOS: no storage)
     std::vector<Step> steps;
@@ -118,6 +122,8 @@ static void release_binding(lcu_ctx* c) {
     c->dmem_bytes = 0; c->staging_elems = 0; c->scratch_bytes = 0;
     c->tc_plans.clear();
     c->nhwc.clear();
+    if (c->lo_buf) { cudaFree(c->lo_buf); c->lo_buf = nullptr; }
+    c->lo_floats = 0;
     c->off.clear(); c->steps.clear();
     c->g = nullptr; c->s = nullptr;
 }
@@ -643,8 +649,20 @@ static void plan_nhwc_handoff(lcu_ctx* c, const Builder& b) {
         if (!ok) continue;
         p.out_nhwc = 1;
         c->nhwc[p.node_id] = 1;
+        // The producer also stores tf32_lo of its output, so the consumers load hi (the value
+        // itself) and lo by TMA instead of splitting on chip (LCU_NO_NHWC_LO=1: split on chip)
+        const char* lo_env = getenv("LCU_NO_NHWC_LO");
+        const bool with_lo = !(lo_env && lo_env[0] == '1');
+        if (with_lo) {
+            const LcuConvShape cs = conv_shape(p);
+            p.out_lo = c->lo_floats;
+            c->lo_floats += align_up((size_t)cs.n * cs.co * cs.ho * cs.wo, 64);
+        }
         for (Step& q : c->steps)
-            if (q.kind == S_CONV && q.in_id == p.node_id) q.in_nhwc = 1;
+            if (q.kind == S_CONV && q.in_id == p.node_id) {
+                q.in_nhwc = 1;
+                if (with_lo) q.in_lo = p.out_lo;
+            }
     }
 }
 
@@ -776,6 +794,10 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
         // zero until the first upload, like the node slots of never-uploaded inputs
         ce = cudaMemsetAsync(c->wsplit, 0, c->wsplit_floats * sizeof(float), c->stream);
         if (ce != cudaSuccess) { release_binding(c); return cuda_fail(ce); }
+    }
+    if (c->lo_floats) {
+        ce = cudaMalloc(&c->lo_buf, c->lo_floats * sizeof(float));
+        if (ce != cudaSuccess) { cudaGetLastError(); release_binding(c); return fail(LANCIUS_ERROR_OOM); }
     }
     if (!c->amaps_host.empty()) {
         const size_t bytes = c->amaps_host.size() * sizeof(CUtensorMap);
@@ -1023,7 +1045,8 @@ static lancius_error run_steps(lcu_ctx* c) {
                                           (int)s.stride, (int)s.pad, (int)ho, (int)wo};
                     if (lcu_conv_nhwc_supported(cs) && !lcu_conv_force_im2col()) {
                         e = lcu_conv2d_tc_nhwc_ex(F(s.out), F(s.in0), F(s.in1), cs, s.relu, c->mode, c->scratch, st,
-                                                  s.in_nhwc, s.out_nhwc);
+                                                  s.in_nhwc, s.out_nhwc, s.in_lo != NPOS ? c->lo_buf + s.in_lo : nullptr,
+                                                  s.out_lo != NPOS ? c->lo_buf + s.out_lo : nullptr);
                         break;
                     }
                     LcuTcGemmPlan& p = c->tc_plans[s.plan_idx];
@@ -1040,7 +1063,7 @@ static lancius_error run_steps(lcu_ctx* c) {
                 }
                 if (s.out_nhwc)
                     e = lcu_conv2d_smallk_ex(F(s.out), F(s.in0), F(s.in1), s.cn, s.ci, s.h, s.w, s.co, s.kh, s.kw, s.stride,
-                                             s.pad, s.relu, 1, st);
+                                             s.pad, s.relu, 1, st, s.out_lo != NPOS ? c->lo_buf + s.out_lo : nullptr);
                 else
                     e = lcu_conv2d(F(s.out), F(s.in0), F(s.in1), s.cn, s.ci, s.h, s.w, s.co, s.kh, s.kw, s.stride, s.pad,
                                    s.relu, c->mode, st);

@@ -1,5 +1,6 @@
 // CUDA-core FP32 GEMM and implicit-GEMM conv launchers (see gemm_simt.cuh).
 #include "gemm_simt.cuh"
+#include "tc_common.cuh"
 
 #include <algorithm>
 
@@ -232,7 +233,7 @@ __global__ void __launch_bounds__(256) k_conv_smallk(float* __restrict__ out, co
 template <int CI, int KH, int KW, int S, bool NHWC>
 __global__ void __launch_bounds__(256) k_conv_smallk_q(float* __restrict__ out, const float* __restrict__ in,
                                                        const float* __restrict__ w, int N, int H, int W, int Co,
-                                                       int pad, int Ho, int Wo, int relu) {
+                                                       int pad, int Ho, int Wo, int relu, float* __restrict__ out_lo) {
     constexpr int K = CI * KH * KW, PW = 3 * S + KW;
     extern __shared__ float4 wt4[];                      // [K][Co / 4], then (NHWC) 8 x [128 px][16 ch]
     float* wt = reinterpret_cast<float*>(wt4);
@@ -311,9 +312,14 @@ __global__ void __launch_bounds__(256) k_conv_smallk_q(float* __restrict__ out, 
 #pragma unroll 4
             for (int it = 0; it < 16; it++) {
                 const int idx = it * 32 + lane, px = idx >> 2, c4 = idx & 3;
-                if (q0 + (px >> 2) < Q)
-                    *reinterpret_cast<float4*>(out + ((size_t)q0 * 4 + px) * Co + g * 16 + c4 * 4) =
-                        stg[px * 4 + (c4 ^ ((px >> 2) & 3))];
+                if (q0 + (px >> 2) < Q) {
+                    const size_t o = ((size_t)q0 * 4 + px) * Co + g * 16 + c4 * 4;
+                    const float4 v = stg[px * 4 + (c4 ^ ((px >> 2) & 3))];
+                    *reinterpret_cast<float4*>(out + o) = v;
+                    if (out_lo)      // tf32_lo for a tensor-core conv that loads hi and lo
+                        *reinterpret_cast<float4*>(out_lo + o) =
+                            tc::tf32_lo4(v);
+                }
             }
             __syncwarp();
         }
@@ -349,12 +355,12 @@ int lcu_conv_smallk_nhwc_ok(size_t N, size_t Ci, size_t H, size_t W, size_t Co, 
 
 lancius_error lcu_conv2d_smallk(float* out, const float* in, const float* w, size_t N, size_t Ci, size_t H, size_t W,
                                 size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu, void* stream) {
-    return lcu_conv2d_smallk_ex(out, in, w, N, Ci, H, W, Co, Kh, Kw, stride, pad, relu, 0, stream);
+    return lcu_conv2d_smallk_ex(out, in, w, N, Ci, H, W, Co, Kh, Kw, stride, pad, relu, 0, stream, nullptr);
 }
 
 lancius_error lcu_conv2d_smallk_ex(float* out, const float* in, const float* w, size_t N, size_t Ci, size_t H, size_t W,
                                    size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu, int out_nhwc,
-                                   void* stream) {
+                                   void* stream, float* out_lo) {
     const size_t Ho = (H + 2 * pad - Kh) / stride + 1, Wo = (W + 2 * pad - Kw) / stride + 1;
     const size_t P = N * Ho * Wo, K = Ci * Kh * Kw;
     if (P == 0 || Co == 0) return LANCIUS_ERROR_OK;
@@ -376,11 +382,11 @@ lancius_error lcu_conv2d_smallk_ex(float* out, const float* in, const float* w, 
             if (out_nhwc)                                                                                             \
                 k_conv_smallk_q<ci, kh, kw, s, true><<<qgrid, 256, qsmem, st>>>(out, in, w, (int)N, (int)H, (int)W,  \
                                                                                (int)Co, (int)pad, (int)Ho, (int)Wo,  \
-                                                                               relu);                                \
+                                                                               relu, out_lo);                        \
             else                                                                                                      \
                 k_conv_smallk_q<ci, kh, kw, s, false><<<qgrid, 256, qsmem, st>>>(out, in, w, (int)N, (int)H, (int)W, \
                                                                                 (int)Co, (int)pad, (int)Ho, (int)Wo, \
-                                                                                relu);                               \
+                                                                                relu, nullptr);                      \
             lcu_note_launch();                                                                                        \
             return lcu_launch_status();                                                                               \
         }

@@ -94,14 +94,15 @@ lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const float* w, Lc
 // in_nhwc: the input already is NHWC FP32 (a previous conv's output); out_nhwc: write the
 // output NHWC (needs lcu_conv_nhwc_out_ok)
 lancius_error lcu_conv2d_tc_nhwc_ex(float* out, const float* in, const float* w, LcuConvShape cs, int relu, int mode,
-                                   void* scratch, void* stream, int in_nhwc, int out_nhwc);
+                                   void* scratch, void* stream, int in_nhwc, int out_nhwc, const float* in_lo,
+                                   float* out_lo);
 int lcu_conv_nhwc_out_ok(LcuConvShape cs);
 // NHWC FP32 -> NCHW FP32 (f64 = 0) or FP64 (f64 = 1)
 lancius_error lcu_nhwc_to_nchw(void* out, const float* in, int n, int c, int h, int w, int f64, void* stream);
 // short-reduction conv writing NHWC (out_nhwc) where lcu_conv_smallk_nhwc_ok holds
 lancius_error lcu_conv2d_smallk_ex(float* out, const float* in, const float* w, size_t N, size_t Ci, size_t H, size_t W,
                                    size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu, int out_nhwc,
-                                   void* stream);
+                                   void* stream, float* out_lo);
 int lcu_conv_smallk_nhwc_ok(size_t N, size_t Ci, size_t H, size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride,
                             size_t pad);
 int lcu_conv_force_im2col(void);

@@ -177,7 +177,8 @@ def test_watchdog_reported_by_synchronize(device):
 
 def test_conv_chain_nhwc_handoff(device, orc):
     """A conv output read only by the next conv stays NHWC between them (producer stores
-    NHWC, consumer reads it in place). Same bytes as with the handoff off, and downloads of
+    NHWC and its tf32_lo, consumer reads both in place). Same bytes as with the hand-off off
+    and as with the consumer splitting on chip, and downloads of
     an NHWC-kept output (FP64 and FP32) come back NCHW. The first conv's output is dead
     after the second conv and its slot is reused by the third, so only the last two conv
     outputs are compared (the second is kept NHWC and read in the last wave)."""
@@ -208,16 +209,19 @@ def test_conv_chain_nhwc_handoff(device, orc):
         return [device.download(n) for n in convs], [device.download(n, np.float32) for n in convs], (g, arrs, convs)
 
     y64, y32, (g, arrs, convs) = run()
-    os.environ["LCU_NO_NHWC_HANDOFF"] = "1"
-    try:
-        r64, r32, _ = run()
-    finally:
-        del os.environ["LCU_NO_NHWC_HANDOFF"]
+    variants = []
+    for var in ("LCU_NO_NHWC_HANDOFF", "LCU_NO_NHWC_LO"):      # NCHW throughout; NHWC split on chip
+        os.environ[var] = "1"
+        try:
+            variants.append(run()[:2])
+        finally:
+            del os.environ[var]
     assert len(convs) == 2
-    for a, b in zip(y64, r64):
-        assert np.array_equal(a, b)
-    for a, b in zip(y32, r32):
-        assert np.array_equal(a, b)
+    for r64, r32 in variants:
+        for a, b in zip(y64, r64):
+            assert np.array_equal(a, b)
+        for a, b in zip(y32, r32):
+            assert np.array_equal(a, b)
     for n, a in arrs:
         g.bind(n, a)
     ref = orc.run_graph(g, convs)
