@@ -20,6 +20,9 @@ CASES = {
     "mlp": lambda g: configs.mlp(g),
     "attention_b2_s96_h2": lambda g: configs.attention(g, batch=2, seq=96, heads=2),
     "conv_b1_hw20": lambda g: configs.conv_stack(g, batch=1, hw=20),
+    # LAYERNORM + GELU + residual + causal ATTENTION through the reference executor
+    "encoder_causal_b2_s24_l2": lambda g: configs.encoder(g, batch=2, seq=24, layers=2, d_model=64,
+                                                          heads=4, ffn=128, causal=True),
 }
 
 if __name__ == "__main__":

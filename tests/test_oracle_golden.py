@@ -59,6 +59,9 @@ def test_rmsnorm_known_answer(orc):
     lambda g: configs.mlp(g),
     lambda g: configs.attention(g, batch=2, seq=96, heads=2),
     lambda g: configs.conv_stack(g, batch=1, hw=20),
+    # encoder-shaped: LAYERNORM, GELU, residual ADD, causal ATTENTION (the only kind the
+    # reference has); pins the oracle's layernorm (lancius_kernels.c:217-236) and GELU (:238-246)
+    lambda g: configs.encoder(g, batch=2, seq=24, layers=2, d_model=64, heads=4, ffn=128, causal=True),
 ])
 def test_oracle_graph_equals_reference_executor(orc, ref, build):
     """Same graph built with this library and with the reference library; the oracle's
@@ -76,13 +79,18 @@ def test_oracle_graph_equals_reference_executor(orc, ref, build):
         assert np.max(np.abs(mine[o1.id] - r)) <= 1e-12 * max(1.0, np.max(np.abs(r)))
 
 
+ENCODER_GOLDEN = lambda g: configs.encoder(g, batch=2, seq=24, layers=2, d_model=64, heads=4,
+                                            ffn=128, causal=True)
+
+
 def test_committed_golden_fixtures(orc):
     """tests/golden/*.npz were produced by the reference library (make_golden.py)."""
     import os
     here = os.path.join(os.path.dirname(__file__), "golden")
     for name, build in (("mlp", lambda g: configs.mlp(g)),
                         ("attention_b2_s96_h2", lambda g: configs.attention(g, batch=2, seq=96, heads=2)),
-                        ("conv_b1_hw20", lambda g: configs.conv_stack(g, batch=1, hw=20))):
+                        ("conv_b1_hw20", lambda g: configs.conv_stack(g, batch=1, hw=20)),
+                        ("encoder_causal_b2_s24_l2", ENCODER_GOLDEN)):
         fx = np.load(os.path.join(here, f"{name}.npz"))
         g = L.Graph()
         b = build(g)
@@ -91,3 +99,21 @@ def test_committed_golden_fixtures(orc):
         for i, o in enumerate(b.outputs):
             want = fx[f"out{i}"]
             assert np.max(np.abs(got[o.id] - want)) <= 1e-12 * max(1.0, np.max(np.abs(want)))
+
+
+def test_layernorm_gelu_oracle_equals_reference_kernels(orc, ref):
+    """orc.layernorm / orc.gelu against the reference's kernel_layernorm and kernel_gelu
+    (lancius_kernels.c:217-246) called directly, including GELU's +-100 clamp and a
+    constant row (zero variance)."""
+    dp = lambda a: a.ctypes.data_as(C.POINTER(C.c_double))
+    rows, hid = 37, 768
+    x = data.normal(11, (rows, hid), 0.0, 3.0)
+    x[5, :] = 2.5
+    gamma, beta = data.normal(12, (hid,)), data.normal(13, (hid,))
+    out = np.empty_like(x)
+    ref.kernel_layernorm(dp(out), dp(x), dp(gamma), dp(beta), C.c_size_t(rows), C.c_size_t(hid), C.c_double(1e-5))
+    assert np.max(np.abs(orc.layernorm(x, gamma, beta) - out)) <= 1e-12 * np.max(np.abs(out))
+    xg = np.concatenate([data.normal(14, (4096,), 0.0, 4.0), [-150.0, -100.0, -99.9, 0.0, 99.9, 100.0, 150.0]])
+    outg = np.empty_like(xg)
+    ref.kernel_gelu(dp(outg), dp(xg), C.c_size_t(xg.size))
+    assert np.max(np.abs(orc.gelu(xg) - outg)) <= 1e-12 * np.max(np.abs(outg))
