@@ -65,6 +65,32 @@ METRIC = {
 }
 
 
+PER_GPU_BATCH = {"attention": 8, "mlp": 64, "conv": 32, "encoder": 16}
+
+
+def config_of(cfg, workload):
+    """The workload keys both arms print (identical dicts, so the two lines compare)."""
+    return {"workload": workload, "per_gpu_batch": PER_GPU_BATCH.get(cfg)}
+
+
+def attention_traffic():
+    """DRAM bytes (read + write) of one k_attn_tc launch, from the committed ncu summary --
+    only while the kernel source is the one that capture measured (its sha256 prefix is
+    recorded there); None otherwise."""
+    import hashlib
+    try:
+        src = open(os.path.join(ROOT, "lancius_b200", "csrc", "cuda", "attention_tc.cu"), "rb").read()
+        txt = open(os.path.join(ROOT, "profiles", "attention_tcgen05_b8_s512_h8_d64.md")).read()
+    except OSError:
+        return None, None
+    h = hashlib.sha256(src).hexdigest()[:16]
+    import re
+    m = re.search(r"source sha256 \(first 16\): `([0-9a-f]{16})`.*?dram bytes per launch: `(\d+)`", txt, re.S)
+    if not m or m.group(1) != h:
+        return None, h
+    return int(m.group(2)), h
+
+
 def metric_of(cfg, built, seconds_per_graph):
     if cfg in ("attention",):
         return built.bytes / seconds_per_graph / 1e9
@@ -150,8 +176,8 @@ def _ref_sample(cfg):
     factor from the sample's time to one full unit of the metric, description)."""
     from lancius_b200 import configs
     if cfg == "attention":
-        return (lambda g: configs.attention(g, batch=2, seq=512, heads=8, head_dim=64, seed=1)), 4.0, \
-            "2 of 8 batch elements (S512 H8 D64 causal), scaled x4 to one batch-8 graph"
+        return (lambda g: configs.attention(g, batch=8, seq=512, heads=8, head_dim=64, seed=1)), 1.0, \
+            "the full batch-8 graph (S512 H8 D64 causal)"
     if cfg == "mlp":
         return (lambda g: configs.mlp(g, batch=64, seed=0)), 1.0, "the full batch-64 graph"
     if cfg == "conv":
@@ -227,7 +253,8 @@ def run_b200(args, rank, world, local_rank):
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
 
-    dev = L.Device(local_rank)
+    mode = L.MODE_TF32 if args.mode == "tf32" else L.MODE_FP32_EXACT
+    dev = L.Device(local_rank, mode)
     g = L.Graph()
     built = build(args.config, g, rank, world)
     sched = g.schedule()
@@ -274,7 +301,7 @@ def run_b200(args, rank, world, local_rank):
     g2 = L.Graph()
     built2 = build(args.config, g2, rank, world)
     sched2 = g2.schedule()
-    dev2 = L.Device(local_rank)
+    dev2 = L.Device(local_rank, mode)
     dev2.set_graph_replay(True)
     dev2.bind(sched2)
     for node, arr in built2.inputs:
@@ -327,11 +354,51 @@ def run_b200(args, rank, world, local_rank):
             d.lib.lcu_host_free(p)
     dev2.close()
 
+    dropin_ms = dropin_e2e_ms(args, rank, world, local_rank, dist)
     if dist:
         t = torch.tensor([total_ms, e2e_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         total_ms, e2e_ms = t.tolist()
+    built.meta["dropin_ms"] = dropin_ms
     return built, total_ms, e2e_ms, dev_ms, launches_per_step, clk, in_bytes, out_bytes, dist
+
+
+def dropin_e2e_ms(args, rank, world, local_rank, dist):
+    """Milliseconds for args.steps requests through the reference's own entry point as an
+    unchanged Lancius program calls it: lancius_schedule_execute_static on a graph whose
+    INPUT nodes hold FP64 host arrays (pageable memory). Each call uploads every bound
+    input (weights included), runs the schedule on the GPU and copies the outputs back to
+    their FP64 host buffers; it returns when they are there. Max over ranks."""
+    import torch
+    import lancius_b200 as L
+    os.environ["LANCIUS_CUDA_DEVICE"] = str(local_rank)
+    os.environ["LANCIUS_CUDA_MODE"] = args.mode
+    lib = L.load()
+    lib.lancius_schedule_execute_static.argtypes = [C.c_void_p, C.c_void_p]
+    lib.lancius_schedule_execute_static.restype = None
+    lib.lancius_dropin_release.argtypes = []
+    g = L.Graph()
+    b = build(args.config, g, rank, world)
+    b.bind_host()
+    sched = g.schedule()
+    flat = np.zeros(sum(n.size * 8 + 32 for n in g.nodes()) // 8 + 1)
+    fp = flat.ctypes.data_as(C.c_void_p)
+    for _ in range(max(2, args.warmup)):
+        lib.lancius_schedule_execute_static(sched.ptr, fp)
+    if lib.lancius_get_error() != 0:
+        raise RuntimeError(f"lancius_schedule_execute_static: error {lib.lancius_get_error()}")
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        lib.lancius_schedule_execute_static(sched.ptr, fp)
+    ms = (time.perf_counter() - t0) * 1e3
+    lib.lancius_dropin_release()
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = t.item()
+    return ms
 
 
 def run_colsplit(args, rank, world, local_rank, n):
@@ -413,9 +480,9 @@ def run_colsplit(args, rank, world, local_rank, n):
             "metric": "GEMM TFLOP/s", "value": round(val, 3), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded U[-1,1), splitmix64)",
-            "config": {"workload": f"gemm{n}_square_fp32_column_split_allgather", "mode": "fp32_exact",
-                       "exchange": "ncclAllGather + repack" if nccl_path else "fused: epilogue stores to peer C over NVLink",
-                       "l2": "flushed between timed steps (256 MiB write)", "parallelism": f"column-split x{world}"},
+            "config": config_of(f"gemm{n}", metric_names(f"gemm{n}")[2]), "mode": "fp32_exact",
+            "exchange": "ncclAllGather + repack" if nccl_path else "fused: epilogue stores to peer C over NVLink",
+            "l2": "flushed between timed steps (256 MiB write)", "parallelism": f"column-split x{world}",
             "roofline": {"bound": "tensor", "achieved": round(val / world, 2), "peak": pk["bf16_tflops"],
                          "unit": "TFLOP/s per GPU", "frac": round(val / world / pk["bf16_tflops"], 4), "traffic": None,
                          "peak_src": pk["src"] + " bf16 (3xTF32 issues 3 TF32 MMAs per product)"},
@@ -540,9 +607,9 @@ def run_decode(args, rank, world, local_rank):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (N(0,1) caches, seeded)",
-            "config": {"workload": f"kv_cache_decode_b{B}_s{S}_h{H}_d{D}_fp32", "per_gpu_batch": B,
-                       "mode": "fp32", "l2": "flushed between timed steps (256 MiB write); caches 2.1 GB > L2",
-                       "parallelism": f"batch-sharded x{world}"},
+            "config": {"workload": f"kv_cache_decode_b{B}_s{S}_h{H}_d{D}_fp32", "per_gpu_batch": B},
+            "mode": "fp32", "l2": "flushed between timed steps (256 MiB write); caches 2.1 GB > L2",
+            "parallelism": f"batch-sharded x{world}",
             "roofline": {"bound": "hbm", "achieved": round(bytes_ / sec / 1e9, 1), "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": round(bytes_ / sec / 1e9 / pk["hbm_gbs"], 4), "traffic": None,
                          "kernel": "k_decode_vec (split-KV) + k_decode_merge", "peak_src": pk["src"] + " hbm_gbs"},
@@ -665,6 +732,8 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="attention")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mode", default="fp32_exact", choices=["fp32_exact", "tf32"],
+                    help="contraction precision: 3xTF32 (FP32-exact, default) or one TF32 pass (fast mode)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
@@ -700,10 +769,12 @@ def main():
     roof = None
     if args.config == "attention":
         achieved = built.bytes / (sec_per_graph) / 1e9
-        # traffic: dram__bytes_read.sum + dram__bytes_write.sum of one k_attn_tc launch
-        # (profiles/attention_tcgen05_b8_s512_h8_d64.md)
+        # traffic: dram__bytes_read.sum + dram__bytes_write.sum of one k_attn_tc launch, from
+        # the ncu capture of this exact kernel source (None when the source changed since)
+        traffic, src_hash = attention_traffic()
         roof = {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": 25256448,
+                "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": traffic,
+                "traffic_src": f"ncu capture of k_attn_tc, source sha256 {src_hash}",
                 "kernel": "attention (one grouped launch over the 8 ATTENTION nodes)",
                 "peak_src": pk["src"] + " hbm_gbs (burst copy)",
                 # the kernel is compute-bound: its algorithmic FLOPs (QK^T and PV over the
@@ -713,11 +784,13 @@ def main():
                                 "frac_of_mode_ceiling": round(built.flops / sec_per_graph / 1e12 / (pk["bf16_tflops"] / 6), 4)}}
     else:
         achieved = built.flops / sec_per_graph / 1e12
+        passes = 1 if args.mode == "tf32" else 3
         roof = {"bound": "tensor", "achieved": round(achieved, 2), "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": round(achieved / pk["bf16_tflops"], 4), "traffic": None, "peak_src": pk["src"] + " bf16",
-                # FP32-exact = 3 TF32 MMAs per product; TF32 dense rate = bf16 / 2
+                # FP32-exact = 3 TF32 MMAs per product, TF32 mode = 1; TF32 dense rate = bf16 / 2
                 "tf32_peak": round(pk["bf16_tflops"] / 2, 1), "frac_of_tf32_peak": round(achieved / (pk["bf16_tflops"] / 2), 4),
-                "mode_ceiling": round(pk["bf16_tflops"] / 6, 1), "frac_of_mode_ceiling": round(achieved / (pk["bf16_tflops"] / 6), 4)}
+                "mode_ceiling": round(pk["bf16_tflops"] / 2 / passes, 1),
+                "frac_of_mode_ceiling": round(achieved / (pk["bf16_tflops"] / 2 / passes), 4)}
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         try:
@@ -731,11 +804,18 @@ def main():
         "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
         "scaling": "strong" if args.config == "encoder_b256" else "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (seeded N(0,1), splitmix64)",
-        "config": {"workload": workload, "per_gpu_batch": built.meta.get("batch"), "mode": "fp32_exact",
-                   "l2": "flushed between timed steps (256 MiB write)", "parallelism": f"batch-sharded x{world}"},
+        "config": config_of(args.config, workload),
+        "mode": args.mode, "l2": "flushed between timed steps (256 MiB write)",
+        "parallelism": f"batch-sharded x{world}",
         "roofline": roof,
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_val, 3), "unit": unit, "h2d_bytes_per_step": in_b, "d2h_bytes_per_step": out_b},
+        # the same workload through lancius_schedule_execute_static, FP64 pageable host buffers
+        # (inputs, weights included, uploaded and outputs copied back on every call)
+        "e2e_dropin": {"value": round(metric_of(args.config, built, built.meta["dropin_ms"] / 1e3 / args.steps) * world, 3),
+                       "unit": unit, "entry": "lancius_schedule_execute_static", "host_dtype": "f64",
+                       "h2d_bytes_per_step": 2 * sum(arr.size * 4 for _, arr in built.inputs),
+                       "d2h_bytes_per_step": 2 * out_b},
         "gpu_launches": launches * args.steps,
         "clocks": clk,
         "step_ms_min_max": [round(min(dev_ms), 5), round(max(dev_ms), 5)],
@@ -778,7 +858,7 @@ def reference_arm(args, metric, unit, workload):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic (seeded N(0,1), splitmix64)",
-            "config": {"workload": workload, "per_gpu_batch": 8, "executor": "lancius_schedule_execute (arena mode)"},
+            "config": config_of(args.config, workload), "executor": "lancius_schedule_execute (arena mode)",
             "cpu_baseline": {"value": round(val, 4), "unit": unit, "kind": "reference", "cores": cores,
                              "sample": "the full batch-8 graph per step on the host CPU, reference C sources "
                                        "compiled by oracle/Makefile; OpenMP threads = all host cores"},
@@ -807,7 +887,7 @@ def reference_arm_sampled(args, metric, unit, workload):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * factor * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic (seeded, splitmix64)",
-            "config": {"workload": workload, "executor": "lancius_schedule_execute (arena mode)"},
+            "config": config_of(args.config, workload), "executor": "lancius_schedule_execute (arena mode)",
             "cpu_baseline": {"value": round(val, 6), "unit": unit, "kind": "reference", "cores": cores,
                              "sample": f"each step: {what}; OpenMP threads = all host cores"},
             "e2e": {"value": round(val, 6), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -835,7 +915,7 @@ def reference_arm_decode(args, metric, unit, workload):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
             "data": "synthetic (N(0,1) caches, seeded)",
-            "config": {"workload": workload, "per_gpu_batch": B, "executor": "kernel_attention_kv_cache per sequence"},
+            "config": {"workload": workload, "per_gpu_batch": B}, "executor": "kernel_attention_kv_cache per sequence",
             "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "kind": "reference", "cores": cores,
                              "sample": f"{nb} of {B} sequences per step, scaled x{B // nb}; one call per sequence "
                                        "on a thread pool of all host cores; FP32-equivalent bytes"},

@@ -43,6 +43,12 @@ void lcu_destroy(lcu_ctx* ctx);
 lancius_error lcu_set_mode(lcu_ctx* ctx, lcu_mode mode);
 void* lcu_stream(lcu_ctx* ctx);                 /* the context's cudaStream_t */
 lancius_error lcu_synchronize(lcu_ctx* ctx);     /* also reports device watchdog flags */
+/* Waits for a stream (NULL = legacy default) and reports a tensor-core watchdog trip
+ * (a bounded mbarrier wait that gave up) as LANCIUS_ERROR_INTERNAL, clearing it. The
+ * per-op launchers that return before the work is done (lcu_attention, lcu_layernorm
+ * ...) report trips here; the blocking ones (lcu_matmul, lcu_conv2d, the INT8 and
+ * column-split GEMMs, lcu_matmul_noalloc) check before they return. */
+lancius_error lcu_check_stream(void* stream);
 /* Test hook (no reference counterpart): launches a kernel whose bounded wait on an
  * mbarrier nothing arrives on gives up and sets the GEMM watchdog word, so the next
  * lcu_synchronize returns LANCIUS_ERROR_INTERNAL (and clears the word). */
@@ -131,7 +137,7 @@ lancius_error lcu_maxpool2d(float* out, const float* in, size_t N, size_t C, siz
 
 /* ---- multi-GPU: column-split GEMM with an NCCL all-gather over NVLink -------
  * No counterpart in the reference (CPU only, distributed execution deferred,
- * KNOWN_LIMITATIONS.md:24); the BASELINE sweep splits the 16384^3 GEMM by columns.
+ * KNOWN_LIMITATIONS.md:24); used to split a large square product (16384^3) by columns.
  * One process (or thread) per GPU. Rank 0 creates the id and shares its 128 bytes
  * with the others out of band (torch.distributed, a file, MPI ...). */
 typedef struct lcu_comm lcu_comm;
@@ -161,10 +167,16 @@ lancius_error lcu_gemm_colsplit_fused(lcu_comm* comm, float* c, const float* a, 
  * FP32-exact mode) return LANCIUS_ERROR_OVERFLOW. All calls on a GPU share the
  * array, so calls that overlap on the GPU race; serialize them. The first call on
  * each device looks up the array's address; make it before any stream capture.
- * Blocks until the product is written. */
+ * With CUDA's default lazy module loading the GPU reserves the array at that first
+ * lookup (which can fail with LANCIUS_ERROR_OOM); with CUDA_MODULE_LOADING=EAGER at
+ * context creation. Blocks until the product is written; a tensor-core watchdog
+ * trip is reported as LANCIUS_ERROR_INTERNAL. */
 lancius_error lcu_matmul_noalloc(float* out, const float* a, const float* b, size_t M, size_t K, size_t N,
                                  const float* bias, int epilogue, int mode, void* stream);
 size_t lcu_noalloc_scratch_capacity(void);
+/* Looks up (and so reserves) the array on the current device without computing:
+ * call it once per GPU at start-up, before any stream capture. */
+lancius_error lcu_noalloc_prepare(void);
 
 /* ---- training, LLM and INT8 operators (the reference's kernels beyond inference) */
 lancius_error lcu_sum(float* out, const float* a, size_t n, void* stream);                       /* scheduler.c:251-256 */

@@ -114,6 +114,7 @@ B200_FUNCS = {
     "lcu_set_mode": (C.c_int, [P, C.c_int]),
     "lcu_stream": (P, [P]),
     "lcu_synchronize": (C.c_int, [P]),
+    "lcu_check_stream": (C.c_int, [P]),
     "lcu_bind_plan": (C.c_int, [P, SCHED_P, GRAPH_P, PLAN_P]),
     "lcu_upload": (C.c_int, [P, NODE_P, P, C.c_int]),
     "lcu_download": (C.c_int, [P, NODE_P, P, C.c_int]),
@@ -168,6 +169,7 @@ B200_FUNCS = {
     "lcu_gemm_colsplit_fused": (C.c_int, [P, P, P, P, c_size, c_size, c_size, C.c_int, P]),
     "lcu_matmul_noalloc": (C.c_int, [P, P, P, c_size, c_size, c_size, P, C.c_int, C.c_int, P]),
     "lcu_noalloc_scratch_capacity": (c_size, []),
+    "lcu_noalloc_prepare": (C.c_int, []),
 }
 
 

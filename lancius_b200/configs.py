@@ -79,10 +79,15 @@ def attention(g, batch=8, seq=512, heads=8, head_dim=64, seed=1, causal=True):
     return b
 
 
-def conv_stack(g, batch=32, hw=224, seed=2, fuse=True):
-    """Config 3: three 3x3 conv+ReLU (3->64 s1, 64->128 s2, 128->256 s2), GAP, Linear 256->1000."""
+def conv_stack(g, batch=32, hw=224, seed=2, fuse=True, rows=None):
+    """Config 3: three 3x3 conv+ReLU (3->64 s1, 64->128 s2, 128->256 s2), GAP, Linear 256->1000.
+    rows=(start, stop) builds the graph for that block of the seeded batch's images."""
     b = Built("conv_stack", g)
-    x = _inp(b, g.input_4d(batch, 3, hw, hw), data.normal(seed, (batch, 3, hw, hw)))
+    xfull = data.normal(seed, (batch, 3, hw, hw))
+    if rows is not None:
+        xfull = xfull[rows[0]:rows[1]]
+        batch = xfull.shape[0]
+    x = _inp(b, g.input_4d(batch, 3, hw, hw), xfull)
     layers = [(3, 64, 1), (64, 128, 2), (128, 256, 2)]
     flops = 0.0
     h, cur = x, hw

@@ -78,6 +78,7 @@ struct lcu_comm {
     float* peer_c[8] = {};              // peer_c[r] = rank r's C (this rank's own at [rank])
     void* peer_base[8] = {};            // IPC mappings to close
     void* dev_buf = nullptr;            // small device buffer for handle exchange and the barrier
+    unsigned char opened[8 * 128] = {}; // the gathered C records the peer mappings were opened from
 };
 
 extern "C" lancius_error lcu_comm_unique_id(void* out, size_t bytes) {
@@ -112,6 +113,7 @@ static void close_peers(lcu_comm* c) {
     }
     c->c_key = nullptr;
     c->c_bytes = 0;
+    memset(c->opened, 0, sizeof(c->opened));
 }
 
 extern "C" void lcu_comm_destroy(lcu_comm* c) {
@@ -180,19 +182,27 @@ GetRangeFn get_range_fn() {
     });
     return fn;
 }
-struct PeerRecord {               // what each rank publishes about its C
+struct PeerRecord {               // what each rank publishes about its C, every call
     cudaIpcMemHandle_t handle;    // of the allocation that contains C
     uint64_t offset;              // C - allocation base
     uint64_t usable;              // allocation bytes from C on
-    uint64_t pad[6];
+    uint64_t c;                   // C's address in the publishing process
+    uint64_t bytes;               // bytes this call writes into every C
+    uint64_t pad[4];
 };
-static_assert(sizeof(PeerRecord) % 16 == 0, "record size");
+static_assert(sizeof(PeerRecord) % 16 == 0 && sizeof(PeerRecord) <= 128, "record size (lcu_comm::opened)");
 }  // namespace
 
-// Opens every rank's C for this C pointer (collective: all ranks call with their own C).
+// Makes every rank's C reachable for this call. Collective on every call: each rank
+// publishes its C's IPC handle, offset and size, the records are all-gathered, and
+// every rank reopens its peer mappings when ANY rank's record differs from the one
+// it last opened -- all ranks see the same gathered records, so all take the same
+// branch, and a buffer freed and reallocated (a new IPC handle) is never used through
+// a stale mapping. The all-gather also orders the call: no rank's GEMM (queued after
+// it on the stream) starts before every rank's stream has reached this point, so the
+// peer stores cannot overtake work queued earlier on the ranks' streams (e.g. a
+// kernel still reading C from the previous call).
 static lancius_error open_peers(lcu_comm* comm, float* c, size_t bytes, cudaStream_t st) {
-    if (comm->c_key == c && comm->c_bytes >= bytes) return LANCIUS_ERROR_OK;
-    close_peers(comm);
     GetRangeFn range = get_range_fn();
     if (!range) { lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP; }
     const int g = comm->nranks;
@@ -206,17 +216,24 @@ static lancius_error open_peers(lcu_comm* comm, float* c, size_t bytes, cudaStre
     if (cudaIpcGetMemHandle(&mine.handle, (void*)base) != cudaSuccess) { cudaGetLastError(); lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
     mine.offset = (uint64_t)((CUdeviceptr)c - base);
     mine.usable = (uint64_t)(size - mine.offset);
+    mine.c = (uint64_t)(uintptr_t)c;
+    mine.bytes = bytes;
     PeerRecord all[8];
     char* d = static_cast<char*>(comm->dev_buf);
     if (cudaMemcpyAsync(d + comm->rank * sizeof(PeerRecord), &mine, sizeof(PeerRecord), cudaMemcpyHostToDevice, st) != cudaSuccess)
         return lcu_check_cuda(cudaGetLastError());
     ncclResult_t r = nccl().all_gather(d + comm->rank * sizeof(PeerRecord), d, sizeof(PeerRecord), ncclInt8, comm->comm, st);
-    if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather (IPC handles)");
+    if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather (C records)");
     if (cudaMemcpyAsync(all, d, g * sizeof(PeerRecord), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
         cudaStreamSynchronize(st) != cudaSuccess)
         return lcu_check_cuda(cudaGetLastError());
+    for (int k = 0; k < g; k++)
+        if (all[k].usable < bytes || all[k].bytes != bytes) {   // every rank fails the same way
+            close_peers(comm); lancius_set_error(LANCIUS_ERROR_SHAPE_MISMATCH); return LANCIUS_ERROR_SHAPE_MISMATCH;
+        }
+    if (comm->c_key == c && memcmp(comm->opened, all, g * sizeof(PeerRecord)) == 0) return LANCIUS_ERROR_OK;
+    close_peers(comm);
     for (int k = 0; k < g; k++) {
-        if (all[k].usable < bytes) { close_peers(comm); lancius_set_error(LANCIUS_ERROR_SHAPE_MISMATCH); return LANCIUS_ERROR_SHAPE_MISMATCH; }
         if (k == comm->rank) { comm->peer_c[k] = c; continue; }
         void* p = nullptr;
         if (cudaIpcOpenMemHandle(&p, all[k].handle, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
@@ -225,6 +242,7 @@ static lancius_error open_peers(lcu_comm* comm, float* c, size_t bytes, cudaStre
         comm->peer_base[k] = p;
         comm->peer_c[k] = reinterpret_cast<float*>(static_cast<char*>(p) + all[k].offset);
     }
+    memcpy(comm->opened, all, g * sizeof(PeerRecord));
     comm->c_key = c;
     comm->c_bytes = bytes;
     return LANCIUS_ERROR_OK;
@@ -266,5 +284,5 @@ extern "C" lancius_error lcu_gemm_colsplit_fused(lcu_comm* comm, float* c, const
         if (r != ncclSuccess) return nccl_fail(r, "ncclAllGather (barrier)");
     }
     // the host record of the group table must stay valid until the copy ran
-    return lcu_check_cuda(cudaStreamSynchronize(st));
+    return lcu_check_stream(st);
 }

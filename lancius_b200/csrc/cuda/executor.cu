@@ -100,7 +100,6 @@ struct lcu_ctx {
     std::vector<size_t> off;            // node id -> byte offset in dmem (NPOS: no storage)
     std::vector<Step> steps;
     cudaGraphExec_t exec = nullptr;
-    int* wd_host = nullptr;             // page-locked copies of the watchdog words
     int graph_launches = 0;
     int last_launches = 0;
 };
@@ -155,7 +154,6 @@ void lcu_destroy(lcu_ctx* c) {
     cudaStreamSynchronize(c->stream);
     release_binding(c);
     cudaStreamDestroy(c->stream);
-    if (c->wd_host) cudaFreeHost(c->wd_host);
     delete c;
 }
 
@@ -182,36 +180,45 @@ lancius_error lcu_set_fusion(lcu_ctx* c, int enable) {
 
 void* lcu_stream(lcu_ctx* c) { return c ? (void*)c->stream : nullptr; }
 
-// Waits for the context's stream, then reads the tensor-core kernels' watchdog words
-// (set when a bounded mbarrier wait gave up): any set word is cleared and reported as
-// LANCIUS_ERROR_INTERNAL. The words are per device, shared by all contexts on it.
-lancius_error lcu_synchronize(lcu_ctx* c) {
-    if (!c) return fail(LANCIUS_ERROR_NULL_PTR);
-    cudaSetDevice(c->device);
+// Points a binding at another schedule object with the same waves over the same nodes
+// (a caller that rebuilds its schedule per run); the launch list is kept.
+void lcu_ctx_retarget_schedule(lcu_ctx* c, lancius_schedule* s) {
+    if (c && c->dmem) c->s = s;
+}
+
+// Waits for `stream`, then reads the tensor-core kernels' watchdog words of the current
+// device (set when a bounded mbarrier wait gave up): any set word is cleared and reported
+// as LANCIUS_ERROR_INTERNAL. The words are per device, shared by every stream on it.
+lancius_error lcu_check_stream(void* stream) {
+    cudaStream_t st = lcu_as_stream(stream);
     int* words[4] = {lcu_gemm_watchdog_addr(), lcu_attention_watchdog_addr(), lcu_conv_watchdog_addr(),
                      lcu_int8_watchdog_addr()};
-    if (!c->wd_host) {
-        if (cudaMallocHost(&c->wd_host, 4 * sizeof(int)) != cudaSuccess) { cudaGetLastError(); c->wd_host = nullptr; }
-    }
-    if (c->wd_host)
-        for (int i = 0; i < 4; i++) {
-            c->wd_host[i] = 0;
-            if (words[i]) cudaMemcpyAsync(&c->wd_host[i], words[i], sizeof(int), cudaMemcpyDeviceToHost, c->stream);
+    int vals[4] = {0, 0, 0, 0};
+    for (int i = 0; i < 4; i++)
+        if (words[i]) {
+            cudaError_t ce = cudaMemcpyAsync(&vals[i], words[i], sizeof(int), cudaMemcpyDeviceToHost, st);
+            if (ce != cudaSuccess) return cuda_fail(ce);
         }
-    cudaError_t ce = cudaStreamSynchronize(c->stream);
+    cudaError_t ce = cudaStreamSynchronize(st);
     if (ce != cudaSuccess) return cuda_fail(ce);
     bool tripped = false;
-    if (c->wd_host)
-        for (int i = 0; i < 4; i++)
-            if (c->wd_host[i] && words[i]) {
-                tripped = true;
-                cudaMemsetAsync(words[i], 0, sizeof(int), c->stream);
-            }
+    for (int i = 0; i < 4; i++)
+        if (vals[i] && words[i]) {
+            tripped = true;
+            cudaMemsetAsync(words[i], 0, sizeof(int), st);
+        }
     if (tripped) {
-        cudaStreamSynchronize(c->stream);
+        cudaStreamSynchronize(st);
         return fail(LANCIUS_ERROR_INTERNAL);
     }
     return LANCIUS_ERROR_OK;
+}
+
+// Waits for the context's stream and reports watchdog trips (lcu_check_stream).
+lancius_error lcu_synchronize(lcu_ctx* c) {
+    if (!c) return fail(LANCIUS_ERROR_NULL_PTR);
+    cudaSetDevice(c->device);
+    return lcu_check_stream(c->stream);
 }
 
 int lcu_last_launch_count(lcu_ctx* c) { return c ? c->last_launches : 0; }

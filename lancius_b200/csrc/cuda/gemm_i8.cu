@@ -419,7 +419,7 @@ lancius_error lcu_matmul_int8(float* out, const float* a, const int8_t* b, doubl
     else if ((e = lcu_int8_pack_kmajor(b8, b, K, N, Kp, s)) != LANCIUS_ERROR_OK) return e;
     if ((e = lcu_launch_status()) != LANCIUS_ERROR_OK) return e;
     e = run_gemm(a8, b8, out, amax_scratch, scale_b, M, N, Kp, 0, 0, st);
-    if (e == LANCIUS_ERROR_OK && own) e = lcu_check_cuda(cudaStreamSynchronize(st));
+    if (e == LANCIUS_ERROR_OK && own) e = lcu_check_stream(st);
     return e;
 }
 
@@ -450,7 +450,7 @@ lancius_error lcu_conv2d_int8(float* out, const float* in, const int8_t* w, doub
     }
     if ((e = lcu_launch_status()) != LANCIUS_ERROR_OK) return e;
     e = run_gemm(a8, b8, out, amax_scratch, scale_w, Co, P, Kp, relu, (int)(Ho * Wo), st);
-    if (e == LANCIUS_ERROR_OK && own) e = lcu_check_cuda(cudaStreamSynchronize(st));
+    if (e == LANCIUS_ERROR_OK && own) e = lcu_check_stream(st);
     return e;
 }
 

@@ -657,7 +657,7 @@ extern "C" lancius_error lcu_gemm_tc(float* c, const float* a, const float* b, s
     if (e != LANCIUS_ERROR_OK) return e;
     e = lcu_gemm_tc_run(&p, d_group, epi, stream);
     // the host-side group record must stay valid until the copy ran
-    if (e == LANCIUS_ERROR_OK) e = lcu_check_cuda(cudaStreamSynchronize(st));
+    if (e == LANCIUS_ERROR_OK) e = lcu_check_stream(st);
     return e;
 }
 
@@ -680,7 +680,7 @@ extern "C" lancius_error lcu_conv2d_tc(float* out, const float* in, const float*
     if (e != LANCIUS_ERROR_OK) return e;
     p.conv = cs;
     e = lcu_gemm_tc_run(&p, d_group, relu ? LCU_EPI_RELU : LCU_EPI_NONE, stream);
-    if (e == LANCIUS_ERROR_OK) e = lcu_check_cuda(cudaStreamSynchronize(st));
+    if (e == LANCIUS_ERROR_OK) e = lcu_check_stream(st);
     return e;
 }
 

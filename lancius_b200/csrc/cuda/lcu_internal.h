@@ -143,4 +143,7 @@ lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, cons
 int lcu_attention_watchdog_read_and_clear(void);
 void lcu_reset_launch_count(void);
 int lcu_launch_count(void);
+// cudaStreamSynchronize + report (and clear) tensor-core watchdog trips as LANCIUS_ERROR_INTERNAL
+lancius_error lcu_check_stream(void* stream);
+void lcu_ctx_retarget_schedule(lcu_ctx* c, lancius_schedule* s);
 }

@@ -93,7 +93,7 @@ lancius_error lcu_conv2d(float* out, const float* in, const float* w, size_t N, 
             if (!scratch) return bad(LANCIUS_ERROR_OOM);
             lancius_error e = lcu_conv2d_tc_nhwc(out, in, w, cs, relu, mode, scratch, stream);
             // the per-device scratch is reused by the next call
-            if (e == LANCIUS_ERROR_OK) e = lcu_check_cuda(cudaStreamSynchronize(lcu_as_stream(stream)));
+            if (e == LANCIUS_ERROR_OK) e = lcu_check_stream(stream);
             return e;
         }
         return lcu_conv2d_tc(out, in, w, cs, relu, mode, stream);

@@ -35,15 +35,34 @@ def rel_err(y, ref_y):
     return float(np.max(np.abs(y - ref_y)) / max(np.max(np.abs(ref_y)), 1e-300))
 
 
-def assert_close(y, ref_y, norm_tol, elem_rel=None, elem_abs=None):
-    """normwise bound, plus (optionally) |y-ref| <= elem_rel*|ref| + elem_abs*max|ref|"""
+# Elementwise part of the FP32-exact bar: |y - ref| <= 1e-4*|ref| + abs_tol*max|ref|.
+# abs_tol is 1e-6 for short reductions. The tensor cores accumulate in FP32 with
+# truncation (round toward zero) after every MMA, which biases each long sum toward zero
+# by about 6e-9 x K of its magnitude (measured on B200: -1.6e-6 at K = 256, -6.3e-6 at
+# 1024, -2.5e-5 at 4096, every tcgen05 kind::tf32 3xTF32 product); an FP32 CPU sum
+# (round to nearest) stays near 2e-7. For contractions over K > 128 the absolute term
+# therefore grows as 8e-9 x K (the measured rate with margin); the normwise bar (1e-4)
+# stays as it is.
+def exact_elem_abs(k=None):
+    return 1e-6 if not k or k <= 128 else 8e-9 * k
+
+
+def assert_close(y, ref_y, norm_tol, elem_rel=None, elem_abs=None, k=None):
+    """normwise max|y-ref|/max|ref| <= norm_tol, and for the FP32-exact bar (norm_tol <=
+    1e-4) also elementwise |y-ref| <= elem_rel*|ref| + elem_abs*max|ref| (defaults 1e-4 and
+    exact_elem_abs(k), k = the longest reduction feeding y)"""
     assert np.all(np.isfinite(y)), "non-finite output"
     e = rel_err(y, ref_y)
     assert e <= norm_tol, f"normwise rel err {e:.3e} > {norm_tol:.1e}"
-    if elem_rel is not None:
+    if elem_rel is None and norm_tol <= 1e-4:
+        elem_rel = 1e-4
+    if elem_rel:   # elem_rel=False: normwise only (a reference that is itself FP32, e.g. ONNX Runtime)
+        if elem_abs is None:
+            elem_abs = exact_elem_abs(k)
         y = np.asarray(y, np.float64)
         ref_y = np.asarray(ref_y, np.float64)
         bound = elem_rel * np.abs(ref_y) + elem_abs * np.max(np.abs(ref_y))
         bad = np.abs(y - ref_y) > bound
-        assert not bad.any(), f"{bad.sum()} elements outside elementwise bound (worst {np.max(np.abs(y-ref_y)-bound):.3e})"
+        need = float(np.max(np.maximum(np.abs(y - ref_y) - elem_rel * np.abs(ref_y), 0)) / max(np.max(np.abs(ref_y)), 1e-300))
+        assert not bad.any(), f"{bad.sum()} elements outside the elementwise bound (abs term needed {need:.3e} > {elem_abs:.1e})"
     return e

@@ -2,7 +2,7 @@
 (training and LLM operators, INT8 weights); shared by the parity tests."""
 import numpy as np
 
-from . import data
+from lancius_b200 import data
 
 
 def training_ops(g, seed=5):

@@ -26,7 +26,9 @@ def test_library_loads_and_exports_all_declared_symbols():
     lib = L.load()
     names = declared()
     assert {"lcu_create", "lancius_schedule_execute_cuda", "lcu_matmul", "lancius_matmul",
-            "lancius_build_memory_plan", "lcu_matmul_noalloc"} <= names
+            "lancius_build_memory_plan", "lcu_matmul_noalloc", "lancius_schedule_execute",
+            "lancius_schedule_execute_parallel", "lancius_schedule_execute_static", "lancius_compile_and_run",
+            "lancius_read_output", "lancius_pool_create", "lcu_check_stream", "lcu_noalloc_prepare"} <= names
     out = subprocess.run(["nm", "-D", "--defined-only", L.LIB_PATH], capture_output=True, text=True).stdout
     exported = {ln.split()[-1] for ln in out.splitlines() if " T " in ln}
     missing = sorted(n for n in names if n not in exported)
@@ -48,3 +50,39 @@ def test_errors_without_device():
     lib = L.load()
     assert not lib.lcu_create(0)
     assert lib.lancius_get_error() == -10
+
+
+def test_pool_runs_every_task():
+    """lancius_pool (reference lancius_threadpool.h): submitted tasks all run before wait returns."""
+    import ctypes as C
+    lib = L.load()
+    lib.lancius_pool_create.restype = C.c_void_p
+    lib.lancius_pool_create.argtypes = [C.c_int]
+    TASK = C.CFUNCTYPE(None, C.c_void_p)
+    lib.lancius_pool_submit.argtypes = [C.c_void_p, TASK, C.c_void_p]
+    lib.lancius_pool_wait.argtypes = [C.c_void_p]
+    lib.lancius_pool_destroy.argtypes = [C.c_void_p]
+    hits = (C.c_int * 300)()
+
+    @TASK
+    def task(arg):
+        hits[arg - 1] += 1
+
+    pool = lib.lancius_pool_create(4)
+    assert pool
+    for rnd in range(2):
+        for i in range(300):
+            lib.lancius_pool_submit(pool, task, i + 1)
+        lib.lancius_pool_wait(pool)
+        assert list(hits) == [rnd + 1] * 300
+    lib.lancius_pool_destroy(pool)
+
+
+def test_dropin_program_links_against_library():
+    """A C program using the reference's executor and stable-FFI names links against
+    liblancius_b200.so alone (run on the GPU by test_gpu_dropin.py)."""
+    L.load()
+    d = os.path.join(ROOT, "tests", "dropin")
+    subprocess.run(["make", "-C", d], check=True, capture_output=True)
+    r = subprocess.run([os.path.join(d, "dropin_main")], capture_output=True, text=True)
+    assert r.returncode == 1 and "usage" in r.stderr

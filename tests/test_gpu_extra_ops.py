@@ -6,7 +6,7 @@ import pytest
 
 from conftest import assert_close
 import lancius_b200 as L
-from lancius_b200 import opgraphs
+import opgraphs
 
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")

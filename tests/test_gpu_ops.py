@@ -61,7 +61,7 @@ def test_matmul(lib, orc, M, K, N, epi):
     da, db, dbias = dev(a), dev(b), dev(bias)
     out = torch.empty((M, N), device="cuda")
     run(lib.lcu_matmul(P(out), P(da), P(db), M, K, N, P(dbias), epi, MODE_FP32_EXACT, None))
-    assert_close(out.cpu().numpy(), ref, 1e-4)
+    assert_close(out.cpu().numpy(), ref, 1e-4, k=K)
 
 
 @pytest.mark.parametrize("M,K,N", [(256, 16384, 256), (300, 4099, 130), (128, 64, 256), (1000, 2000, 3000)])
@@ -73,7 +73,7 @@ def test_matmul_tensor_core_exact(lib, orc, M, K, N):
     ref = orc.matmul(a, b)
     out = torch.empty((M, N), device="cuda")
     run(lib.lcu_matmul(P(out), P(dev(a)), P(dev(b)), M, K, N, None, EPI_NONE, MODE_FP32_EXACT, None))
-    assert_close(out.cpu().numpy(), ref, 1e-4)
+    assert_close(out.cpu().numpy(), ref, 1e-4, k=min(K, 8192))   # K > 8192 is split, partials summed
 
 
 @pytest.mark.parametrize("M,K,N", [(512, 768, 3072), (2048, 2048, 2048)])
@@ -122,7 +122,7 @@ def test_conv2d(lib, orc, shape, relu):
     ref = orc.conv2d(x, w, s, p, bool(relu))
     out = torch.empty(ref.shape, device="cuda")
     run(lib.lcu_conv2d(P(out), P(dev(x)), P(dev(w)), N, Ci, H, W, Co, Kh, Kw, s, p, relu, MODE_FP32_EXACT, None))
-    assert_close(out.cpu().numpy(), ref, 1e-4)
+    assert_close(out.cpu().numpy(), ref, 1e-4, k=Ci * Kh * Kw)
 
 
 @pytest.mark.parametrize("shape", [(2, 64, 32, 32, 128, 3, 3, 1, 1), (2, 16, 64, 64, 48, 5, 5, 2, 2)])

@@ -4,7 +4,7 @@ import numpy as np
 import pytest
 
 import lancius_b200 as L
-from lancius_b200 import opgraphs
+import opgraphs
 import oracle
 
 
