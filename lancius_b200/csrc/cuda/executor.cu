@@ -26,7 +26,7 @@ namespace {
 constexpr size_t NPOS = (size_t)-1;
 constexpr size_t SLOT_ALIGN = 256;
 
-enum StepKind { S_GEMM, S_ATTN, S_CONV, S_LN, S_SOFTMAX, S_SUMAX1, S_ELT, S_BCAST, S_MAXPOOL, S_MISC };
+enum StepKind { S_GEMM, S_ATTN, S_CONV, S_LN, S_SOFTMAX, S_SUMAX1, S_ELT, S_BCAST, S_MAXPOOL, S_MISC, S_MLP2 };
 
 struct Step {
     StepKind kind;
@@ -53,6 +53,11 @@ struct Step {
     int out_nhwc = 0;          // S_CONV: store the output NHWC for the convs that read it
     size_t in_lo = (size_t)-1; // S_CONV: tf32_lo of the NHWC input in ctx->lo_buf (float offset)
     size_t out_lo = (size_t)-1;// S_CONV: where to store tf32_lo of the NHWC output
+    const lancius_node* node0 = nullptr;   // first node of the step's group
+    size_t table2_off = 0;     // S_MLP2: the second product's group table
+    size_t N2 = 0;             // S_MLP2: columns of the second product (its K is N)
+    int epi2 = 0;              // S_MLP2: the second product's epilogue
+    size_t ticket_off = 0;     // S_MLP2: ceil(M / 16) zeroed counters
 };
 
 struct Chain {          // a MATMUL and the epilogue nodes folded into it
@@ -615,8 +620,32 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                 } break;
                 default: return fail(LANCIUS_ERROR_UNSUPPORTED_OP);
             }
+            st.node0 = n;
             c->steps.push_back(st);
         }
+    }
+    // MATMUL(+bias, act) immediately followed by a small MATMUL(+bias) -> SOFTMAX over its
+    // output: one launch (k_mlp2) instead of two. The second product's weight and bias
+    // must be INPUT nodes (resident before the first product runs). LCU_NO_MLP_FUSE=1: two.
+    const char* no_mlp_env = getenv("LCU_NO_MLP_FUSE");
+    const bool no_mlp_fuse = no_mlp_env && no_mlp_env[0] == '1';
+    for (size_t i = 0; !no_mlp_fuse && i + 1 < c->steps.size(); i++) {
+        Step &s1 = c->steps[i], &s2 = c->steps[i + 1];
+        if (s1.kind != S_GEMM || s2.kind != S_GEMM || s1.tc || s2.tc || s1.count != 1 || s2.count != 1) continue;
+        if (s2.epi != LCU_EPI_SOFTMAX_ROW || s1.epi == LCU_EPI_SOFTMAX_ROW || s2.K != s1.N || s2.M != s1.M) continue;
+        const LcuGemmGroup* t1 = reinterpret_cast<const LcuGemmGroup*>(b.tables.data() + s1.table_off);
+        const LcuGemmGroup* t2 = reinterpret_cast<const LcuGemmGroup*>(b.tables.data() + s2.table_off);
+        if ((const void*)t2->a != (const void*)t1->c || t1->resid || t2->resid) continue;
+        const lancius_node* m2 = s2.node0;
+        const Chain& ch2 = b.chain[m2->id];
+        if (m2->inputs[1]->op != LANCIUS_OP_INPUT || (ch2.bias_src && ch2.bias_src->op != LANCIUS_OP_INPUT)) continue;
+        if (!lcu_mlp2_ok(s1.M, s1.N, s1.K, s2.N)) continue;
+        s1.kind = S_MLP2;
+        s1.table2_off = s2.table_off;
+        s1.N2 = s2.N;
+        s1.epi2 = s2.epi;
+        s1.ticket_off = b.add_table(std::vector<unsigned>((s1.M + 15) / 16 + 1, 0u));
+        c->steps.erase(c->steps.begin() + (long)(i + 1));
     }
     return LANCIUS_ERROR_OK;
 }
@@ -746,6 +775,12 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
     auto patch = [&](const float*& p) { if (p) p = reinterpret_cast<const float*>(c->dmem + ((size_t)p - 1)); };
     for (Step& st : c->steps) {
         char* base = b.tables.data() + st.table_off;
+        if (st.kind == S_MLP2) {
+            for (size_t toff : {st.table_off, st.table2_off}) {
+                LcuGemmGroup* t = (LcuGemmGroup*)(b.tables.data() + toff);
+                patch(t->a); patch(t->b); patch((const float*&)t->c); patch(t->bias); patch(t->resid);
+            }
+        }
         if (st.kind == S_GEMM || (st.kind == S_CONV && st.tc)) {
             LcuGemmGroup* t = (LcuGemmGroup*)base;
             for (int i = 0; i < st.count; i++) {
@@ -774,6 +809,16 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
         } else if (st.kind == S_ATTN) {
             LcuAttnGroup* t = (LcuAttnGroup*)base;
             for (int i = 0; i < st.count; i++) { patch(t[i].q); patch(t[i].k); patch(t[i].v); patch((const float*&)t[i].o); }
+            if (lcu_attention_tc_supported(st.D)) {   // Q/K/V tensor maps of every node, read by TMA
+                std::vector<CUtensorMap> maps(3 * st.count);
+                for (int i = 0; i < st.count; i++)
+                    if (!lcu_attention_tc_make_maps(&maps[3 * i], t[i].q, t[i].k, t[i].v, 1, st.S, st.H)) {
+                        release_binding(c);
+                        return fail(LANCIUS_ERROR_INTERNAL);
+                    }
+                st.amap_idx = (int)c->amaps_host.size();
+                c->amaps_host.insert(c->amaps_host.end(), maps.begin(), maps.end());
+            }
         } else if (st.kind == S_LN) {
             LcuRowGroup* t = (LcuRowGroup*)base;
             for (int i = 0; i < st.count; i++) { patch((const float*&)t[i].out); patch(t[i].in); patch(t[i].gamma); patch(t[i].beta); }
@@ -782,6 +827,10 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
             for (int i = 0; i < st.count; i++) { patch((const float*&)t[i].out); patch(t[i].a); patch(t[i].b); }
         }
         st.table_off += table_base;
+        if (st.kind == S_MLP2) {   // its second table and its tickets live in the table region too
+            st.table2_off += table_base;
+            st.ticket_off += table_base;
+        }
     }
     if (!b.tables.empty()) {
         ce = cudaMemcpyAsync(c->dmem + table_base, b.tables.data(), b.tables.size(), cudaMemcpyHostToDevice, c->stream);
@@ -1027,10 +1076,15 @@ static lancius_error run_steps(lcu_ctx* c) {
                     e = lcu_gemm_simt_grouped((const LcuGemmGroup*)(base + s.table_off), s.count, s.M, s.N, s.K, s.epi, st);
                 }
                 break;
+            case S_MLP2:
+                e = lcu_mlp2((const LcuGemmGroup*)(base + s.table_off), (const LcuGemmGroup*)(base + s.table2_off), s.M, s.N,
+                             s.K, s.epi, s.N2, s.epi2, reinterpret_cast<unsigned*>(base + s.ticket_off), st);
+                break;
             case S_ATTN:
                 if (lcu_attention_tc_supported(s.D) && !lcu_force_simt())
                     e = lcu_attention_tc((const LcuAttnGroup*)(base + s.table_off), nullptr, nullptr, nullptr, nullptr,
-                                         (size_t)s.count, s.S, s.H, s.causal, st);
+                                         (size_t)s.count, s.S, s.H, s.causal, c->mode,
+                                         s.amap_idx >= 0 ? c->amaps + s.amap_idx : nullptr, st);
                 else
                     e = lcu_attention_simt((const LcuAttnGroup*)(base + s.table_off), nullptr, nullptr, nullptr, nullptr,
                                            (size_t)s.count, s.S, s.H, s.D, s.causal, st);

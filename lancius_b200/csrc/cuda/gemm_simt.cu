@@ -38,15 +38,15 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-__global__ void __launch_bounds__(256) k_gemm_skinny(const LcuGemmGroup* __restrict__ groups, LcuGemmGroup one,
-                                                     size_t M, size_t N, size_t K, int epi) {
+// One 16 x 32 output tile (rows m0.., columns n0..) of C = A B with the epilogue `epi`,
+// computed by the 256 threads of the calling CTA in the dynamic shared memory.
+__device__ __forceinline__ void skinny_tile(const LcuGemmGroup& gr, size_t M, size_t N, size_t K, int epi, size_t m0,
+                                            size_t n0) {
     extern __shared__ float sk_smem[];
     float* As0 = sk_smem;                                          // [stage][16][129]
     float* Bs0 = sk_smem + SK_STAGES * SK_A_FLOATS;                // [stage][128][32]
     float* part = Bs0 + SK_STAGES * SK_B_FLOATS;                   // [warp][16][33]
-    const LcuGemmGroup gr = groups ? groups[blockIdx.z] : one;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t m0 = (size_t)blockIdx.y * SK_TM, n0 = (size_t)blockIdx.x * SK_TN;
     const int chunks = (int)((K + SK_KC - 1) / SK_KC);
     auto load = [&](int kc) {                                      // chunk kc -> stage kc % SK_STAGES
         const size_t k0 = (size_t)kc * SK_KC;
@@ -124,13 +124,43 @@ __global__ void __launch_bounds__(256) k_gemm_skinny(const LcuGemmGroup* __restr
     }
 }
 
+__global__ void __launch_bounds__(256) k_gemm_skinny(const LcuGemmGroup* __restrict__ groups, LcuGemmGroup one,
+                                                     size_t M, size_t N, size_t K, int epi) {
+    const LcuGemmGroup gr = groups ? groups[blockIdx.z] : one;
+    skinny_tile(gr, M, N, K, epi, (size_t)blockIdx.y * SK_TM, (size_t)blockIdx.x * SK_TN);
+}
+
+// Two chained small products in one launch: H = epi1(A1 B1 + bias1) [M, N1], then
+// Y = epi2(H B2 + bias2) [M, N2 <= 32] -- the MLP's Linear -> ReLU -> Linear -> softmax.
+// Each CTA computes one 16 x 32 tile of H as k_gemm_skinny does and stores it. The CTAs of
+// a 16-row block then take a ticket after a device-scope fence; the last one of the block,
+// which sees every tile of those H rows, computes the block's rows of Y (one tile: all N2
+// columns) and resets the ticket for the next launch on the stream. One launch, and no
+// CTA ever waits for another.
+__global__ void __launch_bounds__(256) k_mlp2(const LcuGemmGroup* __restrict__ l1, const LcuGemmGroup* __restrict__ l2,
+                                              size_t M, size_t N1, size_t K1, int epi1, size_t N2, int epi2,
+                                              unsigned* __restrict__ tickets) {
+    __shared__ unsigned last;
+    const size_t m0 = (size_t)blockIdx.y * SK_TM;
+    skinny_tile(*l1, M, N1, K1, epi1, m0, (size_t)blockIdx.x * SK_TN);
+    __threadfence();                     // this CTA's H tile is visible device-wide before its ticket
+    __syncthreads();
+    if (threadIdx.x == 0) last = atomicAdd(&tickets[blockIdx.y], 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();                     // ... and every other tile of the block is visible here
+    skinny_tile(*l2, M, N2, N1, epi2, m0, 0);
+    if (threadIdx.x == 0) tickets[blockIdx.y] = 0u;
+}
+
 static bool skinny_configured() {
     static bool done[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) return false;
     if (!done[dev] &&
-        cudaFuncSetAttribute(k_gemm_skinny, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_BYTES) == cudaSuccess)
+        cudaFuncSetAttribute(k_gemm_skinny, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_BYTES) == cudaSuccess &&
+        cudaFuncSetAttribute(k_mlp2, cudaFuncAttributeMaxDynamicSharedMemorySize, SK_SMEM_BYTES) == cudaSuccess)
         done[dev] = true;
     return done[dev];
 }
@@ -138,6 +168,21 @@ static bool skinny_configured() {
 static bool use_skinny(size_t M, size_t N, int count) {
     const size_t tiles = ((N + BN - 1) / BN) * ((M + BM - 1) / BM) * (size_t)count;
     return tiles < 64 && M * N <= (1u << 20);
+}
+
+int lcu_mlp2_ok(size_t M, size_t N1, size_t K1, size_t N2) {
+    return M > 0 && M <= 4096 && N2 > 0 && N2 <= (size_t)SK_TN && use_skinny(M, N1, 1) && !lcu_use_tensor_cores(M, N1, K1) &&
+           !lcu_use_tensor_cores(M, N2, N1);
+}
+
+lancius_error lcu_mlp2(const LcuGemmGroup* d_l1, const LcuGemmGroup* d_l2, size_t M, size_t N1, size_t K1, int epi1,
+                       size_t N2, int epi2, unsigned* d_tickets, void* stream) {
+    if (!lcu_mlp2_ok(M, N1, K1, N2)) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    if (!skinny_configured()) return lcu_launch_status();
+    dim3 g((unsigned)((N1 + SK_TN - 1) / SK_TN), (unsigned)((M + SK_TM - 1) / SK_TM), 1);
+    k_mlp2<<<g, 256, SK_SMEM_BYTES, lcu_as_stream(stream)>>>(d_l1, d_l2, M, N1, K1, epi1, N2, epi2, d_tickets);
+    lcu_note_launch();
+    return lcu_launch_status();
 }
 
 int lcu_gemm_softmax_fold_ok(size_t M, size_t N, size_t K) {

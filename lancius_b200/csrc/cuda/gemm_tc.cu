@@ -6,7 +6,9 @@
 // the GEMM kernel streams them with TMA through a 4-stage mbarrier ring:
 //
 //   warp 0      TMA producer (one elected lane)
-//   warp 1      TMEM allocation + tcgen05.mma issue (one lane)
+//   warp 1      TMEM allocation + tcgen05.mma issue for rows 0-127 (one lane)
+//   warp 10     tcgen05.mma issue for rows 128-255 (one lane): one thread's MMAs complete
+//               one after another; two issuing threads overlap on the tensor pipe
 //   warps 2-9   epilogue: tcgen05.ld -> +bias -> ReLU/GELU -> +residual -> global
 //               (two warps per TMEM lane quadrant; in raw-A mode they also split A)
 //
@@ -28,7 +30,8 @@ namespace {
 
 constexpr int BM = 256, BN = 256, BK = 16, STAGES = 3;
 constexpr int EPI_WARPS = 8;                         // two per TMEM lane quadrant
-constexpr int THREADS = 64 + 32 * EPI_WARPS;
+constexpr int THREADS = 64 + 32 * EPI_WARPS + 32;     // + the second MMA issuer (warp 10)
+constexpr int MMA_WARP2 = 2 + EPI_WARPS;
 constexpr int A_TILE = BM * BK * 4;                  // 16 KB (two 128-row halves)
 constexpr int B_CHUNK = BK * 32 * 4;                 // 2 KB: 16 k-rows x 32 n
 constexpr int B_TILE = BN * BK * 4;                  // 16 KB
@@ -61,7 +64,7 @@ struct Smem {
     uint64_t empty[STAGES];
     uint64_t conv[STAGES];     // raw-A mode: the stage's A tile has been split in place
     uint64_t accum;
-    uint64_t drain;
+    uint64_t drain, drain2;
     uint32_t tmem_base;
     int abort;
     int consumed;
@@ -90,10 +93,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            tc::mbar_init(&sm->full[s], 1); tc::mbar_init(&sm->empty[s], 1); tc::mbar_init(&sm->conv[s], EPI_WARPS);
+            tc::mbar_init(&sm->full[s], 1); tc::mbar_init(&sm->empty[s], 2); tc::mbar_init(&sm->conv[s], EPI_WARPS);
         }
-        tc::mbar_init(&sm->accum, 1);
+        tc::mbar_init(&sm->accum, 2);
         tc::mbar_init(&sm->drain, 1);
+        tc::mbar_init(&sm->drain2, 1);
         sm->abort = 0;
         sm->consumed = 0;
         tc::fence_barrier_init();
@@ -136,9 +140,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
             }
             issued = kt + 1;
         }
-    } else if (warp == 1 && lane == 0) {
-        // ---------------- MMA issuer ----------------
+    } else if ((warp == 1 || warp == MMA_WARP2) && lane == 0) {
+        // ---------------- MMA issuers: warp 1 rows 0-127, warp 10 rows 128-255 ----------------
         constexpr uint32_t idesc = tc::idesc_tf32(128, BN, false, true);
+        const int half = warp == 1 ? 0 : 1;
         bool ok = true;
         for (int kt = 0; kt < KT && ok; kt++) {
             int s = kt % STAGES;
@@ -159,8 +164,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
             for (int kb = 0; kb < BK / 8; kb++) {
                 uint64_t dbh = tc::smem_desc(b_hi + kb * 1024, B_CHUNK, 512, tc::SWZ_128B_BASE32B);
                 uint64_t dbl = tc::smem_desc(b_lo + kb * 1024, B_CHUNK, 512, tc::SWZ_128B_BASE32B);
-#pragma unroll
-                for (int half = 0; half < 2; half++) {       // rows 0-127 and 128-255 share the B tile
+                {                                            // rows 0-127 and 128-255 share the B tile
                     const uint32_t hoff = (uint32_t)half * (128 * BK * 4), d = tmem + (uint32_t)half * BN;
                     uint64_t dah = tc::smem_desc(a_hi + hoff + kb * 32, 16, 512, tc::SWZ_64B);
                     uint32_t acc = (kt | kb) ? 1u : 0u;
@@ -174,11 +178,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
                     }
                 }
             }
-            tc::mma_commit(&sm->empty[s]);          // stage s is free once these MMAs retire
-            sm->consumed = kt + 1;
+            tc::mma_commit(&sm->empty[s]);          // stage s is free once both issuers' MMAs retire
+            if (half == 0) sm->consumed = kt + 1;
         }
         if (ok) tc::mma_commit(&sm->accum);
-    } else if (warp >= 2) {
+    } else if (warp >= 2 && warp < MMA_WARP2) {
         if (a_maps) {
             // ---------------- A splitter (raw-A mode) ----------------
             // The FP32 tile serves as hi as it is (the MMA reads it truncated to TF32);
@@ -331,9 +335,10 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
         if (warp == 0 && lane == 0)
             for (int kt = sm->consumed; kt < issued; kt++)
                 if (!tc::mbar_wait(&sm->full[kt % STAGES], (kt / STAGES) & 1, &never, nullptr, 0)) break;
-        if (warp == 1 && lane == 0) {
-            tc::mma_commit(&sm->drain);
-            tc::mbar_wait(&sm->drain, 0, &never, nullptr, 0);
+        if ((warp == 1 || warp == MMA_WARP2) && lane == 0) {
+            uint64_t* d = warp == 1 ? &sm->drain : &sm->drain2;
+            tc::mma_commit(d);
+            tc::mbar_wait(d, 0, &never, nullptr, 0);
         }
         __syncthreads();
     }

@@ -44,6 +44,11 @@ struct LcuTcGemmPlan {
 // all N <= 32 columns held by one tile (a MATMUL -> ADD(bias) -> SOFTMAX chain)
 constexpr int LCU_EPI_SOFTMAX_ROW = 16;
 int lcu_gemm_softmax_fold_ok(size_t M, size_t N, size_t K);
+// Two chained small products in one launch (gemm_simt.cu, k_mlp2): H = epi1(A1 B1 + bias1),
+// then Y = epi2(H B2 + bias2) with N2 <= 32; tickets: ceil(M / 16) zeroed words, left zeroed.
+int lcu_mlp2_ok(size_t M, size_t N1, size_t K1, size_t N2);
+lancius_error lcu_mlp2(const LcuGemmGroup* d_l1, const LcuGemmGroup* d_l2, size_t M, size_t N1, size_t K1, int epi1,
+                       size_t N2, int epi2, unsigned* d_tickets, void* stream);
 
 extern "C" {
 size_t lcu_gemm_tc_scratch_bytes(size_t M, size_t N, size_t K, int G, int Ga, int Gb, int passes);
@@ -138,8 +143,15 @@ int* lcu_int8_watchdog_addr(void);
 int* lcu_gemm_watchdog_addr(void);
 void* lcu_scratch_acquire_gather(size_t bytes);
 void* lcu_scratch_acquire_decode(size_t bytes);
+// mode: LCU_MODE_FP32_EXACT (3xTF32) or LCU_MODE_TF32 (one pass)
+// d_table: a grouped launch over `B` operand sets, whose Q/K/V tensor maps (3 per set, made by
+// lcu_attention_tc_make_maps with B = 1) are at d_maps in device memory; else q/k/v/o are
+// [B][S][H][D] and the maps are built per call.
 lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, const float* k, const float* v, float* o,
-                               size_t B, size_t S, size_t H, int causal, void* stream);
+                               size_t B, size_t S, size_t H, int causal, int mode, const CUtensorMap* d_maps,
+                               void* stream);
+bool lcu_attention_tc_make_maps(CUtensorMap* maps, const float* q, const float* k, const float* v, size_t B, size_t S,
+                                size_t H);
 int lcu_attention_watchdog_read_and_clear(void);
 void lcu_reset_launch_count(void);
 int lcu_launch_count(void);

@@ -108,10 +108,42 @@ def test_caller_plan_path(device, orc):
 
 
 def test_fused_launch_count(device):
-    """MLP: 2 GEMM launches per graph (bias + ReLU, and bias + softmax, in their epilogues)."""
+    """MLP: one launch per graph. Layer 1 (bias + ReLU in the epilogue) and layer 2 (bias +
+    row softmax) run in one kernel: the last CTA of each 16-row block computes that block's
+    layer 2 from the finished hidden rows. LCU_NO_MLP_FUSE=1 gives the two-launch form and
+    the same bits."""
+    import os
     b = configs.mlp(L.Graph())
-    run_gpu(device, b)
-    assert device.last_launch_count == 2
+    (y,), _ = run_gpu(device, b)
+    assert device.last_launch_count == 1
+    device.execute()                       # the tickets were reset: a second run is identical
+    assert np.array_equal(device.download(b.outputs[0]), y)
+    os.environ["LCU_NO_MLP_FUSE"] = "1"
+    try:
+        b2 = configs.mlp(L.Graph())
+        (y2,), _ = run_gpu(device, b2)
+        assert device.last_launch_count == 2
+    finally:
+        del os.environ["LCU_NO_MLP_FUSE"]
+    assert np.array_equal(y, y2)
+
+
+def test_mlp_fused_other_shapes(device, orc):
+    """The one-launch two-layer form on ragged shapes: rows not a multiple of 16, hidden
+    width not a multiple of 32, GELU between the layers, 32 output columns."""
+    from lancius_b200 import data
+    for M, K, N1, N2, act in ((37, 100, 70, 7, "relu"), (130, 64, 96, 32, "gelu"), (5, 33, 40, 3, "relu")):
+        g = L.Graph()
+        bb = configs.Built("mlp_shape", g)
+        x = configs._inp(bb, g.input(M, K), data.uniform(81, (M, K), -1, 1))
+        h = configs._linear(g, bb, x, data.normal(82, (K, N1), 0, 0.2), data.normal(83, (N1,)), M)
+        h = g.relu(h) if act == "relu" else g.gelu(h)
+        y = g.softmax(configs._linear(g, bb, h, data.normal(84, (N1, N2), 0, 0.2), data.normal(85, (N2,)), M))
+        bb.outputs = [y]
+        (got,), _ = run_gpu(device, bb)
+        assert device.last_launch_count == 1, (M, K, N1, N2)
+        (ref,) = oracle_outputs(orc, bb)
+        assert_close(got, ref, 1e-4)
 
 
 def test_lenet_model_file_on_gpu(device, orc):

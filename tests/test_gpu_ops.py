@@ -104,6 +104,18 @@ def test_attention(lib, orc, B, S, H, D, causal):
     assert_close(y, ref, 1e-4)
 
 
+@pytest.mark.parametrize("B,S,H,causal", [(8, 512, 8, 1), (2, 512, 12, 0), (1, 300, 3, 1)])
+def test_attention_tf32_mode(lib, orc, B, S, H, causal):
+    """The one-pass TF32 fast mode of the tensor-core attention (normwise 2e-2)."""
+    D = 64
+    q, k, v = (data.normal(s, (B, S, H, D)) for s in (14, 15, 16))
+    ref = np.stack([orc.attention(q[i], k[i], v[i], bool(causal)) for i in range(B)])
+    out = torch.empty((B, S, H, D), device="cuda")
+    run(lib.lcu_attention(P(out), P(dev(q)), P(dev(k)), P(dev(v)), B, S, H, D, causal, MODE_TF32, None))
+    err = assert_close(out.cpu().numpy(), ref, 2e-2)
+    assert err > 1e-6          # the single pass really ran (FP32-exact stays near 1e-7)
+
+
 @pytest.mark.parametrize("shape", [(2, 3, 17, 19, 8, 3, 3, 1, 1), (2, 64, 28, 28, 128, 3, 3, 2, 1),
                                    (4, 3, 64, 64, 64, 3, 3, 1, 1), (2, 128, 30, 30, 256, 3, 3, 2, 1),
                                    (3, 64, 25, 25, 128, 3, 3, 1, 1),
