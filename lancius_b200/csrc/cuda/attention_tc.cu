@@ -59,7 +59,7 @@ __device__ __forceinline__ unsigned long long gtime() { unsigned long long t; as
 #endif
 
 struct Bars {
-    uint64_t k_full[NSK], k_empty[NSK], k_raw[NSK], v_full[NSV], v_empty[NSV], v_raw[NSV];
+    uint64_t k_full[NSK], k_empty[NSK], v_full[NSV], v_empty[NSV];
     uint64_t s_full[2], p_ready[2], pv_done[2];   // per S/P buffer (tile parity)
     uint64_t q_full, q_empty, q_ready, o_free, drain, drain_pv;
     uint32_t tmem;
@@ -110,7 +110,8 @@ __device__ __forceinline__ float ex2(float x) {
 }
 
 struct Item { LcuAttnGroup p; int b, h, q0, T; };
-struct AttnMaps { CUtensorMap m[3]; };   // Q, K, V over [B][S][H][D] (per-op launches)
+constexpr int NMAPS = 5;                // Q, K, V, K_lo, V_lo
+struct AttnMaps { CUtensorMap m[NMAPS]; };   // over [B][S][H][D] (per-op launches)
 
 // Work slots of the persistent grid. Causal cost grows with the query tile index, so
 // tile qt is paired with tile nqt-1-qt: slot 2p is the heavy member of pair p, slot
@@ -169,10 +170,10 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < NSK; s++) {
-            tc::mbar_init(&bar->k_full[s], 64); tc::mbar_init(&bar->k_empty[s], 1); tc::mbar_init(&bar->k_raw[s], 1);
+            tc::mbar_init(&bar->k_full[s], 1); tc::mbar_init(&bar->k_empty[s], 1);
         }
         for (int s = 0; s < NSV; s++) {
-            tc::mbar_init(&bar->v_full[s], 64); tc::mbar_init(&bar->v_empty[s], 1); tc::mbar_init(&bar->v_raw[s], 1);
+            tc::mbar_init(&bar->v_full[s], 1); tc::mbar_init(&bar->v_empty[s], 1);
         }
         for (int b = 0; b < 2; b++) {
             tc::mbar_init(&bar->s_full[b], 1); tc::mbar_init(&bar->p_ready[b], 128); tc::mbar_init(&bar->pv_done[b], 1);
@@ -407,71 +408,53 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
             }
         }
     } else {
-        // ======================= loaders: warps 5-6 K (+ Q stage), 7-8 V =======================
-        // One elected thread per role puts the raw FP32 tile (= the hi operand) in place with
-        // two TMA boxes (32 d x 64 keys each, swizzled as the MMA reads them); then the role's
-        // 64 threads write lo = x - hi(x) beside it. Tiles are finished two behind the copies,
-        // so two are in flight while one is split.
-        const bool is_k = warp < 7;
-        const int t = threadIdx.x - (is_k ? 160 : 224);   // 0..63
-        const int NSt = is_k ? NSK : NSV;
-        uint8_t* base_st = is_k ? kst : vst;
-        uint64_t* full = is_k ? bar->k_full : bar->v_full;
-        uint64_t* empty = is_k ? bar->k_empty : bar->v_empty;
-        uint64_t* raw = is_k ? bar->k_raw : bar->v_raw;
-        auto hi_off = [&](int r, int d) -> uint32_t { return is_k ? k_off(r, d) : v_off(r, d); };
-        auto lo_off = [&](int r, int d) -> uint32_t { return is_k ? k_off(r + BKV, d) : (uint32_t)KV_HALF + v_off(r, d); };
-        int gt = 0, ii = 0;
-        bool ok = true;
-        auto finish = [&](int g) -> bool {
-            const int st = g % NSt;
-            if (!bwait(&raw[st], (g / NSt) & 1, abort, &g_attn_watchdog, 33)) return false;
-            uint8_t* stage = base_st + st * STAGE;
-#pragma unroll 4
-            for (int c = 0; c < 16 && EXACT; c++) {
-                const int d = 4 * ((c + t) & 15);          // rotate the column group: no bank conflicts
-                const float4 v = *reinterpret_cast<const float4*>(stage + hi_off(t, d));
-                *reinterpret_cast<float4*>(stage + lo_off(t, d)) =
-                    make_float4(v.x - hi_part(v.x), v.y - hi_part(v.y), v.z - hi_part(v.z), v.w - hi_part(v.w));
-            }
-            tc::fence_proxy_async();
-            tc::mbar_arrive(&full[st]);
-            return true;
-        };
-        constexpr int LAG = 2;                       // tiles copied ahead of the one being split
-        for (int x = x0; x < n_slots && ok; x = next_valid(x, n_slots, per, nqt), ii++) {
-            const Item it = get_item(x, table, base, bstride, B, H, nqt, S, causal);
-            const CUtensorMap* maps = gmaps ? gmaps + 3 * it.b : pm.m;
-            const int cb = gmaps ? 0 : it.b;         // the batch coordinate of the map
-            if (t == 0 && gmaps) { tc::tmap_acquire(maps + (is_k ? 0 : 2)); if (is_k) tc::tmap_acquire(maps + 1); }
-            if (is_k && t == 0) {   // this item's Q rows, once the previous ones were taken
-                if (ii >= 1 && !bwait(&bar->q_empty, (ii - 1) & 1, abort, &g_attn_watchdog, 30)) { ok = false; }
-                else {
+        // ======================= producers: warp 5 K (+ Q stage), warp 7 V =======================
+        // One thread per operand puts each key tile in place with TMA: the raw FP32 values
+        // (= the hi operand: the MMA reads only their TF32 bits) and, FP32-exact, their lo
+        // parts from the copies the split pass made (lcu_attention_tc runs it first), each as
+        // two boxes of 32 d x 64 keys, swizzled as the MMA reads them. Nothing is computed
+        // here: splitting in shared memory next to the MMAs' operand reads was measured to
+        // cost more than the split pass's extra HBM traffic.
+        const bool is_k = warp == 5;
+        if ((warp == 5 || warp == 7) && lane == 0) {
+            const int NSt = is_k ? NSK : NSV;
+            uint8_t* base_st = is_k ? kst : vst;
+            uint64_t* full = is_k ? bar->k_full : bar->v_full;
+            uint64_t* empty = is_k ? bar->k_empty : bar->v_empty;
+            int gt = 0, ii = 0;
+            bool ok = true;
+            for (int x = x0; x < n_slots && ok; x = next_valid(x, n_slots, per, nqt), ii++) {
+                const Item it = get_item(x, table, base, bstride, B, H, nqt, S, causal);
+                const CUtensorMap* maps = gmaps ? gmaps + NMAPS * it.b : pm.m;
+                const int cb = gmaps ? 0 : it.b;         // the batch coordinate of the map
+                const CUtensorMap* mhi = maps + (is_k ? 1 : 2);
+                const CUtensorMap* mlo = maps + (is_k ? 3 : 4);
+                if (gmaps) {
+                    tc::tmap_acquire(mhi);
+                    if (EXACT) tc::tmap_acquire(mlo);
+                    if (is_k) tc::tmap_acquire(maps);
+                }
+                if (is_k) {   // this item's Q rows, once the previous ones were taken
+                    if (ii >= 1 && !bwait(&bar->q_empty, (ii - 1) & 1, abort, &g_attn_watchdog, 30)) { ok = false; break; }
                     tc::mbar_expect_tx(&bar->q_full, Q_STAGE);
                     tma_load_4d(qst, maps + 0, &bar->q_full, 0, it.h, it.q0, cb);
                     tma_load_4d(qst + BQ * 128, maps + 0, &bar->q_full, 32, it.h, it.q0, cb);
                 }
-            }
-            if (__shfl_sync(0xffffffffu, (int)ok, 0) == 0) ok = false;
-            if (!ok) break;
-            const CUtensorMap* mkv = maps + (is_k ? 1 : 2);
-            for (int j = 0; j < it.T; j++, gt++) {
-                const int st = gt % NSt;
-                if (t == 0) {
-                    if (gt >= NSt && !bwait(&empty[st], ((gt / NSt) - 1) & 1, abort, &g_attn_watchdog, 31)) ok = false;
-                    else {
-                        uint8_t* dst = base_st + st * STAGE;
-                        tc::mbar_expect_tx(&raw[st], KV_HALF);
-                        for (int a = 0; a < 2; a++)   // d 0-31 and 32-63
-                            tma_load_4d(dst + a * (is_k ? 2 * BKV * 128 : BKV * 128), mkv, &raw[st], 32 * a, it.h,
-                                        j * BKV, cb);
+                for (int j = 0; j < it.T; j++, gt++) {
+                    const int st = gt % NSt;
+                    if (gt >= NSt && !bwait(&empty[st], ((gt / NSt) - 1) & 1, abort, &g_attn_watchdog, 31)) { ok = false; break; }
+                    uint8_t* dst = base_st + st * STAGE;
+                    tc::mbar_expect_tx(&full[st], EXACT ? 2 * KV_HALF : KV_HALF);
+                    for (int a = 0; a < 2; a++) {   // d 0-31 and 32-63
+                        // K: per 32-d atom 64 hi rows then 64 lo rows; V: hi chunks, then lo chunks
+                        uint8_t* h = dst + a * (is_k ? 2 * BKV * 128 : BKV * 128);
+                        tma_load_4d(h, mhi, &full[st], 32 * a, it.h, j * BKV, cb);
+                        if (EXACT) tma_load_4d(h + (is_k ? BKV * 128 : KV_HALF), mlo, &full[st], 32 * a, it.h, j * BKV, cb);
                     }
+                    if (gt < 7) TRACE(is_k ? 50 + gt : 57 + (gt < 6 ? gt : 5));
                 }
-                if (gt >= LAG && !(ok = ok && finish(gt - LAG))) break;
-                if (t == 0 && gt < 7) TRACE(is_k ? 50 + gt : 57 + (gt < 6 ? gt : 5));
             }
         }
-        for (int g = gt - LAG < 0 ? 0 : gt - LAG; ok && g < gt; g++) ok = finish(g);
     }
 
     tc::tc_fence_before();
@@ -493,6 +476,20 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
 }  // namespace
 
 namespace {
+// lo = x - hi(x) (exact in FP32) of every K and V element, into lo[B][2][S][H][D]: the
+// split pass of the FP32-exact attention (one read and one write of K and V in HBM).
+__global__ void k_attn_split_lo(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstride, int B,
+                                size_t n, float* __restrict__ lo) {
+    const size_t n4 = n / 4, total = (size_t)B * 2 * n4;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t b = i / (2 * n4), r = i - b * 2 * n4, which = r / n4, e = r - which * n4;
+        const float* src = table ? (which ? table[b].v : table[b].k) : (which ? base.v : base.k) + b * bstride;
+        const float4 x = __ldg(reinterpret_cast<const float4*>(src) + e);
+        reinterpret_cast<float4*>(lo + (b * 2 + which) * n)[e] =
+            make_float4(x.x - hi_part(x.x), x.y - hi_part(x.y), x.z - hi_part(x.z), x.w - hi_part(x.w));
+    }
+}
+
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -524,25 +521,43 @@ bool make_qkv_map(CUtensorMap* m, const float* base, size_t B, size_t S, size_t 
 // Q, K, V tensor maps of one attention operand set over [B][S][H][D] (B = 1 for one node of
 // a grouped launch): Q in 128-row boxes, K in 64-row boxes (128-byte swizzle, K-major), V in
 // 64-row boxes (128-byte swizzle of 32-byte atoms, N-major for the PV product).
-extern "C" bool lcu_attention_tc_make_maps(CUtensorMap* maps, const float* q, const float* k, const float* v, size_t B,
-                                           size_t S, size_t H) {
+// lo: the [B][2][S][H][D] lo copies (K then V per operand set) the split pass writes.
+extern "C" bool lcu_attention_tc_make_maps(CUtensorMap* maps, const float* q, const float* k, const float* v,
+                                           const float* lo, size_t B, size_t S, size_t H) {
+    const size_t n = S * H * D;
     return make_qkv_map(maps + 0, q, B, S, H, 0, BQ, CU_TENSOR_MAP_SWIZZLE_128B) &&
            make_qkv_map(maps + 1, k, B, S, H, 0, BKV, CU_TENSOR_MAP_SWIZZLE_128B) &&
-           make_qkv_map(maps + 2, v, B, S, H, 0, BKV, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
+           make_qkv_map(maps + 2, v, B, S, H, 0, BKV, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) &&
+           make_qkv_map(maps + 3, lo, B, S, H, 2 * n, BKV, CU_TENSOR_MAP_SWIZZLE_128B) &&
+           make_qkv_map(maps + 4, lo + n, B, S, H, 2 * n, BKV, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B);
 }
+
+extern "C" size_t lcu_attention_tc_lo_floats(size_t B, size_t S, size_t H) { return 2 * B * S * H * D; }
 
 extern "C" int lcu_attention_tc_supported(size_t D_) { return D_ == (size_t)D; }
 
 extern "C" lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, const float* k, const float* v,
                                           float* o, size_t B, size_t S, size_t H, int causal, int mode,
-                                          const CUtensorMap* d_maps, void* stream) {
+                                          const CUtensorMap* d_maps, float* lo, void* stream) {
     if (B == 0 || S == 0 || H == 0) return LANCIUS_ERROR_OK;
     AttnMaps pm{};
-    if (!d_table && !lcu_attention_tc_make_maps(pm.m, q, k, v, B, S, H)) {
-        lancius_set_error(LANCIUS_ERROR_INTERNAL);
-        return LANCIUS_ERROR_INTERNAL;
+    if (!d_table) {
+        if (!lo && !(lo = static_cast<float*>(lcu_scratch_acquire(lcu_attention_tc_lo_floats(B, S, H) * 4)))) {
+            lancius_set_error(LANCIUS_ERROR_OOM);
+            return LANCIUS_ERROR_OOM;
+        }
+        if (!lcu_attention_tc_make_maps(pm.m, q, k, v, lo, B, S, H)) {
+            lancius_set_error(LANCIUS_ERROR_INTERNAL);
+            return LANCIUS_ERROR_INTERNAL;
+        }
     }
-    if (d_table && !d_maps) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    if (d_table && (!d_maps || !lo)) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    if (mode != LCU_MODE_TF32) {
+        const size_t total4 = 2 * B * S * H * D / 4;
+        k_attn_split_lo<<<lcu_blocks(total4, 256), 256, 0, lcu_as_stream(stream)>>>(d_table, LcuAttnGroup{q, k, v, o},
+                                                                                  S * H * D, (int)B, S * H * D, lo);
+        lcu_note_launch();
+    }
     static bool configured[64] = {};   // the attribute is per device
     int dev_ = 0;
     cudaGetDevice(&dev_);

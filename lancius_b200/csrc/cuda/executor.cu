@@ -45,7 +45,8 @@ struct Step {
     double dscale = 1.0;       // INT8 weight scale
     size_t packed_off = (size_t)-1;   // INT8 MATMUL: K-major copy of the weights in ctx->packed
     size_t wsplit_off = (size_t)-1;   // tensor-core MATMUL on INPUT weights: hi/lo copies in ctx->wsplit
-    int amap_idx = -1;                // tensor-core MATMUL in raw-A mode: first of its maps in ctx->amaps
+    int amap_idx = -1;                // tensor-core MATMUL in raw-A mode / tensor-core ATTENTION: first of its maps in ctx->amaps
+    float* attn_lo = nullptr;         // tensor-core ATTENTION: K/V lo copies ([count][2][S][H][D])
     float eps = 1e-5f;
     uint32_t node_id = 0;      // S_CONV: the conv node (its output)
     uint32_t in_id = 0;        // S_CONV: the input node
@@ -96,6 +97,7 @@ struct lcu_ctx {
     std::vector<WSplit> wsplits;
     float* wsplit = nullptr;
     size_t wsplit_floats = 0;
+    std::vector<float*> attn_lo;        // lo copies of the tensor-core attention steps
     std::vector<CUtensorMap> amaps_host;  // raw-A tensor maps of every step, uploaded to amaps at bind
     CUtensorMap* amaps = nullptr;
     std::vector<uint8_t> nhwc;          // node id -> 1: a conv output stored NHWC (only convs read it)
@@ -122,6 +124,8 @@ static void release_binding(lcu_ctx* c) {
     if (c->wsplit) { cudaFree(c->wsplit); c->wsplit = nullptr; }
     c->wsplits.clear(); c->wsplit_floats = 0;
     if (c->amaps) { cudaFree(c->amaps); c->amaps = nullptr; }
+    for (float* p : c->attn_lo) cudaFree(p);
+    c->attn_lo.clear();
     c->amaps_host.clear();
     c->dmem_bytes = 0; c->staging_elems = 0; c->scratch_bytes = 0;
     c->tc_plans.clear();
@@ -810,9 +814,18 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
             LcuAttnGroup* t = (LcuAttnGroup*)base;
             for (int i = 0; i < st.count; i++) { patch(t[i].q); patch(t[i].k); patch(t[i].v); patch((const float*&)t[i].o); }
             if (lcu_attention_tc_supported(st.D)) {   // Q/K/V tensor maps of every node, read by TMA
-                std::vector<CUtensorMap> maps(3 * st.count);
+                const size_t per_set = lcu_attention_tc_lo_floats(1, st.S, st.H);
+                float* lo = nullptr;
+                if (cudaMalloc(&lo, per_set * st.count * sizeof(float)) != cudaSuccess) {
+                    cudaGetLastError();
+                    release_binding(c);
+                    return fail(LANCIUS_ERROR_OOM);
+                }
+                c->attn_lo.push_back(lo);
+                st.attn_lo = lo;
+                std::vector<CUtensorMap> maps(5 * st.count);
                 for (int i = 0; i < st.count; i++)
-                    if (!lcu_attention_tc_make_maps(&maps[3 * i], t[i].q, t[i].k, t[i].v, 1, st.S, st.H)) {
+                    if (!lcu_attention_tc_make_maps(&maps[5 * i], t[i].q, t[i].k, t[i].v, lo + per_set * i, 1, st.S, st.H)) {
                         release_binding(c);
                         return fail(LANCIUS_ERROR_INTERNAL);
                     }
@@ -1084,7 +1097,7 @@ static lancius_error run_steps(lcu_ctx* c) {
                 if (lcu_attention_tc_supported(s.D) && !lcu_force_simt())
                     e = lcu_attention_tc((const LcuAttnGroup*)(base + s.table_off), nullptr, nullptr, nullptr, nullptr,
                                          (size_t)s.count, s.S, s.H, s.causal, c->mode,
-                                         s.amap_idx >= 0 ? c->amaps + s.amap_idx : nullptr, st);
+                                         s.amap_idx >= 0 ? c->amaps + s.amap_idx : nullptr, s.attn_lo, st);
                 else
                     e = lcu_attention_simt((const LcuAttnGroup*)(base + s.table_off), nullptr, nullptr, nullptr, nullptr,
                                            (size_t)s.count, s.S, s.H, s.D, s.causal, st);

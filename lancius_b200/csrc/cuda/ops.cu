@@ -72,7 +72,7 @@ lancius_error lcu_attention(float* out, const float* q, const float* k, const fl
     if (D != 64 && D != 128) return bad(LANCIUS_ERROR_UNSUPPORTED_OP);
     if ((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15u)) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
     if (lcu_attention_tc_supported(D) && !lcu_force_simt())
-        return lcu_attention_tc(nullptr, q, k, v, out, B, S, H, causal ? 1 : 0, mode, nullptr, stream);
+        return lcu_attention_tc(nullptr, q, k, v, out, B, S, H, causal ? 1 : 0, mode, nullptr, nullptr, stream);
     return lcu_attention_simt(nullptr, q, k, v, out, B, S, H, D, causal ? 1 : 0, stream);
 }
 
