@@ -253,7 +253,7 @@ def run_b200(args, rank, world, local_rank):
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
 
-    mode = L.MODE_TF32 if args.mode == "tf32" else L.MODE_FP32_EXACT
+    mode = {"tf32": L.MODE_TF32, "bf16": L.MODE_BF16}.get(args.mode, L.MODE_FP32_EXACT)
     dev = L.Device(local_rank, mode)
     g = L.Graph()
     built = build(args.config, g, rank, world)
@@ -732,8 +732,9 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--config", default="attention")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--mode", default="fp32_exact", choices=["fp32_exact", "tf32"],
-                    help="contraction precision: 3xTF32 (FP32-exact, default) or one TF32 pass (fast mode)")
+    ap.add_argument("--mode", default="fp32_exact", choices=["fp32_exact", "tf32", "bf16"],
+                    help="contraction precision: 3xTF32 (FP32-exact, default), one TF32 pass, or BF16 GEMMs "
+                         "(conv and attention then run one TF32 pass)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     rank = int(os.environ.get("RANK", 0))
@@ -768,6 +769,8 @@ def main():
     pk = peaks()
     roof = None
     passes = 1 if args.mode == "tf32" else 3
+    if args.mode == "bf16":   # BF16 GEMMs against the BF16 peak; attention runs one TF32 pass
+        passes = 1 if args.config == "attention" else 0.5
     if args.config == "attention":
         achieved = built.bytes / (sec_per_graph) / 1e9
         # traffic: dram__bytes_read.sum + dram__bytes_write.sum of one k_attn_tc launch, from
@@ -802,7 +805,8 @@ def main():
     line = {
         "metric": metric, "value": round(value, 3), "unit": unit, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 5), "higher_is_better": True,
-        "scaling": "strong" if args.config == "encoder_b256" else "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": "strong" if args.config == "encoder_b256" else "weak", "vs_baseline": None,
+        "dtype": {"tf32": "tf32", "bf16": "bf16 (GEMM operands), f32 accumulate"}.get(args.mode, "f32"),
         "data": "synthetic (seeded N(0,1), splitmix64)",
         "config": config_of(args.config, workload),
         "mode": args.mode, "l2": "flushed between timed steps (256 MiB write)",

@@ -6,7 +6,7 @@
  * The three executors keep the reference's names, arguments and host-side memory
  * contract (which node gets which runtime_data pointer), but run the math on a GPU
  * through an implicit per-thread device context (device LANCIUS_CUDA_DEVICE, default
- * 0; LANCIUS_CUDA_MODE=tf32 selects the one-pass TF32 fast mode, default FP32-exact):
+ * 0; LANCIUS_CUDA_MODE=tf32 or bf16 selects a fast mode, default FP32-exact):
  * bound INPUT data is uploaded, the schedule runs on the device, and every node
  * that no other node reads (the graph's outputs) is copied back into its FP64
  * runtime_data before the call returns. LCU_DROPIN_DOWNLOAD_ALL=1 copies back every

@@ -29,8 +29,12 @@ extern "C" {
 /* Contraction precision (GEMM, conv, attention).
  *  FP32_EXACT: 3xTF32 split on tcgen05 (a_hi*b_hi + a_hi*b_lo + a_lo*b_hi), FP32
  *              accumulate; parity bar normwise rel 1e-4 vs the FP64 reference.
- *  TF32:       one tcgen05 kind::tf32 pass; parity bar 2e-2.                  */
-typedef enum { LCU_MODE_FP32_EXACT = 0, LCU_MODE_TF32 = 1 } lcu_mode;
+ *  TF32:       one tcgen05 kind::tf32 pass; parity bar 2e-2.
+ *  BF16:       tensor-core GEMMs (lcu_matmul, graph MATMULs) on BF16 copies of both
+ *              operands (round to nearest even), tcgen05 kind::f16, FP32 accumulate;
+ *              conv and attention run the TF32 pass; parity bar 2e-2. The column-split
+ *              and allocation-free GEMMs take FP32_EXACT and TF32 only.              */
+typedef enum { LCU_MODE_FP32_EXACT = 0, LCU_MODE_TF32 = 1, LCU_MODE_BF16 = 2 } lcu_mode;
 
 /* Epilogue fused into GEMM / conv stores. */
 typedef enum { LCU_EPI_NONE = 0, LCU_EPI_RELU = 1, LCU_EPI_GELU = 2 } lcu_epilogue;

@@ -7,4 +7,4 @@ only binds that library.
 """
 from ._lib import LIB_PATH, load  # noqa: F401
 from .graph import Graph, LanciusError, Node, Schedule  # noqa: F401
-from .runtime import EPI_GELU, EPI_NONE, EPI_RELU, MODE_FP32_EXACT, MODE_TF32, Device  # noqa: F401
+from .runtime import EPI_GELU, EPI_NONE, EPI_RELU, MODE_FP32_EXACT, MODE_TF32, MODE_BF16, Device  # noqa: F401

@@ -82,8 +82,9 @@ lancius_error bind(lancius_schedule* s, bool all) {
         tl.ctx = lcu_create(device_index());
         if (!tl.ctx) return lancius_get_error();
         lcu_set_graph_replay(tl.ctx, 1);
-        const char* m = std::getenv("LANCIUS_CUDA_MODE");   // "tf32": the one-pass fast mode
+        const char* m = std::getenv("LANCIUS_CUDA_MODE");   // "tf32" / "bf16": the fast modes
         if (m && !std::strcmp(m, "tf32")) lcu_set_mode(tl.ctx, LCU_MODE_TF32);
+        if (m && !std::strcmp(m, "bf16")) lcu_set_mode(tl.ctx, LCU_MODE_BF16);
     }
     if (tl.all == (int)all && key == tl.key) {
         lcu_ctx_retarget_schedule(tl.ctx, s);

@@ -168,7 +168,7 @@ void lcu_destroy(lcu_ctx* c) {
 
 lancius_error lcu_set_mode(lcu_ctx* c, lcu_mode mode) {
     if (!c) return fail(LANCIUS_ERROR_NULL_PTR);
-    if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32) return fail(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+    if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32 && mode != LCU_MODE_BF16) return fail(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
     if (c->mode != (int)mode && c->exec) { cudaGraphExecDestroy(c->exec); c->exec = nullptr; }
     c->mode = mode;
     return LANCIUS_ERROR_OK;
@@ -1072,17 +1072,17 @@ static lancius_error run_steps(lcu_ctx* c) {
             case S_GEMM:
                 if (s.tc) {
                     LcuTcGemmPlan& p = c->tc_plans[s.plan_idx];
-                    int passes = c->mode == LCU_MODE_TF32 ? 1 : 3;
+                    int passes = lcu_gemm_passes(c->mode);
                     if (p.passes != passes || p.M != s.M) {
                         e = lcu_gemm_tc_prepare(&p, c->scratch, s.M, s.N, s.K, s.count, s.ga, s.gb, passes);
                         if (e != LANCIUS_ERROR_OK) break;
-                        if (s.wsplit_off != NPOS) {
+                        if (s.wsplit_off != NPOS && passes > 0) {
                             const size_t mat = s.K * ((s.N + 3) & ~size_t(3));
                             float* hi = c->wsplit + s.wsplit_off;
                             e = lcu_gemm_tc_use_presplit_b(&p, hi, hi + s.gb * mat);
                             if (e != LANCIUS_ERROR_OK) break;
                         }
-                        if (s.amap_idx >= 0 && (e = lcu_gemm_tc_use_raw_a(&p, c->amaps + s.amap_idx)) != LANCIUS_ERROR_OK) break;
+                        if (s.amap_idx >= 0 && passes > 0 && (e = lcu_gemm_tc_use_raw_a(&p, c->amaps + s.amap_idx)) != LANCIUS_ERROR_OK) break;
                     }
                     e = lcu_gemm_tc_run(&p, (const LcuGemmGroup*)(base + s.table_off), s.epi, st);
                 } else {
@@ -1096,7 +1096,7 @@ static lancius_error run_steps(lcu_ctx* c) {
             case S_ATTN:
                 if (lcu_attention_tc_supported(s.D) && !lcu_force_simt())
                     e = lcu_attention_tc((const LcuAttnGroup*)(base + s.table_off), nullptr, nullptr, nullptr, nullptr,
-                                         (size_t)s.count, s.S, s.H, s.causal, c->mode,
+                                         (size_t)s.count, s.S, s.H, s.causal, lcu_contraction_mode(c->mode),
                                          s.amap_idx >= 0 ? c->amaps + s.amap_idx : nullptr, s.attn_lo, st);
                 else
                     e = lcu_attention_simt((const LcuAttnGroup*)(base + s.table_off), nullptr, nullptr, nullptr, nullptr,
@@ -1118,13 +1118,13 @@ static lancius_error run_steps(lcu_ctx* c) {
                     const LcuConvShape cs{(int)s.cn, (int)s.ci, (int)s.h, (int)s.w, (int)s.co, (int)s.kh, (int)s.kw,
                                           (int)s.stride, (int)s.pad, (int)ho, (int)wo};
                     if (lcu_conv_nhwc_supported(cs) && !lcu_conv_force_im2col()) {
-                        e = lcu_conv2d_tc_nhwc_ex(F(s.out), F(s.in0), F(s.in1), cs, s.relu, c->mode, c->scratch, st,
+                        e = lcu_conv2d_tc_nhwc_ex(F(s.out), F(s.in0), F(s.in1), cs, s.relu, lcu_contraction_mode(c->mode), c->scratch, st,
                                                   s.in_nhwc, s.out_nhwc, s.in_lo != NPOS ? c->lo_buf + s.in_lo : nullptr,
                                                   s.out_lo != NPOS ? c->lo_buf + s.out_lo : nullptr);
                         break;
                     }
                     LcuTcGemmPlan& p = c->tc_plans[s.plan_idx];
-                    int passes = c->mode == LCU_MODE_TF32 ? 1 : 3;
+                    int passes = lcu_gemm_passes(lcu_contraction_mode(c->mode));
                     if (p.passes != passes || p.M != s.M) {
                         e = lcu_gemm_tc_prepare(&p, c->scratch, s.M, s.N, s.K, 1, 1, 1, passes);
                         if (e != LANCIUS_ERROR_OK) break;
@@ -1140,7 +1140,7 @@ static lancius_error run_steps(lcu_ctx* c) {
                                              s.pad, s.relu, 1, st, s.out_lo != NPOS ? c->lo_buf + s.out_lo : nullptr);
                 else
                     e = lcu_conv2d(F(s.out), F(s.in0), F(s.in1), s.cn, s.ci, s.h, s.w, s.co, s.kh, s.kw, s.stride, s.pad,
-                                   s.relu, c->mode, st);
+                                   s.relu, lcu_contraction_mode(c->mode), st);
                 break;
             case S_MAXPOOL: e = lcu_maxpool2d(F(s.out), F(s.in0), s.cn, s.ci, s.h, s.w, s.kh, s.stride, st); break;
             case S_MISC: e = run_misc(s, base, c->scratch, c->packed, st); break;

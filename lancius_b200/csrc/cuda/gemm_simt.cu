@@ -26,13 +26,18 @@ constexpr int SK_TM = 16, SK_TN = 32, SK_WARPS = 8, SK_KC = 128;
 // shared with cp.async (4-byte copies, zero-filled past the matrix edge) SK_STAGES - 1
 // chunks ahead, so a small product pays about one memory latency instead of one per chunk.
 constexpr int SK_STAGES = 6;
-constexpr int SK_A_FLOATS = SK_TM * (SK_KC + 1), SK_B_FLOATS = SK_KC * SK_TN;
+constexpr int SK_AP = SK_KC + 4;                 // A row pitch in floats (16-byte rows for cp.async)
+constexpr int SK_A_FLOATS = SK_TM * SK_AP, SK_B_FLOATS = SK_KC * SK_TN;
 constexpr int SK_SMEM_BYTES = SK_STAGES * (SK_A_FLOATS + SK_B_FLOATS) * 4 + SK_WARPS * SK_TM * (SK_TN + 1) * 4;
 
 // `src` must be a valid address even when !valid (nothing is read then; the word is zeroed)
 __device__ __forceinline__ void cp_async4(float* dst, const float* src, bool valid) {
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
                  "l"(src), "r"(valid ? 4 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async16(float* dst, const float* src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)),
+                 "l"(src), "r"(valid ? 16 : 0) : "memory");
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N>
@@ -48,15 +53,33 @@ __device__ __forceinline__ void skinny_tile(const LcuGemmGroup& gr, size_t M, si
     float* part = Bs0 + SK_STAGES * SK_B_FLOATS;                   // [warp][16][33]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int chunks = (int)((K + SK_KC - 1) / SK_KC);
+    // 16-byte copies when every row starts 16-byte aligned (a float4 is then wholly inside
+    // or wholly outside the matrix), else 4-byte ones
+    const bool vec = K % 4 == 0 && N % 4 == 0 && ((reinterpret_cast<uintptr_t>(gr.a) | reinterpret_cast<uintptr_t>(gr.b)) & 15) == 0;
     auto load = [&](int kc) {                                      // chunk kc -> stage kc % SK_STAGES
         const size_t k0 = (size_t)kc * SK_KC;
         float* As = As0 + (kc % SK_STAGES) * SK_A_FLOATS;
         float* Bs = Bs0 + (kc % SK_STAGES) * SK_B_FLOATS;
+        if (vec) {
+#pragma unroll
+            for (int r = 0; r < SK_TM * SK_KC / 4 / 256; r++) {   // A: 16 rows x 32 float4
+                const int idx = threadIdx.x + 256 * r, i = idx / (SK_KC / 4), kk = 4 * (idx % (SK_KC / 4));
+                const bool v = m0 + i < M && k0 + kk < K;
+                cp_async16(As + i * SK_AP + kk, v ? gr.a + (m0 + i) * K + k0 + kk : gr.a, v);
+            }
+#pragma unroll
+            for (int r = 0; r < SK_KC * SK_TN / 4 / 256; r++) {   // B: 128 k x 8 float4
+                const int idx = threadIdx.x + 256 * r, kk = idx / (SK_TN / 4), j = 4 * (idx % (SK_TN / 4));
+                const bool v = k0 + kk < K && n0 + j < N;
+                cp_async16(Bs + kk * SK_TN + j, v ? gr.b + (k0 + kk) * N + n0 + j : gr.b, v);
+            }
+            return;
+        }
 #pragma unroll
         for (int r = 0; r < SK_TM * SK_KC / 256; r++) {           // A: 16 rows x 128 k, coalesced along k
             const int idx = threadIdx.x + 256 * r, i = idx / SK_KC, kk = idx % SK_KC;
             const bool v = m0 + i < M && k0 + kk < K;
-            cp_async4(As + i * (SK_KC + 1) + kk, v ? gr.a + (m0 + i) * K + k0 + kk : gr.a, v);
+            cp_async4(As + i * SK_AP + kk, v ? gr.a + (m0 + i) * K + k0 + kk : gr.a, v);
         }
 #pragma unroll
         for (int r = 0; r < SK_KC * SK_TN / 256; r++) {           // B: 128 k x 32 n, coalesced along n
@@ -84,7 +107,7 @@ __device__ __forceinline__ void skinny_tile(const LcuGemmGroup& gr, size_t M, si
         for (int kk = warp * (SK_KC / SK_WARPS); kk < (warp + 1) * (SK_KC / SK_WARPS); kk++) {
             const float b = Bs[kk * SK_TN + lane];
 #pragma unroll
-            for (int i = 0; i < SK_TM; i++) acc[i] = fmaf(As[i * (SK_KC + 1) + kk], b, acc[i]);
+            for (int i = 0; i < SK_TM; i++) acc[i] = fmaf(As[i * SK_AP + kk], b, acc[i]);
         }
     }
     cp_async_wait<0>();
@@ -142,6 +165,14 @@ __global__ void __launch_bounds__(256) k_mlp2(const LcuGemmGroup* __restrict__ l
                                               unsigned* __restrict__ tickets) {
     __shared__ unsigned last;
     const size_t m0 = (size_t)blockIdx.y * SK_TM;
+    {   // the second product's weights and bias into L2 now, for whichever CTA finishes last
+        const LcuGemmGroup g2 = *l2;
+        const size_t lines = (N1 * N2 * 4 + 127) / 128, nb = (size_t)gridDim.x * gridDim.y;
+        const size_t cta = blockIdx.x + (size_t)gridDim.x * blockIdx.y;
+        for (size_t i = cta * blockDim.x + threadIdx.x; i < lines; i += nb * blockDim.x)
+            asm volatile("prefetch.global.L2 [%0];" ::"l"(reinterpret_cast<const char*>(g2.b) + 128 * i));
+        if (g2.bias && cta == 0 && threadIdx.x == 0) asm volatile("prefetch.global.L2 [%0];" ::"l"(g2.bias));
+    }
     skinny_tile(*l1, M, N1, K1, epi1, m0, (size_t)blockIdx.x * SK_TN);
     __threadfence();                     // this CTA's H tile is visible device-wide before its ticket
     __syncthreads();

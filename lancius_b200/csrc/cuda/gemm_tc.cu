@@ -18,6 +18,7 @@
 // Every mbarrier wait is bounded (tc::kSpinLimit); a timeout sets the watchdog
 // word, unwinds the CTA and frees its TMEM.
 #include "tc_common.cuh"
+#include <cuda_bf16.h>
 #include <cstdio>
 #ifndef LCU_GEMM_DEBUG
 #define LCU_GEMM_DEBUG 0
@@ -87,7 +88,11 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
     const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
     const int k_begin = split * kchunk;
     const int k_end = min(K, k_begin + kchunk);
-    const int KT = (k_end - k_begin + BK - 1) / BK;
+    // passes == 0: BF16 operands (kind::f16, K = 16 per MMA): a stage holds 32 k of them in
+    // the same 64-byte rows that hold 16 k of TF32
+    const bool bf = passes == 0;
+    const int KSTEP = bf ? 2 * BK : BK;
+    const int KT = (k_end - k_begin + KSTEP - 1) / KSTEP;
     volatile int* abort = &sm->abort;
     if (threadIdx.x == 0) GTRACE(0);
 
@@ -117,7 +122,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
         // ---------------- TMA producer ----------------
         // raw-A mode: only the FP32 A tile arrives; the epilogue warps split it into hi/lo in place
         const uint32_t tx = a_maps ? (passes > 1 ? A_TILE + 2 * B_TILE : A_TILE + B_TILE)
-                                   : (passes > 1 ? STAGE_BYTES : A_TILE + B_TILE);
+                                   : (passes > 1 ? STAGE_BYTES : A_TILE + B_TILE);   // BF16: A_TILE + B_TILE too
         const int ga = groups[g].aidx, gb = groups[g].bidx;      // scratch slots of this group's operands
         const CUtensorMap* ma = a_maps ? a_maps + ga : &ta_hi;
         for (int kt = 0; kt < KT; kt++) {
@@ -125,11 +130,14 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
             if (kt >= STAGES && !tc::mbar_wait(&sm->empty[s], ((kt / STAGES) - 1) & 1, abort, &g_gemm_watchdog, 1)) break;
             uint8_t* st = tiles + s * STAGE_BYTES;
             tc::mbar_expect_tx(&sm->full[s], tx);
-            int k0 = k_begin + kt * BK;
+            int k0 = k_begin + kt * KSTEP;
             tc::tma_load_3d(st, ma, &sm->full[s], k0, m0, a_maps ? 0 : ga);               // A: two 128-row boxes
             tc::tma_load_3d(st + A_TILE / 2, ma, &sm->full[s], k0, m0 + 128, a_maps ? 0 : ga);
-            for (int j = 0; j < BN / 32; j++)
-                tc::tma_load_3d(st + 2 * A_TILE + j * B_CHUNK, &tb_hi, &sm->full[s], n0 + 32 * j, k0, gb);
+            if (bf)   // B^T, K-major like A: one box of 256 rows of 32 k
+                tc::tma_load_3d(st + 2 * A_TILE, &tb_hi, &sm->full[s], k0, n0, gb);
+            else
+                for (int j = 0; j < BN / 32; j++)
+                    tc::tma_load_3d(st + 2 * A_TILE + j * B_CHUNK, &tb_hi, &sm->full[s], n0 + 32 * j, k0, gb);
             if (passes > 1) {
                 if (!a_maps) {
                     tc::tma_load_3d(st + A_TILE, &ta_lo, &sm->full[s], k0, m0, ga);
@@ -160,8 +168,18 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
             }
             uint32_t st = tc::smem_u32(tiles + s * STAGE_BYTES);
             uint32_t a_hi = st, a_lo = st + A_TILE, b_hi = st + 2 * A_TILE, b_lo = st + 2 * A_TILE + B_TILE;
+            if (bf) {
+                constexpr uint32_t idb = tc::idesc_bf16(128, BN);
+                const uint32_t hoff = (uint32_t)half * (128 * BK * 4), d = tmem + (uint32_t)half * BN;
 #pragma unroll
-            for (int kb = 0; kb < BK / 8; kb++) {
+                for (int kb = 0; kb < 2; kb++) {             // 16 k (32 bytes) per MMA
+                    const uint64_t da = tc::smem_desc(a_hi + hoff + kb * 32, 16, 512, tc::SWZ_64B);
+                    const uint64_t db = tc::smem_desc(b_hi + kb * 32, 16, 512, tc::SWZ_64B);
+                    tc::mma_bf16(d, da, db, idb, (kt | kb) ? 1u : 0u);
+                }
+            }
+#pragma unroll
+            for (int kb = 0; kb < BK / 8 && !bf; kb++) {
                 uint64_t dbh = tc::smem_desc(b_hi + kb * 1024, B_CHUNK, 512, tc::SWZ_128B_BASE32B);
                 uint64_t dbl = tc::smem_desc(b_lo + kb * 1024, B_CHUNK, 512, tc::SWZ_128B_BASE32B);
                 {                                            // rows 0-127 and 128-255 share the B tile
@@ -387,6 +405,36 @@ __global__ void k_split(const LcuGemmGroup* __restrict__ groups, int which, size
     split_rows(which == 0 ? gr.a : gr.b, rows, cols, pitch, hi + base, lo ? lo + base : nullptr);
 }
 
+// BF16 (round to nearest even) copies of the GEMM operands: A row-major into [M][pitch],
+// B [K][N] transposed into [N][pitch] (K-major, as the kernel reads both). Zero padding.
+__global__ void k_to_bf16_a(const LcuGemmGroup* __restrict__ groups, size_t M, size_t K, size_t pitch,
+                            __nv_bfloat16* __restrict__ dst) {
+    const LcuGemmGroup& gr = groups[blockIdx.y];
+    if (gr.adup) return;
+    __nv_bfloat16* out = dst + (size_t)gr.aidx * M * pitch;
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < M * pitch; i += (size_t)gridDim.x * blockDim.x) {
+        const size_t r = i / pitch, c = i - r * pitch;
+        out[i] = __float2bfloat16_rn(c < K ? gr.a[r * K + c] : 0.f);
+    }
+}
+__global__ void k_to_bf16_bt(const LcuGemmGroup* __restrict__ groups, size_t K, size_t N, size_t pitch,
+                             __nv_bfloat16* __restrict__ dst) {
+    __shared__ float t[32][33];
+    const LcuGemmGroup& gr = groups[blockIdx.z];
+    if (gr.bdup) return;
+    __nv_bfloat16* out = dst + (size_t)gr.bidx * N * pitch;
+    const size_t k0 = (size_t)blockIdx.y * 32, n0 = (size_t)blockIdx.x * 32;
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const size_t k = k0 + r, n = n0 + threadIdx.x;
+        t[r][threadIdx.x] = (k < K && n < N) ? gr.b[k * N + n] : 0.f;
+    }
+    __syncthreads();
+    for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+        const size_t n = n0 + r, k = k0 + threadIdx.x;
+        if (n < N && k < pitch) out[n * pitch + k] = __float2bfloat16_rn(t[threadIdx.x][r]);
+    }
+}
+
 __global__ void k_split_one(const float* __restrict__ src, size_t rows, size_t cols, size_t pitch, float* __restrict__ hi,
                             float* __restrict__ lo) {
     split_rows(src, rows, cols, pitch, hi, lo);
@@ -472,6 +520,20 @@ bool make_map(CUtensorMap* m, const float* base, size_t inner, size_t rows, size
 }
 
 size_t pad4(size_t v) { return (v + 3) & ~size_t(3); }
+
+// 3D map over [G][rows][pitch] BF16, box {32 k (64 bytes), box_rows}, 64-byte swizzle (K-major)
+bool make_map_bf16(CUtensorMap* m, const void* base, size_t inner, size_t rows, size_t groups, size_t pitch,
+                   uint32_t box_rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return false;
+    cuuint64_t dims[3] = {inner, rows, groups};
+    cuuint64_t strides[2] = {pitch * 2, rows * pitch * 2};
+    cuuint32_t box[3] = {32, box_rows, 1};
+    cuuint32_t es[3] = {1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
 size_t al256(size_t v) { return (v + 255) & ~size_t(255); }
 
 }  // namespace
@@ -488,6 +550,11 @@ constexpr int kMaxChunk = 8192;
 int split_count(size_t K) { return K > (size_t)kMaxChunk ? (int)((K + kMaxChunk - 1) / kMaxChunk) : 1; }
 
 extern "C" size_t lcu_gemm_tc_scratch_bytes(size_t M, size_t N, size_t K, int G, int Ga, int Gb, int passes) {
+    if (passes == 0) {   // BF16: A [Ga][M][pad8(K)] and B^T [Gb][N][pad8(K)]
+        const size_t kp = (K + 7) & ~size_t(7);
+        int sp = split_count(K);
+        return al256((size_t)Ga * M * kp * 2) + al256((size_t)Gb * N * kp * 2) + (sp > 1 ? al256((size_t)G * sp * M * N * 4) : 0);
+    }
     size_t a = al256((size_t)Ga * M * pad4(K) * 4), b = al256((size_t)Gb * K * pad4(N) * 4);
     int sp = split_count(K);
     size_t part = sp > 1 ? al256((size_t)G * sp * M * N * 4) : 0;
@@ -500,6 +567,20 @@ extern "C" lancius_error lcu_gemm_tc_prepare(LcuTcGemmPlan* p, void* scratch, si
     p->conv = LcuConvShape{};
     p->b_presplit = 0;
     p->d_amaps = nullptr;
+    if (passes == 0) {   // BF16 operands, both K-major: A [Ga][M][Kp], B^T [Gb][N][Kp]
+        p->Kp = (K + 7) & ~size_t(7);
+        char* s = static_cast<char*>(scratch);
+        p->s_ahi = (float*)s; s += al256((size_t)Ga * M * p->Kp * 2);
+        p->s_bhi = (float*)s; s += al256((size_t)Gb * N * p->Kp * 2);
+        p->s_alo = p->s_blo = nullptr;
+        p->splits = split_count(K);
+        p->kchunk = p->splits > 1 ? (int)(((K + p->splits - 1) / p->splits + 2 * BK - 1) / (2 * BK) * (2 * BK)) : (int)(K ? K : 1);
+        p->partial = p->splits > 1 ? (float*)s : nullptr;
+        bool ok = make_map_bf16(&p->a_hi, p->s_ahi, K, M, Ga, p->Kp, 128) && make_map_bf16(&p->b_hi, p->s_bhi, K, N, Gb, p->Kp, BN);
+        if (!ok) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+        p->a_lo = p->a_hi; p->b_lo = p->b_hi;
+        return LANCIUS_ERROR_OK;
+    }
     size_t a = al256((size_t)Ga * M * p->Kp * 4), b = al256((size_t)Gb * K * p->Np * 4);
     char* s = static_cast<char*>(scratch);
     p->s_ahi = (float*)s; s += a;
@@ -574,7 +655,15 @@ extern "C" lancius_error lcu_gemm_tc_run_dst(const LcuTcGemmPlan* p, const LcuGe
     cudaStream_t st = lcu_as_stream(stream);
     float* lo_a = p->passes > 1 ? p->s_alo : nullptr;
     float* lo_b = p->passes > 1 ? p->s_blo : nullptr;
-    if (p->K > 0) {
+    if (p->K > 0 && p->passes == 0) {
+        __nv_bfloat16* a16 = reinterpret_cast<__nv_bfloat16*>(p->s_ahi);
+        __nv_bfloat16* b16 = reinterpret_cast<__nv_bfloat16*>(p->s_bhi);
+        k_to_bf16_a<<<dim3(lcu_blocks(p->M * p->Kp, 256), p->G), 256, 0, st>>>(d_groups, p->M, p->K, p->Kp, a16);
+        k_to_bf16_bt<<<dim3((unsigned)((p->N + 31) / 32), (unsigned)((p->Kp + 31) / 32), p->G), dim3(32, 8), 0, st>>>(
+            d_groups, p->K, p->N, p->Kp, b16);
+        lcu_note_launch();
+        lcu_note_launch();
+    } else if (p->K > 0) {
         if (!p->d_amaps) {
             k_split<<<dim3((unsigned)(p->M < 65535 ? p->M : 65535), p->G), 256, 0, st>>>(d_groups, 0, p->M, p->K, p->Kp, p->s_ahi, lo_a);
             lcu_note_launch();
@@ -647,7 +736,7 @@ extern "C" void* lcu_scratch_acquire_decode(size_t bytes) { return acquire_from(
 
 extern "C" lancius_error lcu_gemm_tc(float* c, const float* a, const float* b, size_t M, size_t K, size_t N,
                                      const float* bias, int epi, int mode, void* stream) {
-    int passes = mode == LCU_MODE_TF32 ? 1 : 3;
+    int passes = lcu_gemm_passes(mode);
     size_t need = lcu_gemm_tc_scratch_bytes(M, N, K, 1, 1, 1, passes) + 256;
     char* scratch = static_cast<char*>(lcu_scratch_acquire(need));
     if (!scratch) { lancius_set_error(LANCIUS_ERROR_OOM); return LANCIUS_ERROR_OOM; }
@@ -670,7 +759,7 @@ extern "C" lancius_error lcu_gemm_tc(float* c, const float* a, const float* b, s
 // stored straight into NCHW by the epilogue (ReLU fused). Scratch from the per-device cache.
 extern "C" lancius_error lcu_conv2d_tc(float* out, const float* in, const float* w, LcuConvShape cs, int relu, int mode,
                                        void* stream) {
-    const int passes = mode == LCU_MODE_TF32 ? 1 : 3;
+    const int passes = lcu_gemm_passes(lcu_contraction_mode(mode));
     const size_t M = cs.co, K = (size_t)cs.ci * cs.kh * cs.kw, N = (size_t)cs.n * cs.ho * cs.wo;
     const size_t need = lcu_gemm_tc_scratch_bytes(M, N, K, 1, 1, 1, passes) + 256;
     char* scratch = static_cast<char*>(lcu_scratch_acquire(need));

@@ -5,6 +5,11 @@
 #include "common.cuh"
 #include <cuda.h>
 
+// tensor-core GEMM passes of a precision mode: 3 (3xTF32), 1 (TF32), 0 (BF16 operands)
+static inline int lcu_gemm_passes(int mode) { return mode == LCU_MODE_BF16 ? 0 : mode == LCU_MODE_TF32 ? 1 : 3; }
+// conv and attention have no BF16 form: the BF16 mode runs them as one TF32 pass
+static inline int lcu_contraction_mode(int mode) { return mode == LCU_MODE_BF16 ? (int)LCU_MODE_TF32 : mode; }
+
 struct LcuGemmGroup {        // one independent product C = act(A*B + bias) + resid
     const float* a;
     const float* b;

@@ -58,7 +58,7 @@ lancius_error lcu_matmul(float* out, const float* a, const float* b, size_t M, s
                          int epilogue, int mode, void* stream) {
     if (!out || (K && (!a || !b))) return bad(LANCIUS_ERROR_NULL_PTR);
     if (epilogue < LCU_EPI_NONE || epilogue > LCU_EPI_GELU) return bad(LANCIUS_ERROR_UNSUPPORTED_OP);
-    if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+    if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32 && mode != LCU_MODE_BF16) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
     if (M == 0 || N == 0) return LANCIUS_ERROR_OK;
     // K == 0 is valid: the product is zero, bias and epilogue still apply
     if (lcu_use_tensor_cores(M, N, K)) return lcu_gemm_tc(out, a, b, M, K, N, bias, epilogue, mode, stream);
@@ -68,11 +68,12 @@ lancius_error lcu_matmul(float* out, const float* a, const float* b, size_t M, s
 lancius_error lcu_attention(float* out, const float* q, const float* k, const float* v, size_t B, size_t S, size_t H,
                             size_t D, int causal, int mode, void* stream) {
     if (!out || !q || !k || !v) return bad(LANCIUS_ERROR_NULL_PTR);
-    if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+    if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32 && mode != LCU_MODE_BF16) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
     if (D != 64 && D != 128) return bad(LANCIUS_ERROR_UNSUPPORTED_OP);
     if ((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) & 15u)) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
     if (lcu_attention_tc_supported(D) && !lcu_force_simt())
-        return lcu_attention_tc(nullptr, q, k, v, out, B, S, H, causal ? 1 : 0, mode, nullptr, nullptr, stream);
+        return lcu_attention_tc(nullptr, q, k, v, out, B, S, H, causal ? 1 : 0, lcu_contraction_mode(mode), nullptr,
+                                nullptr, stream);
     return lcu_attention_simt(nullptr, q, k, v, out, B, S, H, D, causal ? 1 : 0, stream);
 }
 
@@ -80,9 +81,10 @@ lancius_error lcu_conv2d(float* out, const float* in, const float* w, size_t N, 
                          size_t C_out, size_t K_h, size_t K_w, size_t stride, size_t pad, int relu, int mode,
                          void* stream) {
     if (!out || !in || !w) return bad(LANCIUS_ERROR_NULL_PTR);
-    if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
+    if (mode != LCU_MODE_FP32_EXACT && mode != LCU_MODE_TF32 && mode != LCU_MODE_BF16) return bad(LANCIUS_ERROR_UNSUPPORTED_DTYPE);
     if (stride == 0 || H_in + 2 * pad < K_h || W_in + 2 * pad < K_w) return bad(LANCIUS_ERROR_SHAPE_MISMATCH);
     size_t Ho = (H_in + 2 * pad - K_h) / stride + 1, Wo = (W_in + 2 * pad - K_w) / stride + 1;
+    mode = lcu_contraction_mode(mode);   // no BF16 conv: one TF32 pass
     if (lcu_conv_smallk_supported(C_in, K_h, K_w, C_out) && !lcu_force_tc_conv())
         return lcu_conv2d_smallk(out, in, w, N, C_in, H_in, W_in, C_out, K_h, K_w, stride, pad, relu, stream);
     if (N && C_in && lcu_use_tensor_cores(C_out, N * Ho * Wo, C_in * K_h * K_w)) {

@@ -11,7 +11,7 @@ from . import _abi
 from ._lib import load
 from .graph import LanciusError
 
-MODE_FP32_EXACT, MODE_TF32 = 0, 1
+MODE_FP32_EXACT, MODE_TF32, MODE_BF16 = 0, 1, 2
 EPI_NONE, EPI_RELU, EPI_GELU = 0, 1, 2
 
 

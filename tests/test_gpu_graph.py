@@ -87,6 +87,20 @@ def test_encoder_reduced(device, orc):
         assert_close(y, r, 1e-4, k=3072)
 
 
+@pytest.mark.parametrize("mode", ["tf32", "bf16"])
+def test_encoder_fast_modes(orc, mode):
+    """The encoder graph in the fast modes (normwise 2e-2): BF16 GEMMs with TF32 attention,
+    or everything in one TF32 pass."""
+    d = L.Device(0, L.MODE_TF32 if mode == "tf32" else L.MODE_BF16)
+    try:
+        b = configs.encoder(L.Graph(), batch=2, seq=128, layers=2)
+        ys, _ = run_gpu(d, b)
+        for y, r in zip(ys, oracle_outputs(orc, b)):
+            assert_close(y, r, 2e-2)
+    finally:
+        d.close()
+
+
 def test_caller_plan_path(device, orc):
     """A caller-supplied lancius_memory_plan (the reference contract) is validated and used
     as-is: no fusion, every node in its planned slot."""

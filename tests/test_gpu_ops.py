@@ -104,6 +104,22 @@ def test_attention(lib, orc, B, S, H, D, causal):
     assert_close(y, ref, 1e-4)
 
 
+@pytest.mark.parametrize("M,K,N", [(512, 768, 3072), (2048, 2048, 2048), (300, 1000, 260), (4096, 16384, 256)])
+def test_matmul_bf16_mode(lib, orc, M, K, N):
+    """BF16 fast mode: both operands rounded to BF16, tcgen05 kind::f16, FP32 accumulate
+    (normwise 2e-2); odd K and N exercise the zero padding of the K-major BF16 copies,
+    K = 16384 the split-K reduction."""
+    from lancius_b200 import MODE_BF16
+    a = data.uniform(8, (M, K), -1, 1)
+    b = data.uniform(9, (K, N), -1, 1)
+    bias = data.normal(10, (N,))
+    ref = np.maximum(orc.matmul(a, b) + bias, 0)
+    out = torch.empty((M, N), device="cuda")
+    run(lib.lcu_matmul(P(out), P(dev(a)), P(dev(b)), M, K, N, P(dev(bias)), EPI_RELU, MODE_BF16, None))
+    err = assert_close(out.cpu().numpy(), ref, 2e-2)
+    assert err > 1e-5          # BF16 operands really were used
+
+
 @pytest.mark.parametrize("B,S,H,causal", [(8, 512, 8, 1), (2, 512, 12, 0), (1, 300, 3, 1)])
 def test_attention_tf32_mode(lib, orc, B, S, H, causal):
     """The one-pass TF32 fast mode of the tensor-core attention (normwise 2e-2)."""
