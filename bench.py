@@ -25,6 +25,14 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 L2_FLUSH_BYTES = 256 << 20     # > 126 MB L2: written between timed steps
+L2_NOTE = "flushed between timed steps (256 MiB write, then read back: no dirty lines left)"
+
+
+def flush_l2(buf):
+    """Evict L2 between timed steps: write a buffer twice its size, then read it back, so
+    the lines left behind are clean and the next step pays no write-back of this buffer."""
+    buf.fill_(1.0)
+    buf.sum()
 
 
 def peaks():
@@ -268,7 +276,7 @@ def run_b200(args, rank, world, local_rank):
 
     def step_device(ev0, ev1):
         with torch.cuda.stream(ext):
-            flush.fill_(1.0)                 # evict L2 between timed steps
+            flush_l2(flush)                 # evict L2 between timed steps
             ev0.record(ext)
         dev.execute(sched)
         with torch.cuda.stream(ext):
@@ -446,7 +454,7 @@ def run_colsplit(args, rank, world, local_rank, n):
     clocks = Clocks(local_rank)
     clocks.start()
     for _ in range(args.steps):
-        flush.fill_(1.0)
+        flush_l2(flush)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(); step(); e1.record()
         evs.append((e0, e1))
@@ -482,7 +490,7 @@ def run_colsplit(args, rank, world, local_rank, n):
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded U[-1,1), splitmix64)",
             "config": config_of(f"gemm{n}", metric_names(f"gemm{n}")[2]), "mode": "fp32_exact",
             "exchange": "ncclAllGather + repack" if nccl_path else "fused: epilogue stores to peer C over NVLink",
-            "l2": "flushed between timed steps (256 MiB write)", "parallelism": f"column-split x{world}",
+            "l2": L2_NOTE, "parallelism": f"column-split x{world}",
             "roofline": {"bound": "tensor", "achieved": round(val / world, 2), "peak": pk["bf16_tflops"],
                          "unit": "TFLOP/s per GPU", "frac": round(val / world / pk["bf16_tflops"], 4), "traffic": None,
                          "peak_src": pk["src"] + " bf16 (3xTF32 issues 3 TF32 MMAs per product)"},
@@ -550,7 +558,7 @@ def run_decode(args, rank, world, local_rank):
         rc = lib.lcu_attention_kv_cache_batched(ptr(out), ptr(q), ptr(kc), ptr(vc), B, S, H, D, sp)
         assert rc == 0, rc
     for _ in range(args.warmup):
-        flush.fill_(1.0); step()
+        flush_l2(flush); step()
     torch.cuda.synchronize()
     if dist:
         dist.barrier()
@@ -558,7 +566,7 @@ def run_decode(args, rank, world, local_rank):
     clocks.start()
     evs = []
     for _ in range(args.steps):
-        flush.fill_(1.0)
+        flush_l2(flush)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(); step(); e1.record()
         evs.append((e0, e1))
@@ -608,7 +616,7 @@ def run_decode(args, rank, world, local_rank):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (N(0,1) caches, seeded)",
             "config": {"workload": f"kv_cache_decode_b{B}_s{S}_h{H}_d{D}_fp32", "per_gpu_batch": B},
-            "mode": "fp32", "l2": "flushed between timed steps (256 MiB write); caches 2.1 GB > L2",
+            "mode": "fp32", "l2": L2_NOTE + "; caches 2.1 GB > L2",
             "parallelism": f"batch-sharded x{world}",
             "roofline": {"bound": "hbm", "achieved": round(bytes_ / sec / 1e9, 1), "peak": pk["hbm_gbs"],
                          "unit": "GB/s", "frac": round(bytes_ / sec / 1e9 / pk["hbm_gbs"], 4), "traffic": None,
@@ -653,7 +661,7 @@ def run_int8_gemm(args, rank, world, local_rank, n):
 
     def step(e0=None, e1=None):
         with torch.cuda.stream(ext):
-            flush.fill_(1.0)
+            flush_l2(flush)
             if e0: e0.record(ext)
         dev.execute(sched)
         if e1:
@@ -704,7 +712,7 @@ def run_int8_gemm(args, rank, world, local_rank, n):
             "scaling": "weak", "vs_baseline": None, "dtype": "s8 x s8 -> s32",
             "data": "synthetic (A ~ U[-1,1), int8 weights ~ U[-127,127], seeded)",
             "config": {"workload": f"int8_weight_matmul{n}", "mode": "dynamic per-tensor INT8 (reference semantics)",
-                       "l2": "flushed between timed steps (256 MiB write)", "parallelism": f"replicas x{world}"},
+                       "l2": L2_NOTE, "parallelism": f"replicas x{world}"},
             "roofline": {"bound": "tensor", "achieved": round(ops / sec / 1e12, 2), "peak": pk["bf16_tflops"] * 2,
                          "unit": "TOPS", "frac": round(ops / sec / 1e12 / (pk["bf16_tflops"] * 2), 4), "traffic": None,
                          "peak_src": pk["src"] + " bf16 x 2 (INT8 dense rate is twice BF16)"},
@@ -809,7 +817,7 @@ def main():
         "dtype": {"tf32": "tf32", "bf16": "bf16 (GEMM operands), f32 accumulate"}.get(args.mode, "f32"),
         "data": "synthetic (seeded N(0,1), splitmix64)",
         "config": config_of(args.config, workload),
-        "mode": args.mode, "l2": "flushed between timed steps (256 MiB write)",
+        "mode": args.mode, "l2": L2_NOTE,
         "parallelism": f"batch-sharded x{world}",
         "roofline": roof,
         "cpu_baseline": cpu,

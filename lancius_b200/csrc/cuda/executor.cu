@@ -823,9 +823,10 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
                 }
                 c->attn_lo.push_back(lo);
                 st.attn_lo = lo;
-                std::vector<CUtensorMap> maps(5 * st.count);
+                std::vector<CUtensorMap> maps(LCU_ATTN_TC_MAPS * st.count);
                 for (int i = 0; i < st.count; i++)
-                    if (!lcu_attention_tc_make_maps(&maps[5 * i], t[i].q, t[i].k, t[i].v, lo + per_set * i, 1, st.S, st.H)) {
+                    if (!lcu_attention_tc_make_maps(&maps[LCU_ATTN_TC_MAPS * i], t[i].q, t[i].k, t[i].v, t[i].o,
+                                                    lo + per_set * i, 1, st.S, st.H)) {
                         release_binding(c);
                         return fail(LANCIUS_ERROR_INTERNAL);
                     }

@@ -149,17 +149,18 @@ int* lcu_gemm_watchdog_addr(void);
 void* lcu_scratch_acquire_gather(size_t bytes);
 void* lcu_scratch_acquire_decode(size_t bytes);
 // mode: LCU_MODE_FP32_EXACT (3xTF32) or LCU_MODE_TF32 (one pass)
-// d_table: a grouped launch over `B` operand sets, whose Q/K/V tensor maps (3 per set, made by
+// d_table: a grouped launch over `B` operand sets, whose tensor maps (made by
 // lcu_attention_tc_make_maps with B = 1) are at d_maps in device memory; else q/k/v/o are
 // [B][S][H][D] and the maps are built per call.
 // lo: lcu_attention_tc_lo_floats(B, S, H) floats for the K/V lo copies (NULL on the per-op
-// path: the per-device scratch is used); a grouped launch's maps (5 per set: Q, K, V, K lo,
-// V lo) must point into that buffer at set i's [2][S][H][D] block.
+// path: the per-device scratch is used); a grouped launch's maps (LCU_ATTN_TC_MAPS per set:
+// Q, K, V, K lo, V lo, O) must point into that buffer at set i's [2][S][H][D] block.
+#define LCU_ATTN_TC_MAPS 6
 lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, const float* k, const float* v, float* o,
                                size_t B, size_t S, size_t H, int causal, int mode, const CUtensorMap* d_maps,
                                float* lo, void* stream);
-bool lcu_attention_tc_make_maps(CUtensorMap* maps, const float* q, const float* k, const float* v, const float* lo,
-                                size_t B, size_t S, size_t H);
+bool lcu_attention_tc_make_maps(CUtensorMap* maps, const float* q, const float* k, const float* v, const float* o,
+                                const float* lo, size_t B, size_t S, size_t H);
 size_t lcu_attention_tc_lo_floats(size_t B, size_t S, size_t H);
 int lcu_attention_watchdog_read_and_clear(void);
 void lcu_reset_launch_count(void);
