@@ -691,6 +691,303 @@ extern "C" lancius_error lcu_conv2d_tc_nhwc_ex(float* out, const float* in, cons
     return lcu_launch_status();
 }
 
+// ---------------------------------------------------------------------------------
+// Short-reduction conv (K = Ci*Kh*Kw <= 32, e.g. the 3-channel stem) on the tensor cores,
+// writing NHWC FP32 plus its tf32_lo copy for a tensor-core conv that reads it next.
+//   D[px][co] = A[px][k] . B[co][k]^T, 128 output pixels per tile (MMA M), K padded to 32
+//   (one 128-byte swizzle row per pixel), FP32-exact as A_hi*[B_hi|B_lo] (N = 2 Co) +
+//   A_lo*B_hi (N = Co): the left Co accumulator columns hold hi*hi + lo*hi, the right
+//   hi*lo.
+//   warps 0-3, 10-13  builders, two groups taking even and odd tiles (A buffer 0 and 1), so
+//              two tiles' gathers are in flight: one pixel per thread; gather its Ci*Kh*Kw
+//              inputs (zero padding) and write them as TF32 hi/lo rows of its A buffer
+//   warps 4-7  epilogue: TMEM -> sum of both halves -> ReLU -> hi and tf32_lo, staged as
+//              128-byte swizzled 32-channel blocks for the TMA store
+//   warp 8     TMEM allocation + MMA issue (one lane)
+//   warp 9     TMA store of the staged tile (one lane)
+// Per tile the tensor work is 8 MMAs; the kernel is bound by the output stores (2 x 4 Co
+// bytes per pixel), which the copy engine performs off the threads' path.
+namespace {
+constexpr int C1_BM = 128, C1_KP = 32, C1_THREADS = 448;
+constexpr int C1_A = C1_BM * C1_KP * 4;            // 16 KB: one of A hi / A lo
+constexpr int C1_B = 256 * C1_KP * 4;              // B hi rows then B lo rows (2 Co <= 256)
+constexpr int C1_STG = 128 * 128;                  // one 32-channel block of 128 pixels
+constexpr int C1_SMEM_BYTES = 2 * 2 * C1_A + C1_B + 8 * C1_STG + 1024 + 1024;   // staging: 2 x 64 KB or 1 x 128 KB
+
+struct SmemC1 {
+    uint64_t a_full[2], a_empty[2], acc_full[2], acc_empty[2], stg_full[2], stg_free[2], drain;
+    uint32_t tmem;
+    int abort;
+};
+
+__device__ __forceinline__ uint32_t c1_swz(int row, int chunk) { return (uint32_t)(row * 128 + ((chunk ^ (row & 7)) << 4)); }
+
+template <int CI, int KH, int KW>
+__global__ void __launch_bounds__(C1_THREADS, 1)
+k_conv_small_tc(const __grid_constant__ CUtensorMap m_hi, const __grid_constant__ CUtensorMap m_lo,
+                const float* __restrict__ in, const float* __restrict__ w, int N, int H, int W, int Co, int stride,
+                int pad, int Ho, int Wo, int relu, int exact, int with_lo, uint32_t tmem_cols) {
+    constexpr int K = CI * KH * KW;
+    static_assert(K <= C1_KP, "reduction fits one 128-byte row");
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* abuf = base;                            // [2][hi | lo]
+    uint8_t* bsm = base + 4 * C1_A;                  // [2 Co rows][128 B]
+    uint8_t* stg0 = bsm + C1_B;                      // nstg x [hi | lo][Co / 32 blocks][128 px][128 B]
+    SmemC1* sm = reinterpret_cast<SmemC1*>(stg0 + 8 * C1_STG);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long long P = (long long)N * Ho * Wo;
+    const int T = (int)((P + C1_BM - 1) / C1_BM);
+    const int nblk = Co / 32;
+    // two staging buffers when they fit (Co <= 64): the epilogue of tile j fills one while
+    // the copy engine drains tile j-1's from the other
+    const int nstg = Co <= 64 ? 2 : 1;
+    const int stg_bytes = 2 * nblk * C1_STG;
+    volatile int* abort = &sm->abort;
+
+    if (threadIdx.x == 0) {
+        for (int b = 0; b < 2; b++) {
+            tc::mbar_init(&sm->a_full[b], 128); tc::mbar_init(&sm->a_empty[b], 1);
+            tc::mbar_init(&sm->acc_full[b], 1); tc::mbar_init(&sm->acc_empty[b], 128);
+        }
+        for (int b = 0; b < 2; b++) { tc::mbar_init(&sm->stg_full[b], 128); tc::mbar_init(&sm->stg_free[b], 1); }
+        tc::mbar_init(&sm->drain, 1);
+        sm->abort = 0;
+        tc::fence_barrier_init();
+        tc::prefetch_tmap(&m_hi);
+        if (with_lo) tc::prefetch_tmap(&m_lo);
+    }
+    // weights -> B rows: hi (the value; the MMA reads its TF32 bits) for co, lo for Co + co
+    for (int i = threadIdx.x; i < Co * C1_KP; i += C1_THREADS) {
+        const int co = i / C1_KP, k = i - co * C1_KP;
+        const float x = k < K ? w[(size_t)co * K + k] : 0.f;
+        reinterpret_cast<float*>(bsm + c1_swz(co, k >> 2))[k & 3] = x;
+        reinterpret_cast<float*>(bsm + c1_swz(Co + co, k >> 2))[k & 3] = tc::tf32_lo(x);
+    }
+    tc::fence_proxy_async();
+    if (warp == 8) tc::tmem_alloc(&sm->tmem, tmem_cols);
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = sm->tmem;
+
+    if (warp < 4 || warp >= 10) {
+        // ---------------- builders ----------------
+        const int g = warp >= 10 ? 1 : 0;            // tiles j with j % 2 == g, A buffer g
+        const int r = threadIdx.x - 320 * g;         // pixel row of the tile
+        int j = g;
+        for (int t = blockIdx.x + g * gridDim.x; t < T; t += 2 * gridDim.x, j += 2) {
+            const int b = g;
+            if (j >= 2 && !tc::mbar_wait(&sm->a_empty[b], ((j >> 1) - 1) & 1, abort, &g_conv_watchdog, 41)) break;
+            const long long p = (long long)t * C1_BM + r;
+            float v[C1_KP];
+#pragma unroll
+            for (int k = 0; k < C1_KP; k++) v[k] = 0.f;
+            if (p < P) {
+                const int n = (int)(p / ((long long)Ho * Wo));
+                const int rem = (int)(p - (long long)n * Ho * Wo), ho = rem / Wo, wo = rem - ho * Wo;
+                const int y0 = ho * stride - pad, x0 = wo * stride - pad;
+                const float* src = in + (size_t)n * CI * H * W;
+#pragma unroll
+                for (int ci = 0; ci < CI; ci++)
+#pragma unroll
+                    for (int kh = 0; kh < KH; kh++)
+#pragma unroll
+                        for (int kw = 0; kw < KW; kw++) {
+                            const int iy = y0 + kh, ix = x0 + kw;
+                            if (iy >= 0 && iy < H && ix >= 0 && ix < W)
+                                v[(ci * KH + kh) * KW + kw] = __ldg(src + ((size_t)ci * H + iy) * W + ix);
+                        }
+            }
+            uint8_t* ah = abuf + b * 2 * C1_A;
+#pragma unroll
+            for (int c = 0; c < C1_KP / 4; c++) {
+                const float4 x = make_float4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+                *reinterpret_cast<float4*>(ah + c1_swz(r, c)) = x;
+                *reinterpret_cast<float4*>(ah + C1_A + c1_swz(r, c)) = tc::tf32_lo4(x);
+            }
+            tc::fence_proxy_async();
+            tc::mbar_arrive(&sm->a_full[b]);
+        }
+    } else if (warp < 8) {
+        // ---------------- epilogue ----------------
+        const int q = warp & 3, row = 32 * q + lane;
+        int j = 0;
+        for (int t = blockIdx.x; t < T; t += gridDim.x, j++) {
+            const int b = j & 1;
+            const int sb = j % nstg, su = j / nstg;
+            if (!tc::mbar_wait(&sm->acc_full[b], (j >> 1) & 1, abort, &g_conv_watchdog, 42)) break;
+            if (j >= nstg && !tc::mbar_wait(&sm->stg_free[sb], (su - 1) & 1, abort, &g_conv_watchdog, 43)) break;
+            tc::tc_fence_after();
+            uint8_t* stg = stg0 + sb * stg_bytes;
+            const uint32_t d = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)b * 2 * Co;
+            for (int blk = 0; blk < nblk; blk++) {
+                float x[32], x2[32];
+                tc::tmem_ld32(d + blk * 32, x);
+                if (exact) tc::tmem_ld32(d + Co + blk * 32, x2);
+                else {
+#pragma unroll
+                    for (int c = 0; c < 32; c++) x2[c] = 0.f;
+                }
+                uint8_t* sh = stg + blk * C1_STG;
+                uint8_t* sl = stg + (nblk + blk) * C1_STG;
+#pragma unroll
+                for (int c = 0; c < 8; c++) {
+                    float4 y = make_float4(x[4 * c] + x2[4 * c], x[4 * c + 1] + x2[4 * c + 1], x[4 * c + 2] + x2[4 * c + 2],
+                                           x[4 * c + 3] + x2[4 * c + 3]);
+                    if (relu) { y.x = fmaxf(y.x, 0.f); y.y = fmaxf(y.y, 0.f); y.z = fmaxf(y.z, 0.f); y.w = fmaxf(y.w, 0.f); }
+                    *reinterpret_cast<float4*>(sh + c1_swz(row, c)) = y;
+                    if (with_lo) *reinterpret_cast<float4*>(sl + c1_swz(row, c)) = tc::tf32_lo4(y);
+                }
+            }
+            tc::tc_fence_before();
+            tc::mbar_arrive(&sm->acc_empty[b]);
+            tc::fence_proxy_async();
+            tc::mbar_arrive(&sm->stg_full[sb]);
+        }
+    } else if (warp == 8) {
+        // ---------------- MMA issue ----------------
+        if (lane == 0) {
+            const uint32_t id_2 = tc::idesc_tf32(C1_BM, 2 * Co, false, false);
+            const uint32_t id_1 = tc::idesc_tf32(C1_BM, Co, false, false);
+            const uint32_t bb = tc::smem_u32(bsm);
+            int j = 0;
+            for (int t = blockIdx.x; t < T; t += gridDim.x, j++) {
+                const int b = j & 1;
+                if (!tc::mbar_wait(&sm->a_full[b], (j >> 1) & 1, abort, &g_conv_watchdog, 44)) break;
+                if (j >= 2 && !tc::mbar_wait(&sm->acc_empty[b], ((j >> 1) - 1) & 1, abort, &g_conv_watchdog, 45)) break;
+                tc::tc_fence_after();
+                const uint32_t ah = tc::smem_u32(abuf + b * 2 * C1_A), d = tmem + (uint32_t)b * 2 * Co;
+#pragma unroll
+                for (int kb = 0; kb < C1_KP / 8; kb++) {
+                    const uint64_t db = tc::smem_desc(bb + kb * 32, 16, 1024, tc::SWZ_128B);
+                    const uint64_t da = tc::smem_desc(ah + kb * 32, 16, 1024, tc::SWZ_128B);
+                    if (exact) {
+                        tc::mma_tf32(d, da, db, id_2, kb ? 1u : 0u);                      // hi x [hi | lo]
+                        tc::mma_tf32(d, tc::smem_desc(ah + C1_A + kb * 32, 16, 1024, tc::SWZ_128B), db, id_1, 1u);   // lo x hi
+                    } else {
+                        tc::mma_tf32(d, da, db, id_1, kb ? 1u : 0u);
+                    }
+                }
+                tc::mma_commit(&sm->a_empty[b]);
+                tc::mma_commit(&sm->acc_full[b]);
+            }
+        }
+    } else if (warp == 9) {
+        // ---------------- TMA store ----------------
+        if (lane == 0) {
+            int j = 0;
+            for (int t = blockIdx.x; t < T; t += gridDim.x, j++) {
+                const int sb = j % nstg;
+                if (!tc::mbar_wait(&sm->stg_full[sb], (j / nstg) & 1, abort, &g_conv_watchdog, 46)) break;
+                const uint8_t* stg = stg0 + sb * stg_bytes;
+                for (int blk = 0; blk < nblk; blk++) {
+                    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                                 ::"l"(reinterpret_cast<uint64_t>(&m_hi)), "r"(tc::smem_u32(stg + blk * C1_STG)),
+                                   "r"(32 * blk), "r"(t * C1_BM) : "memory");
+                    if (with_lo)
+                        asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+                                     ::"l"(reinterpret_cast<uint64_t>(&m_lo)), "r"(tc::smem_u32(stg + (nblk + blk) * C1_STG)),
+                                       "r"(32 * blk), "r"(t * C1_BM) : "memory");
+                }
+                asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                if (nstg == 2) {   // the previous tile's buffer is free once its copies read it
+                    asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory");
+                    if (j >= 1) tc::mbar_arrive(&sm->stg_free[(j - 1) & 1]);
+                } else {
+                    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+                    tc::mbar_arrive(&sm->stg_free[0]);
+                }
+            }
+            asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        }
+    }
+
+    tc::tc_fence_before();
+    __syncthreads();
+    if (sm->abort && warp == 8 && lane == 0) {   // let issued MMAs retire before TMEM is released
+        int never = 0;
+        tc::mma_commit(&sm->drain);
+        tc::mbar_wait(&sm->drain, 0, &never, nullptr, 0);
+    }
+    __syncthreads();
+    if (warp == 8) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, tmem_cols);
+    }
+}
+
+bool make_nhwc_out_map(CUtensorMap* m, float* out, long long P, int Co) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || (reinterpret_cast<uintptr_t>(out) & 15)) return false;
+    cuuint64_t dims[2] = {(cuuint64_t)Co, (cuuint64_t)P};
+    cuuint64_t strides[1] = {(cuuint64_t)Co * 4};
+    cuuint32_t box[2] = {32, C1_BM}, es[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, out, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
+// The stem geometries instantiated above; Co a multiple of 32 up to 128.
+extern "C" int lcu_conv_small_tc_ok(size_t N, size_t Ci, size_t H, size_t W, size_t Co, size_t Kh, size_t Kw,
+                                    size_t stride, size_t pad) {
+    const char* e = getenv("LCU_CONV_SMALL_SIMT");
+    if (e && e[0] == '1') return 0;
+    const bool geo = (Ci == 3 && Kh == 3 && Kw == 3) || (Ci == 1 && Kh == 3 && Kw == 3) || (Ci == 3 && Kh == 1 && Kw == 1);
+    if (!geo || Co % 32 || Co == 0 || Co > 128 || stride < 1 || H + 2 * pad < Kh || W + 2 * pad < Kw) return 0;
+    const size_t Ho = (H + 2 * pad - Kh) / stride + 1, Wo = (W + 2 * pad - Kw) / stride + 1;
+    return N * Ho * Wo < (1ull << 31) && N * Ci * H * W < (1ull << 31);
+}
+
+// out (and out_lo, when given) NHWC [N][Ho][Wo][Co]; in NCHW; w [Co][Ci][Kh][Kw].
+// mode LCU_MODE_TF32: one pass; otherwise 3xTF32 (FP32-exact).
+extern "C" lancius_error lcu_conv2d_small_tc_nhwc(float* out, float* out_lo, const float* in, const float* w, size_t N,
+                                                  size_t Ci, size_t H, size_t W, size_t Co, size_t Kh, size_t Kw,
+                                                  size_t stride, size_t pad, int relu, int mode, void* stream) {
+    if (!lcu_conv_small_tc_ok(N, Ci, H, W, Co, Kh, Kw, stride, pad)) {
+        lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP);
+        return LANCIUS_ERROR_UNSUPPORTED_OP;
+    }
+    const int Ho = (int)((H + 2 * pad - Kh) / stride + 1), Wo = (int)((W + 2 * pad - Kw) / stride + 1);
+    const long long P = (long long)N * Ho * Wo;
+    if (P == 0) return LANCIUS_ERROR_OK;
+    CUtensorMap mh, ml;
+    if (!make_nhwc_out_map(&mh, out, P, (int)Co) || (out_lo && !make_nhwc_out_map(&ml, out_lo, P, (int)Co))) {
+        lancius_set_error(LANCIUS_ERROR_INTERNAL);
+        return LANCIUS_ERROR_INTERNAL;
+    }
+    if (!out_lo) ml = mh;
+    static int n_sm = 0;
+    if (!n_sm) { int dev = 0; cudaGetDevice(&dev); cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev); }
+    const long long T = (P + C1_BM - 1) / C1_BM;
+    const unsigned grid = (unsigned)std::min<long long>(T, n_sm > 0 ? n_sm : LCU_SMS);
+    uint32_t cols = 32;
+    while (cols < 4 * Co) cols <<= 1;
+    const int exact = mode == LCU_MODE_TF32 ? 0 : 1;
+    cudaStream_t st = lcu_as_stream(stream);
+#define LCU_C1(ci, kh, kw)                                                                                          \
+    if (Ci == ci && Kh == kh && Kw == kw) {                                                                         \
+        static bool conf[64] = {};                                                                                  \
+        int dev = 0;                                                                                                \
+        cudaGetDevice(&dev);                                                                                        \
+        if (dev >= 0 && dev < 64 && !conf[dev]) {                                                                   \
+            if (cudaFuncSetAttribute(k_conv_small_tc<ci, kh, kw>, cudaFuncAttributeMaxDynamicSharedMemorySize,      \
+                                     C1_SMEM_BYTES) != cudaSuccess)                                                 \
+                return lcu_launch_status();                                                                         \
+            conf[dev] = true;                                                                                       \
+        }                                                                                                           \
+        k_conv_small_tc<ci, kh, kw><<<grid, C1_THREADS, C1_SMEM_BYTES, st>>>(                                       \
+            mh, ml, in, w, (int)N, (int)H, (int)W, (int)Co, (int)stride, (int)pad, Ho, Wo, relu, exact,             \
+            out_lo ? 1 : 0, cols);                                                                                  \
+        lcu_note_launch();                                                                                          \
+        return lcu_launch_status();                                                                                 \
+    }
+    LCU_C1(3, 3, 3) LCU_C1(1, 3, 3) LCU_C1(3, 1, 1)
+#undef LCU_C1
+    lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP);
+    return LANCIUS_ERROR_UNSUPPORTED_OP;
+}
+
 extern "C" int lcu_conv_watchdog_read_and_clear(void) {
     int v = 0, z = 0;
     cudaMemcpyFromSymbol(&v, g_conv_watchdog, sizeof(int));

@@ -443,6 +443,12 @@ lancius_error lcu_conv2d_smallk_ex(float* out, const float* in, const float* w, 
     if (!smallk_fits_int(N, Ci, H, W, Co, Ho, Wo))
         return lcu_conv2d_simt(out, in, w, N, Ci, H, W, Co, Kh, Kw, stride, pad, relu, stream);
     cudaStream_t st = lcu_as_stream(stream);
+    // NHWC output for a tensor-core conv that reads it next: the tensor-core stem kernel
+    // (FP32-exact), whose TMA stores keep the output write at HBM speed
+    if (out_nhwc && lcu_conv_small_tc_ok(N, Ci, H, W, Co, Kh, Kw, stride, pad) && (reinterpret_cast<uintptr_t>(out) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(out_lo) & 15) == 0)
+        return lcu_conv2d_small_tc_nhwc(out, out_lo, in, w, N, Ci, H, W, Co, Kh, Kw, stride, pad, relu, LCU_MODE_FP32_EXACT,
+                                        stream);
     // register-blocked variants for common stems (4 pixels x 16 channels per thread)
     const bool qshape = smallk_q_shape(N, Ci, H, W, Co, Kh, Kw, stride, pad) && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
     if (out_nhwc && !qshape) { lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP; }

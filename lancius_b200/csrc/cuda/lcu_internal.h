@@ -113,6 +113,13 @@ lancius_error lcu_nhwc_to_nchw(void* out, const float* in, int n, int c, int h, 
 lancius_error lcu_conv2d_smallk_ex(float* out, const float* in, const float* w, size_t N, size_t Ci, size_t H, size_t W,
                                    size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad, int relu, int out_nhwc,
                                    void* stream, float* out_lo);
+// tensor-core short-reduction conv (Ci*Kh*Kw <= 32 stems, Co % 32 == 0, Co <= 128) writing
+// NHWC (+ its tf32_lo copy when out_lo is given)
+int lcu_conv_small_tc_ok(size_t N, size_t Ci, size_t H, size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride,
+                         size_t pad);
+lancius_error lcu_conv2d_small_tc_nhwc(float* out, float* out_lo, const float* in, const float* w, size_t N, size_t Ci,
+                                       size_t H, size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride, size_t pad,
+                                       int relu, int mode, void* stream);
 int lcu_conv_smallk_nhwc_ok(size_t N, size_t Ci, size_t H, size_t W, size_t Co, size_t Kh, size_t Kw, size_t stride,
                             size_t pad);
 int lcu_conv_force_im2col(void);

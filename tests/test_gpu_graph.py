@@ -287,18 +287,27 @@ def test_conv_chain_nhwc_handoff(device, orc):
 
     y64, y32, (g, arrs, convs) = run()
     variants = []
-    for var in ("LCU_NO_NHWC_HANDOFF", "LCU_NO_NHWC_LO"):      # NCHW throughout; NHWC split on chip
+    # NHWC split on chip (same kernels otherwise: same bytes); NCHW throughout (the stem
+    # runs on CUDA cores in exact FP32 order instead of the tensor-core stem: within the
+    # conv bound)
+    for var in ("LCU_NO_NHWC_LO", "LCU_NO_NHWC_HANDOFF"):
         os.environ[var] = "1"
         try:
             variants.append(run()[:2])
         finally:
             del os.environ[var]
     assert len(convs) == 2
-    for r64, r32 in variants:
+    for i, (r64, r32) in enumerate(variants):
         for a, b in zip(y64, r64):
-            assert np.array_equal(a, b)
+            if i == 0:
+                assert np.array_equal(a, b)
+            else:
+                assert_close(a, b, 1e-4, k=64 * 9)
         for a, b in zip(y32, r32):
-            assert np.array_equal(a, b)
+            if i == 0:
+                assert np.array_equal(a, b)
+            else:
+                assert_close(a, b, 1e-4, k=64 * 9)
     for n, a in arrs:
         g.bind(n, a)
     ref = orc.run_graph(g, convs)

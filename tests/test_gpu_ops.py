@@ -153,6 +153,32 @@ def test_conv2d(lib, orc, shape, relu):
     assert_close(out.cpu().numpy(), ref, 1e-4, k=Ci * Kh * Kw)
 
 
+@pytest.mark.parametrize("shape", [(2, 3, 40, 44, 64, 3, 3, 1, 1), (3, 3, 37, 29, 32, 3, 3, 2, 1),
+                                   (2, 1, 33, 35, 128, 3, 3, 1, 0), (2, 3, 21, 23, 96, 1, 1, 1, 0)])
+@pytest.mark.parametrize("relu", [0, 1])
+def test_conv_small_tc_nhwc(lib, orc, shape, relu):
+    """The tensor-core stem conv (K = Ci*Kh*Kw <= 32, 3xTF32) that feeds an NHWC conv:
+    ragged pixel counts (P % 128 != 0), stride 2, no padding, Co = 32..128. Its NHWC output
+    matches the FP64 reference, and its lo copy is exactly tf32_lo of every output."""
+    N, Ci, H, W, Co, Kh, Kw, s, p = shape
+    f = lib.lcu_conv2d_small_tc_nhwc
+    f.restype = C.c_int
+    f.argtypes = [C.c_void_p] * 4 + [C.c_size_t] * 9 + [C.c_int, C.c_int, C.c_void_p]
+    x = data.normal(23, (N, Ci, H, W))
+    w = data.normal(24, (Co, Ci, Kh, Kw), 0, np.sqrt(2.0 / (Ci * Kh * Kw)))
+    ref = orc.conv2d(x, w, s, p, bool(relu))
+    Ho, Wo = ref.shape[2], ref.shape[3]
+    out = torch.empty((N, Ho, Wo, Co), device="cuda")
+    lo = torch.empty((N, Ho, Wo, Co), device="cuda")
+    run(f(P(out), P(lo), P(dev(x)), P(dev(w)), N, Ci, H, W, Co, Kh, Kw, s, p, relu, MODE_FP32_EXACT, None))
+    y = np.ascontiguousarray(out.cpu().numpy().transpose(0, 3, 1, 2))
+    assert_close(y, ref, 1e-4, k=Ci * Kh * Kw)
+    hi = (y.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+    d = (y - hi).view(np.uint32)
+    want = ((d + np.uint32(0x1000)) & np.uint32(0xFFFFE000)).view(np.float32)   # round to nearest TF32
+    assert np.array_equal(np.ascontiguousarray(lo.cpu().numpy().transpose(0, 3, 1, 2)), want)
+
+
 @pytest.mark.parametrize("shape", [(2, 64, 32, 32, 128, 3, 3, 1, 1), (2, 16, 64, 64, 48, 5, 5, 2, 2)])
 def test_conv2d_split_on_chip_matches_split_pass(lib, shape):
     """The direct conv splits its NHWC input tiles into TF32 hi/lo on chip; the result is
