@@ -50,6 +50,7 @@ struct ConvArgs {
     int passes, relu;
     int raw_b;       // 1: the input map covers plain FP32 NHWC; the epilogue warps split it on chip
     int out_nhwc;    // 1 (persistent kernel only): store the output NHWC for a conv that reads it next
+    int tma_out;     // with out_nhwc: the epilogue stages 32 x 32 blocks and stores them by TMA (maps to_hi/to_lo)
     float* out_lo;   // with out_nhwc: also store tf32_lo of every output there (NHWC), so the next
                      // conv loads hi (the value itself) and lo by TMA and needs no splitter
 };
@@ -242,7 +243,10 @@ k_conv_tc(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
 constexpr int PT_BM = 128, PT_STAGES = 4;
 constexpr int PT_A_TILE = PT_BM * BK * 4;                       // 8 KB
 constexpr int PT_STAGE_BYTES = 2 * PT_A_TILE + 2 * B_TILE;      // 48 KB
-constexpr int PT_SMEM_BYTES = PT_STAGES * PT_STAGE_BYTES + 4 * 32 * 32 * 4 + 1024 + 256;
+// epilogue staging: per epilogue warp 32 x 32 floats (NCHW transpose) or, for a TMA-stored
+// NHWC output, a hi and a lo block of 32 pixels x 32 channels (128-byte swizzled rows)
+constexpr int PT_EPI_FLOATS = 4 * 2 * 32 * 32;
+constexpr int PT_SMEM_BYTES = PT_STAGES * PT_STAGE_BYTES + PT_EPI_FLOATS * 4 + 1024 + 256;
 
 constexpr int PT_THREADS = 320;
 
@@ -255,11 +259,11 @@ struct SmemPT {
 __global__ void __launch_bounds__(PT_THREADS, 1)
 k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUtensorMap tw_lo,
           const __grid_constant__ CUtensorMap tx_hi, const __grid_constant__ CUtensorMap tx_lo, float* __restrict__ out,
-          ConvArgs a) {
+          ConvArgs a, const __grid_constant__ CUtensorMap to_hi, const __grid_constant__ CUtensorMap to_lo) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     float* stage_f = reinterpret_cast<float*>(tiles + PT_STAGES * PT_STAGE_BYTES);
-    SmemPT* sm = reinterpret_cast<SmemPT*>(stage_f + 4 * 32 * 32);
+    SmemPT* sm = reinterpret_cast<SmemPT*>(stage_f + PT_EPI_FLOATS);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int hw = a.ho * a.wo;
     const int tiles_per_img = (a.ho + a.rows - 1) / a.rows;
@@ -382,7 +386,7 @@ k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
     } else if (warp >= 2) {
         // ---------------- epilogue: rows = output channels, columns = pixels ----------------
         const int q = warp & 3;
-        float* sb = stage_f + q * 32 * 32;           // 32x32 block, float4 slots XOR-swizzled by row
+        float* sb = stage_f + q * 2 * 32 * 32;       // 32x32 block, float4 slots XOR-swizzled by row
         const bool v4base = hw % 4 == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
         int j = 0;
         for (int t = blockIdx.x; t < T; t += gridDim.x, j++) {
@@ -399,6 +403,38 @@ k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
             tc::tmem_ld32_issue(tbase, va);
             for (int c = 0; c < bn; c += 32) {
                 tc::tmem_ld_wait(va);
+                if (a.tma_out) {
+                    // NHWC by TMA: lane = channel; the block is staged as 32 pixel rows of 32
+                    // channels (128-byte swizzle) in hi and lo halves and stored as one box
+                    // each, clipped at the image's last pixel and at Co. Plain stores of these
+                    // rows were measured to cost ~120 us of the conv stack's 0.81 ms.
+                    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // previous block read
+                    __syncwarp();
+                    float* sl = sb + 32 * 32;
+#pragma unroll
+                    for (int px = 0; px < 32; px++) {
+                        float x = __uint_as_float(va[px]);
+                        if (a.relu) x = fmaxf(x, 0.f);
+                        const int o = px * 32 + ((((lane >> 2) ^ (px & 7))) << 2) + (lane & 3);
+                        sb[o] = x;
+                        if (a.out_lo) sl[o] = tc::tf32_lo(x);
+                    }
+                    if (c + 32 < bn) tc::tmem_ld32_issue(tbase + (uint32_t)(c + 32), va);
+                    tc::fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0 && c < valid) {
+                        const int pix = ho0 * a.wo + c;
+                        asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+                                     ::"l"(reinterpret_cast<uint64_t>(&to_hi)), "r"(tc::smem_u32(sb)), "r"(co0), "r"(pix), "r"(img)
+                                     : "memory");
+                        if (a.out_lo)
+                            asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+                                         ::"l"(reinterpret_cast<uint64_t>(&to_lo)), "r"(tc::smem_u32(sl)), "r"(co0), "r"(pix),
+                                           "r"(img) : "memory");
+                        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int jj = 0; jj < 8; jj++)
                     *reinterpret_cast<float4*>(sb + lane * 32 + ((jj ^ (lane & 7)) << 2)) =
@@ -442,6 +478,7 @@ k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&sm->acc_empty[b]);
         }
+        if (a.tma_out && lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     }
 
     tc::tc_fence_before();
@@ -677,11 +714,31 @@ extern "C" lancius_error lcu_conv2d_tc_nhwc_ex(float* out, const float* in, cons
         else mx_lo = mx_hi;
     }
     if (!ok) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    // NHWC output by TMA stores of 32 x 32 blocks (LCU_CONV_NO_TMA_OUT=1: plain stores)
+    CUtensorMap mo_hi, mo_lo;
+    int tma_out = 0;
+    if (out_nhwc) {
+        const char* env = getenv("LCU_CONV_NO_TMA_OUT");
+        tma_out = !(env && env[0] == '1') && cs.co % 4 == 0 && !(reinterpret_cast<uintptr_t>(out) & 15) &&
+                  !(reinterpret_cast<uintptr_t>(out_lo) & 15);
+        if (tma_out) {
+            cuuint64_t dims[3] = {(cuuint64_t)cs.co, (cuuint64_t)cs.ho * cs.wo, (cuuint64_t)cs.n};
+            cuuint64_t strides[2] = {(cuuint64_t)cs.co * 4, (cuuint64_t)cs.ho * cs.wo * cs.co * 4};
+            cuuint32_t box[3] = {32, 32, 1}, es[3] = {1, 1, 1};
+            tma_out = fn(&mo_hi, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, out, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            if (tma_out && out_lo)
+                tma_out = fn(&mo_lo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, out_lo, dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+        }
+    }
+    if (!tma_out) mo_hi = mw_hi;
+    if (!tma_out || !out_lo) mo_lo = mo_hi;
     ConvArgs a{cs.n, cs.ci, cs.co, cs.kh, cs.kw, cs.stride, cs.pad, cs.ho, cs.wo, rows, cs.co > 128 ? 2 : 1, passes, relu, raw,
-               out_nhwc, out_nhwc ? out_lo : nullptr};
+               out_nhwc, tma_out, out_nhwc ? out_lo : nullptr};
     if (pt) {
         const long long T = (long long)cs.n * ((cs.ho + rows - 1) / rows) * ((cs.co + PT_BM - 1) / PT_BM);
-        k_conv_pt<<<(unsigned)std::min<long long>(T, n_sm), PT_THREADS, PT_SMEM_BYTES, st>>>(mw_hi, mw_lo, mx_hi, mx_lo, out, a);
+        k_conv_pt<<<(unsigned)std::min<long long>(T, n_sm), PT_THREADS, PT_SMEM_BYTES, st>>>(mw_hi, mw_lo, mx_hi, mx_lo, out, a, mo_hi, mo_lo);
         lcu_note_launch();
         return lcu_launch_status();
     }
