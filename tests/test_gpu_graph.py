@@ -124,28 +124,37 @@ def test_caller_plan_path(device, orc):
 def test_fused_launch_count(device):
     """MLP: one launch per graph. Layer 1 (bias + ReLU in the epilogue) and layer 2 (bias +
     row softmax) run in one kernel: the last CTA of each 16-row block computes that block's
-    layer 2 from the finished hidden rows. LCU_NO_MLP_FUSE=1 gives the two-launch form and
-    the same bits."""
+    layer 2 from the finished hidden rows. The two-launch form gives
+    the same bits. The one-launch form is opt-in (LCU_MLP_FUSE=1); the default is two."""
     import os
-    b = configs.mlp(L.Graph())
-    (y,), _ = run_gpu(device, b)
-    assert device.last_launch_count == 1
-    device.execute()                       # the tickets were reset: a second run is identical
-    assert np.array_equal(device.download(b.outputs[0]), y)
-    os.environ["LCU_NO_MLP_FUSE"] = "1"
+    os.environ["LCU_MLP_FUSE"] = "1"
     try:
-        b2 = configs.mlp(L.Graph())
-        (y2,), _ = run_gpu(device, b2)
-        assert device.last_launch_count == 2
+        b = configs.mlp(L.Graph())
+        (y,), _ = run_gpu(device, b)
+        assert device.last_launch_count == 1
+        device.execute()                       # the tickets were reset: a second run is identical
+        assert np.array_equal(device.download(b.outputs[0]), y)
     finally:
-        del os.environ["LCU_NO_MLP_FUSE"]
+        del os.environ["LCU_MLP_FUSE"]
+    b2 = configs.mlp(L.Graph())
+    (y2,), _ = run_gpu(device, b2)
+    assert device.last_launch_count == 2
     assert np.array_equal(y, y2)
 
 
 def test_mlp_fused_other_shapes(device, orc):
     """The one-launch two-layer form on ragged shapes: rows not a multiple of 16, hidden
     width not a multiple of 32, GELU between the layers, 32 output columns."""
+    import os
     from lancius_b200 import data
+    os.environ["LCU_MLP_FUSE"] = "1"
+    try:
+        _mlp_fused_shapes(device, orc, data)
+    finally:
+        del os.environ["LCU_MLP_FUSE"]
+
+
+def _mlp_fused_shapes(device, orc, data):
     for M, K, N1, N2, act in ((37, 100, 70, 7, "relu"), (130, 64, 96, 32, "gelu"), (5, 33, 40, 3, "relu")):
         g = L.Graph()
         bb = configs.Built("mlp_shape", g)
