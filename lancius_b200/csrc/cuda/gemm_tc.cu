@@ -35,10 +35,7 @@ constexpr int THREADS = 64 + 32 * EPI_WARPS + 32;     // + the second MMA issuer
 constexpr int MMA_WARP2 = 2 + EPI_WARPS;
 constexpr int A_TILE = BM * BK * 4;                  // 16 KB (two 128-row halves)
 constexpr int B_CHUNK = BK * 32 * 4;                 // 2 KB: 16 k-rows x 32 n
-constexpr int B_TILE = BN * BK * 4;                  // 16 KB
-constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE; // 64 KB
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + BN * 4 /*bias slice*/;
-constexpr uint32_t TMEM_COLS = 512;   // two 128x256 FP32 accumulators (rows 0-127, 128-255)
+constexpr uint32_t TMEM_COLS = 512;   // two 128x256 FP32 accumulators (rows 0-127, 128-255) at columns 0 and 256
 
 __device__ int g_gemm_watchdog = 0;
 
@@ -71,13 +68,21 @@ struct Smem {
     int consumed;
 };
 
-template <bool DST>   // DST: the epilogue stores into LcuColDest's destinations
+// Dynamic shared memory of a launch with TBN-column tiles.
+constexpr int smem_bytes(int tbn) { return STAGES * (2 * A_TILE + 2 * tbn * BK * 4) + 1024 + 256 + tbn * 4; }
+
+// DST: the epilogue stores into LcuColDest's destinations. TBN: tile columns, 256 or 192
+// (192 for products whose 256-wide tiles would leave SMs idle in the last round, e.g.
+// 8192 x 768: 96 tiles of 256 x 256 against 128 of 256 x 192 on 148 SMs; N = 192 MMAs run
+// at ~3/4 of the time of N = 256 ones).
+template <bool DST, int TBN>
 __global__ void __launch_bounds__(THREADS, 1)
 k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUtensorMap ta_lo,
           const __grid_constant__ CUtensorMap tb_hi, const __grid_constant__ CUtensorMap tb_lo,
           const LcuGemmGroup* __restrict__ groups, int M, int N, int K, int epi, int passes,
           int splits, int kchunk, float* __restrict__ partial, int conv_hw, LcuColDest dst,
           const CUtensorMap* __restrict__ a_maps) {
+    constexpr int BN = TBN, B_TILE = BN * BK * 4, STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;
     extern __shared__ uint8_t smem_raw[];
     uint8_t* tiles = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Smem* sm = reinterpret_cast<Smem*>(tiles + STAGES * STAGE_BYTES);
@@ -170,7 +175,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
             uint32_t a_hi = st, a_lo = st + A_TILE, b_hi = st + 2 * A_TILE, b_lo = st + 2 * A_TILE + B_TILE;
             if (bf) {
                 constexpr uint32_t idb = tc::idesc_bf16(128, BN);
-                const uint32_t hoff = (uint32_t)half * (128 * BK * 4), d = tmem + (uint32_t)half * BN;
+                const uint32_t hoff = (uint32_t)half * (128 * BK * 4), d = tmem + (uint32_t)half * 256;
 #pragma unroll
                 for (int kb = 0; kb < 2; kb++) {             // 16 k (32 bytes) per MMA
                     const uint64_t da = tc::smem_desc(a_hi + hoff + kb * 32, 16, 512, tc::SWZ_64B);
@@ -183,7 +188,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
                 uint64_t dbh = tc::smem_desc(b_hi + kb * 1024, B_CHUNK, 512, tc::SWZ_128B_BASE32B);
                 uint64_t dbl = tc::smem_desc(b_lo + kb * 1024, B_CHUNK, 512, tc::SWZ_128B_BASE32B);
                 {                                            // rows 0-127 and 128-255 share the B tile
-                    const uint32_t hoff = (uint32_t)half * (128 * BK * 4), d = tmem + (uint32_t)half * BN;
+                    const uint32_t hoff = (uint32_t)half * (128 * BK * 4), d = tmem + (uint32_t)half * 256;
                     uint64_t dah = tc::smem_desc(a_hi + hoff + kb * 32, 16, 512, tc::SWZ_64B);
                     uint32_t acc = (kt | kb) ? 1u : 0u;
                     if (passes > 1) {
@@ -266,7 +271,7 @@ k_gemm_tc(const __grid_constant__ CUtensorMap ta_hi, const __grid_constant__ CUt
             tc::tc_fence_after();
             float* sb = reinterpret_cast<float*>(tiles) + (size_t)(warp - 2) * 32 * 36;
             auto taddr = [&](int i) {
-                return tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((i / nc) * BN + (i % nc) * 32);
+                return tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)((i / nc) * 256 + (i % nc) * 32);
             };
             const int total = nh * nc;
             uint32_t va[32];
@@ -647,8 +652,9 @@ extern "C" lancius_error lcu_gemm_tc_run_dst(const LcuTcGemmPlan* p, const LcuGe
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 64) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
     if (!configured[dev]) {
-        if (cudaFuncSetAttribute(k_gemm_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess ||
-            cudaFuncSetAttribute(k_gemm_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+        if (cudaFuncSetAttribute(k_gemm_tc<false, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(256)) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemm_tc<true, 256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(256)) != cudaSuccess ||
+            cudaFuncSetAttribute(k_gemm_tc<false, 192>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes(192)) != cudaSuccess)
             return lcu_launch_status();
         configured[dev] = true;
     }
@@ -675,13 +681,26 @@ extern "C" lancius_error lcu_gemm_tc_run_dst(const LcuTcGemmPlan* p, const LcuGe
             k_split<<<dim3((unsigned)(p->K < 65535 ? p->K : 65535), p->G), 256, 0, st>>>(d_groups, 1, p->K, p->N, p->Np, p->s_bhi, lo_b);
         if (p->conv.n || !p->b_presplit) lcu_note_launch();
     }
-    dim3 grid((unsigned)((p->N + BN - 1) / BN), (unsigned)((p->M + BM - 1) / BM), (unsigned)(p->G * p->splits));
-    if (dst.n_dst > 0)
-        k_gemm_tc<true><<<grid, THREADS, SMEM_BYTES, st>>>(p->a_hi, p->a_lo, p->b_hi, p->b_lo, d_groups, (int)p->M, (int)p->N,
+    // tile width: 192 where it takes fewer tile-column-rounds of the SMs (a tile's time is
+    // about proportional to its width); BF16 and the fused all-gather keep 256
+    const size_t mt = (p->M + BM - 1) / BM, gz = (size_t)p->G * p->splits;
+    auto cost = [&](size_t bn) { return ((mt * ((p->N + bn - 1) / bn) * gz + LCU_SMS - 1) / LCU_SMS) * bn; };
+    const char* bn_env = getenv("LCU_GEMM_BN");
+    const bool narrow = p->passes > 0 && dst.n_dst == 0 && !(bn_env && atoi(bn_env) == 256) &&
+                        ((bn_env && atoi(bn_env) == 192) || cost(192) < cost(256));
+    const unsigned tbn = narrow ? 192u : 256u;
+    dim3 grid((unsigned)((p->N + tbn - 1) / tbn), (unsigned)((p->M + BM - 1) / BM), (unsigned)(p->G * p->splits));
+    if (narrow)
+        k_gemm_tc<false, 192><<<grid, THREADS, smem_bytes(192), st>>>(p->a_hi, p->a_lo, p->b_hi, p->b_lo, d_groups, (int)p->M,
+                                                                      (int)p->N, (int)p->K, epi, p->passes, p->splits,
+                                                                      p->kchunk, p->partial,
+                                                                      p->conv.n ? p->conv.ho * p->conv.wo : 0, dst, p->d_amaps);
+    else if (dst.n_dst > 0)
+        k_gemm_tc<true, 256><<<grid, THREADS, smem_bytes(256), st>>>(p->a_hi, p->a_lo, p->b_hi, p->b_lo, d_groups, (int)p->M, (int)p->N,
                                                            (int)p->K, epi, p->passes, p->splits, p->kchunk, p->partial,
                                                            p->conv.n ? p->conv.ho * p->conv.wo : 0, dst, p->d_amaps);
     else
-        k_gemm_tc<false><<<grid, THREADS, SMEM_BYTES, st>>>(p->a_hi, p->a_lo, p->b_hi, p->b_lo, d_groups, (int)p->M, (int)p->N,
+        k_gemm_tc<false, 256><<<grid, THREADS, smem_bytes(256), st>>>(p->a_hi, p->a_lo, p->b_hi, p->b_lo, d_groups, (int)p->M, (int)p->N,
                                                             (int)p->K, epi, p->passes, p->splits, p->kchunk, p->partial,
                                                             p->conv.n ? p->conv.ho * p->conv.wo : 0, dst, p->d_amaps);
     lcu_note_launch();

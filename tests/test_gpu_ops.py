@@ -104,6 +104,28 @@ def test_attention(lib, orc, B, S, H, D, causal):
     assert_close(y, ref, 1e-4)
 
 
+@pytest.mark.parametrize("M,K,N", [(1024, 3072, 768), (520, 768, 1000)])
+def test_matmul_tile_widths(lib, orc, M, K, N):
+    """The tensor-core GEMM's 256 x 192 tiles (chosen when they take fewer rounds of the SMs,
+    as for the encoder's FFN2 / O-projection shapes) and its 256 x 256 tiles, forced by
+    LCU_GEMM_BN: both match the FP64 reference, ragged N included."""
+    import os
+    a = data.uniform(31, (M, K), -1, 1)
+    b = data.uniform(32, (K, N), -1, 1)
+    bias = data.normal(33, (N,))
+    ref = np.maximum(orc.matmul(a, b) + bias, 0)
+    outs = []
+    for bn in ("192", "256"):
+        os.environ["LCU_GEMM_BN"] = bn
+        try:
+            out = torch.empty((M, N), device="cuda")
+            run(lib.lcu_matmul(P(out), P(dev(a)), P(dev(b)), M, K, N, P(dev(bias)), EPI_RELU, MODE_FP32_EXACT, None))
+            outs.append(out.cpu().numpy())
+        finally:
+            del os.environ["LCU_GEMM_BN"]
+        assert_close(outs[-1], ref, 1e-4, k=K)
+
+
 @pytest.mark.parametrize("M,K,N", [(512, 768, 3072), (2048, 2048, 2048), (300, 1000, 260), (4096, 16384, 256)])
 def test_matmul_bf16_mode(lib, orc, M, K, N):
     """BF16 fast mode: both operands rounded to BF16, tcgen05 kind::f16, FP32 accumulate
