@@ -701,7 +701,8 @@ extern "C" lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const flo
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = exact ? 1 : 0;
+    static const bool no_pdl = [] { const char* e = getenv("LCU_ATTN_NO_PDL"); return e && e[0] == '1'; }();
+    cfg.numAttrs = exact && !no_pdl ? 1 : 0;
     const CUtensorMap* dm = d_table ? d_maps : nullptr;
     const size_t bstride = S * H * D;
     cudaError_t e = exact ? cudaLaunchKernelEx(&cfg, k_attn_tc<true>, d_table, base, bstride, (int)B, (int)S, (int)H, causal,
