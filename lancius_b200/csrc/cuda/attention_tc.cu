@@ -28,9 +28,12 @@
 //              Q_hi K_lo in the right half of S, and S = left + right; same for
 //              P_hi*[V_hi|V_lo] and P_lo*V_hi into O.
 //   warp 10    K producer, warp 11 V producer (one lane each): TMA of the raw key tile
-//              (= the hi operand: the MMA reads only the TF32 bits) and of its lo part
-//              from the copy the split pass made. The kernel is launched as a programmatic
-//              dependent of that pass; only these loads wait for it.
+//              (= the hi operand: the MMA reads only the TF32 bits).
+//   warps 12-13 K and V splitters: lo = x - hi(x) of each landed tile into the stage's lo
+//              half, then the stage is released to the issuers. (LCU_ATTN_SPLIT_PASS=1
+//              instead runs a split pass over all of K and V first, whose lo copies the
+//              producers load by TMA; the kernel is then that pass's programmatic
+//              dependent. Measured 36.9 against 34.4 us per graph for the in-CTA split.)
 // S/P live in two TMEM buffers used by alternate key tiles, so the softmax of tile j never
 // waits for PV of tile j-1. TMEM columns: Q hi [0,64) lo [64,128); S/P buffers [128,256)
 // and [256,384); O halves [384,512). Every mbarrier wait is bounded.
@@ -40,8 +43,8 @@
 namespace {
 
 constexpr int D = 64, BQ = 128, BKV = 64, NSK = 3, NSV = 3, NBUF = 2;
-constexpr int W_S = 8, W_PV = 9, W_K = 10, W_V = 11;
-constexpr int THREADS = 384;
+constexpr int W_S = 8, W_PV = 9, W_K = 10, W_V = 11, W_KS = 12, W_VS = 13;
+constexpr int THREADS = 448;
 constexpr int NSOFT = 256;                      // softmax threads (warps 0-7)
 constexpr int KV_HALF = BKV * D * 4;            // 16 KB: one hi or lo tile
 constexpr int STAGE = 2 * KV_HALF;              // hi + lo
@@ -71,6 +74,7 @@ __device__ __forceinline__ unsigned long long gtime() { unsigned long long t; as
 
 struct Bars {
     uint64_t k_full[NSK], k_empty[NSK], v_full[NSV], v_empty[NSV];
+    uint64_t k_split[NSK], v_split[NSV];   // in-kernel split: the stage's lo half is written
     uint64_t s_full[NBUF], p_ready[NBUF], pv_done[NBUF];   // per S/P buffer
     uint64_t xch[4][2];      // per row quadrant and exchange parity: both halves posted
     uint64_t q_full, q_ready, o_free, drain, drain_pv;
@@ -162,7 +166,10 @@ __device__ __forceinline__ int next_valid(int x, int n_slots, int per, int nqt) 
 
 // EXACT: 3xTF32 (FP32-exact). Otherwise the TF32 fast mode: one pass, Q K^T and P V on the
 // raw FP32 operands (the MMA reads their TF32 bits), no lo copies anywhere.
-template <bool EXACT>
+// INSPLIT (FP32-exact only): the lo halves of the K and V stages are computed in the CTA
+// (warps 12 and 13) from the raw tile the TMA brought, instead of loaded from the split
+// pass's copies.
+template <bool EXACT, bool INSPLIT>
 __global__ void __launch_bounds__(THREADS, 1)
 k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstride, int B, int S, int H, int causal,
           float scale_log2, const CUtensorMap* __restrict__ gmaps, const __grid_constant__ AttnMaps pm) {
@@ -188,10 +195,10 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
     if (threadIdx.x == 0) {
         TRACE(62);
         for (int s = 0; s < NSK; s++) {
-            tc::mbar_init(&bar->k_full[s], 1); tc::mbar_init(&bar->k_empty[s], 1);
+            tc::mbar_init(&bar->k_full[s], 1); tc::mbar_init(&bar->k_empty[s], 1); tc::mbar_init(&bar->k_split[s], 1);
         }
         for (int s = 0; s < NSV; s++) {
-            tc::mbar_init(&bar->v_full[s], 1); tc::mbar_init(&bar->v_empty[s], 1);
+            tc::mbar_init(&bar->v_full[s], 1); tc::mbar_init(&bar->v_empty[s], 1); tc::mbar_init(&bar->v_split[s], 1);
         }
         for (int b = 0; b < NBUF; b++) {
             tc::mbar_init(&bar->s_full[b], 1); tc::mbar_init(&bar->p_ready[b], NSOFT); tc::mbar_init(&bar->pv_done[b], 1);
@@ -406,7 +413,7 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                 for (int j = 0; j < it.T; j++, gt++) {
                     const int st = gt % NSK, b = gt % NBUF, use = gt / NBUF;
                     // buffer b is free once the PV of its previous tile (gt - NBUF) has read P
-                    if (!bwait(&bar->k_full[st], (gt / NSK) & 1, abort, &g_attn_watchdog, 22) ||
+                    if (!bwait(EXACT && INSPLIT ? &bar->k_split[st] : &bar->k_full[st], (gt / NSK) & 1, abort, &g_attn_watchdog, 22) ||
                         (use >= 1 && !bwait(&bar->pv_done[b], (use - 1) & 1, abort, &g_attn_watchdog, 23))) { ok = false; break; }
                     tc::tc_fence_after();
                     if (gt < 4) TRACE(34 + 2 * gt);
@@ -447,7 +454,7 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                 for (int j = 0; j < it.T; j++, gt++) {
                     const int st = gt % NSV, b = gt % NBUF, use = gt / NBUF;
                     if (!bwait(&bar->p_ready[b], use & 1, abort, &g_attn_watchdog, 24) ||
-                        !bwait(&bar->v_full[st], (gt / NSV) & 1, abort, &g_attn_watchdog, 25)) { ok = false; break; }
+                        !bwait(EXACT && INSPLIT ? &bar->v_split[st] : &bar->v_full[st], (gt / NSV) & 1, abort, &g_attn_watchdog, 25)) { ok = false; break; }
                     // the first PV of an item overwrites O: the previous item's O must have been read
                     if (j == 0 && ii >= 1 && !bwait(&bar->o_free, (ii - 1) & 1, abort, &g_attn_watchdog, 26)) { ok = false; break; }
                     tc::tc_fence_after();
@@ -488,19 +495,58 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
             }
             asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
         }
+    } else if (warp == W_KS || warp == W_VS) {
+        // ======================= in-kernel split: warp 12 K, warp 13 V =======================
+        // lo = x - hi(x) of each landed raw tile into the stage's lo half. Both halves share
+        // the swizzle pattern (K: lo rows are hi rows + 64; V: lo chunks are hi chunks + 2),
+        // so lo goes at the hi byte offset plus a constant.
+        if (EXACT && INSPLIT) {
+            const bool is_k = warp == W_KS;
+            const int NSt = is_k ? NSK : NSV;
+            uint8_t* base_st = is_k ? kst : vst;
+            uint64_t* full = is_k ? bar->k_full : bar->v_full;
+            uint64_t* done = is_k ? bar->k_split : bar->v_split;
+            int gt = 0;
+            bool ok = true;
+            for (int x = x0; x < n_slots && ok; x = next_valid(x, n_slots, per, nqt)) {
+                const Item it = get_item(x, table, base, bstride, B, H, nqt, S, causal);
+                for (int j = 0; j < it.T; j++, gt++) {
+                    const int st = gt % NSt;
+                    if (!bwait(&full[st], (gt / NSt) & 1, abort, &g_attn_watchdog, 32)) { ok = false; break; }
+                    uint8_t* dst = base_st + st * STAGE;
+#pragma unroll 1
+                    for (int u0 = 0; u0 < KV_HALF / 16 / 32; u0 += 8) {
+                        float4 v[8];
+                        uint8_t* src[8];
+#pragma unroll
+                        for (int u = 0; u < 8; u++) {
+                            const int i = lane + 32 * (u0 + u);               // float4 index in the 16 KB hi data
+                            src[u] = is_k ? dst + (i >> 9) * (2 * BKV * 128) + (i & 511) * 16 : dst + i * 16;
+                            v[u] = *reinterpret_cast<const float4*>(src[u]);
+                        }
+#pragma unroll
+                        for (int u = 0; u < 8; u++)
+                            *reinterpret_cast<float4*>(src[u] + (is_k ? BKV * 128 : KV_HALF)) =
+                                make_float4(v[u].x - hi_part(v[u].x), v[u].y - hi_part(v[u].y), v[u].z - hi_part(v[u].z),
+                                            v[u].w - hi_part(v[u].w));
+                    }
+                    tc::fence_proxy_async();                  // visible to the tensor core's operand reads
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&done[st]);
+                }
+            }
+        }
     } else {
         // ======================= producers: warp 10 K, warp 11 V =======================
         // One thread per operand puts each key tile in place with TMA: the raw FP32 values
-        // (= the hi operand: the MMA reads only their TF32 bits) and, FP32-exact, their lo
-        // parts from the copies the split pass made (lcu_attention_tc runs it first), each as
-        // two boxes of 32 d x 64 keys, swizzled as the MMA reads them. Nothing is computed
-        // here: splitting in shared memory next to the MMAs' operand reads was measured to
-        // cost more than the split pass's extra HBM traffic.
+        // (= the hi operand: the MMA reads only their TF32 bits) as two boxes of 32 d x 64
+        // keys, swizzled as the MMA reads them; with a split pass, also their lo parts from
+        // its copies.
         const bool is_k = warp == W_K;
         if ((warp == W_K || warp == W_V) && lane == 0) {
             // lo comes from the split pass this kernel may have started beside (a no-op
             // without a programmatic dependency)
-            if (EXACT) asm volatile("griddepcontrol.wait;" ::: "memory");
+            if (EXACT && !INSPLIT) asm volatile("griddepcontrol.wait;" ::: "memory");
             const int NSt = is_k ? NSK : NSV;
             uint8_t* base_st = is_k ? kst : vst;
             uint64_t* full = is_k ? bar->k_full : bar->v_full;
@@ -516,19 +562,19 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                 if (is_k && gt == 0) TRACE(3);
                 if (gmaps) {
                     tc::tmap_acquire(mhi);
-                    if (EXACT) tc::tmap_acquire(mlo);
+                    if (EXACT && !INSPLIT) tc::tmap_acquire(mlo);
                 }
                 if (is_k && gt == 0) TRACE(7);
                 for (int j = 0; j < it.T; j++, gt++) {
                     const int st = gt % NSt;
                     if (gt >= NSt && !bwait(&empty[st], ((gt / NSt) - 1) & 1, abort, &g_attn_watchdog, 31)) { ok = false; break; }
                     uint8_t* dst = base_st + st * STAGE;
-                    tc::mbar_expect_tx(&full[st], EXACT ? 2 * KV_HALF : KV_HALF);
+                    tc::mbar_expect_tx(&full[st], EXACT && !INSPLIT ? 2 * KV_HALF : KV_HALF);
                     for (int a = 0; a < 2; a++) {   // d 0-31 and 32-63
                         // K: per 32-d atom 64 hi rows then 64 lo rows; V: hi chunks, then lo chunks
                         uint8_t* h = dst + a * (is_k ? 2 * BKV * 128 : BKV * 128);
                         tma_load_4d(h, mhi, &full[st], 32 * a, it.h, j * BKV, cb);
-                        if (EXACT) tma_load_4d(h + (is_k ? BKV * 128 : KV_HALF), mlo, &full[st], 32 * a, it.h, j * BKV, cb);
+                        if (EXACT && !INSPLIT) tma_load_4d(h + (is_k ? BKV * 128 : KV_HALF), mlo, &full[st], 32 * a, it.h, j * BKV, cb);
                     }
                     if (gt < 7) TRACE(is_k ? 50 + gt : 57 + (gt < 5 ? gt : 4));
                 }
@@ -634,11 +680,14 @@ bool make_qkv_map(CUtensorMap* m, const float* base, size_t B, size_t S, size_t 
 extern "C" bool lcu_attention_tc_make_maps(CUtensorMap* maps, const float* q, const float* k, const float* v,
                                            const float* o, const float* lo, size_t B, size_t S, size_t H) {
     const size_t n = S * H * D;
+    // without lo copies (the kernel splits K and V itself) the lo slots repeat the K and V maps
     return make_qkv_map(maps + 0, q, B, S, H, 0, BQ, CU_TENSOR_MAP_SWIZZLE_128B) &&
            make_qkv_map(maps + 1, k, B, S, H, 0, BKV, CU_TENSOR_MAP_SWIZZLE_128B) &&
            make_qkv_map(maps + 2, v, B, S, H, 0, BKV, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) &&
-           make_qkv_map(maps + 3, lo, B, S, H, 2 * n, BKV, CU_TENSOR_MAP_SWIZZLE_128B) &&
-           make_qkv_map(maps + 4, lo + n, B, S, H, 2 * n, BKV, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) &&
+           (lo ? make_qkv_map(maps + 3, lo, B, S, H, 2 * n, BKV, CU_TENSOR_MAP_SWIZZLE_128B)
+               : make_qkv_map(maps + 3, k, B, S, H, 0, BKV, CU_TENSOR_MAP_SWIZZLE_128B)) &&
+           (lo ? make_qkv_map(maps + 4, lo + n, B, S, H, 2 * n, BKV, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)
+               : make_qkv_map(maps + 4, v, B, S, H, 0, BKV, CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B)) &&
            make_qkv_map(maps + 5, o, B, S, H, 0, BQ, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
@@ -646,13 +695,22 @@ extern "C" size_t lcu_attention_tc_lo_floats(size_t B, size_t S, size_t H) { ret
 
 extern "C" int lcu_attention_tc_supported(size_t D_) { return D_ == (size_t)D; }
 
+// FP32-exact: lo of K and V is made inside the attention kernel unless LCU_ATTN_SPLIT_PASS=1
+// (then a split pass writes it into a lo buffer first and the kernel loads it by TMA).
+static bool attn_split_pass() {
+    static const bool v = [] { const char* e = getenv("LCU_ATTN_SPLIT_PASS"); return e && e[0] == '1'; }();
+    return v;
+}
+extern "C" int lcu_attention_tc_needs_lo(void) { return attn_split_pass() ? 1 : 0; }
+
 extern "C" lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, const float* k, const float* v,
                                           float* o, size_t B, size_t S, size_t H, int causal, int mode,
                                           const CUtensorMap* d_maps, float* lo, void* stream) {
     if (B == 0 || S == 0 || H == 0) return LANCIUS_ERROR_OK;
     AttnMaps pm{};
+    const bool exact = mode != LCU_MODE_TF32, split_pass = exact && attn_split_pass();
     if (!d_table) {
-        if (!lo && !(lo = static_cast<float*>(lcu_scratch_acquire(lcu_attention_tc_lo_floats(B, S, H) * 4)))) {
+        if (split_pass && !lo && !(lo = static_cast<float*>(lcu_scratch_acquire(lcu_attention_tc_lo_floats(B, S, H) * 4)))) {
             lancius_set_error(LANCIUS_ERROR_OOM);
             return LANCIUS_ERROR_OOM;
         }
@@ -661,15 +719,14 @@ extern "C" lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const flo
             return LANCIUS_ERROR_INTERNAL;
         }
     }
-    if (d_table && (!d_maps || !lo)) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
+    if (d_table && (!d_maps || (split_pass && !lo))) { lancius_set_error(LANCIUS_ERROR_INTERNAL); return LANCIUS_ERROR_INTERNAL; }
     static int sms = 0;
     if (!sms) {
         int dev = 0;
         cudaGetDevice(&dev);
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) sms = LCU_SMS;
     }
-    const bool exact = mode != LCU_MODE_TF32;
-    if (exact) {
+    if (split_pass) {
         const size_t total4 = 2 * B * S * H * D / 4;
         k_attn_split_lo<<<lcu_blocks(total4, SPLIT_THREADS, 16u * (unsigned)sms), SPLIT_THREADS, 0, lcu_as_stream(stream)>>>(
             d_table, LcuAttnGroup{q, k, v, o}, S * H * D, (int)B, S * H * D, lo);
@@ -679,17 +736,18 @@ extern "C" lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const flo
     int dev_ = 0;
     cudaGetDevice(&dev_);
     if (dev_ >= 0 && dev_ < 64 && !configured[dev_]) {
-        if (cudaFuncSetAttribute(k_attn_tc<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess ||
-            cudaFuncSetAttribute(k_attn_tc<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
+        if (cudaFuncSetAttribute(k_attn_tc<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess ||
+            cudaFuncSetAttribute(k_attn_tc<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess ||
+            cudaFuncSetAttribute(k_attn_tc<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess)
             return lcu_launch_status();
         configured[dev_] = true;
     }
     LcuAttnGroup base{q, k, v, o};
     float scale_log2 = (float)(1.4426950408889634 / 8.0);   // log2(e) / sqrt(64)
     // persistent grid: one CTA per SM (TMEM and shared memory allow no more), each walks
-    // pairs of query tiles of equal total cost with stride gridDim.x. FP32-exact, it is a
-    // programmatic dependent of the split pass: its CTAs start while the split runs and
-    // only the loads of lo wait for it.
+    // pairs of query tiles of equal total cost with stride gridDim.x. After a split pass it
+    // is that pass's programmatic dependent: its CTAs start while the split runs and only
+    // the loads of lo wait for it.
     const size_t pairs = ((S + BQ - 1) / BQ + 1) / 2 * H * B;
     const unsigned grid = (unsigned)(pairs < (size_t)sms ? pairs : (size_t)sms);
     cudaLaunchConfig_t cfg = {};
@@ -702,13 +760,15 @@ extern "C" lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const flo
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     static const bool no_pdl = [] { const char* e = getenv("LCU_ATTN_NO_PDL"); return e && e[0] == '1'; }();
-    cfg.numAttrs = exact && !no_pdl ? 1 : 0;
+    cfg.numAttrs = split_pass && !no_pdl ? 1 : 0;
     const CUtensorMap* dm = d_table ? d_maps : nullptr;
     const size_t bstride = S * H * D;
-    cudaError_t e = exact ? cudaLaunchKernelEx(&cfg, k_attn_tc<true>, d_table, base, bstride, (int)B, (int)S, (int)H, causal,
-                                               scale_log2, dm, pm)
-                          : cudaLaunchKernelEx(&cfg, k_attn_tc<false>, d_table, base, bstride, (int)B, (int)S, (int)H, causal,
-                                               scale_log2, dm, pm);
+    cudaError_t e = !exact     ? cudaLaunchKernelEx(&cfg, k_attn_tc<false, false>, d_table, base, bstride, (int)B, (int)S, (int)H,
+                                                    causal, scale_log2, dm, pm)
+                    : split_pass ? cudaLaunchKernelEx(&cfg, k_attn_tc<true, false>, d_table, base, bstride, (int)B, (int)S,
+                                                      (int)H, causal, scale_log2, dm, pm)
+                                 : cudaLaunchKernelEx(&cfg, k_attn_tc<true, true>, d_table, base, bstride, (int)B, (int)S,
+                                                      (int)H, causal, scale_log2, dm, pm);
     if (e != cudaSuccess) {
         cudaGetLastError();
         return lcu_check_cuda(e);

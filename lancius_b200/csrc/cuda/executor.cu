@@ -818,18 +818,20 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
             for (int i = 0; i < st.count; i++) { patch(t[i].q); patch(t[i].k); patch(t[i].v); patch((const float*&)t[i].o); }
             if (lcu_attention_tc_supported(st.D)) {   // Q/K/V tensor maps of every node, read by TMA
                 const size_t per_set = lcu_attention_tc_lo_floats(1, st.S, st.H);
-                float* lo = nullptr;
-                if (cudaMalloc(&lo, per_set * st.count * sizeof(float)) != cudaSuccess) {
-                    cudaGetLastError();
-                    release_binding(c);
-                    return fail(LANCIUS_ERROR_OOM);
+                float* lo = nullptr;   // K/V lo copies only for the split-pass form
+                if (lcu_attention_tc_needs_lo()) {
+                    if (cudaMalloc(&lo, per_set * st.count * sizeof(float)) != cudaSuccess) {
+                        cudaGetLastError();
+                        release_binding(c);
+                        return fail(LANCIUS_ERROR_OOM);
+                    }
+                    c->attn_lo.push_back(lo);
                 }
-                c->attn_lo.push_back(lo);
                 st.attn_lo = lo;
                 std::vector<CUtensorMap> maps(LCU_ATTN_TC_MAPS * st.count);
                 for (int i = 0; i < st.count; i++)
                     if (!lcu_attention_tc_make_maps(&maps[LCU_ATTN_TC_MAPS * i], t[i].q, t[i].k, t[i].v, t[i].o,
-                                                    lo + per_set * i, 1, st.S, st.H)) {
+                                                    lo ? lo + per_set * i : nullptr, 1, st.S, st.H)) {
                         release_binding(c);
                         return fail(LANCIUS_ERROR_INTERNAL);
                     }

@@ -169,6 +169,7 @@ lancius_error lcu_attention_tc(const LcuAttnGroup* d_table, const float* q, cons
 bool lcu_attention_tc_make_maps(CUtensorMap* maps, const float* q, const float* k, const float* v, const float* o,
                                 const float* lo, size_t B, size_t S, size_t H);
 size_t lcu_attention_tc_lo_floats(size_t B, size_t S, size_t H);
+int lcu_attention_tc_needs_lo(void);   // 0: the kernel splits K and V itself, lo may be NULL
 int lcu_attention_watchdog_read_and_clear(void);
 void lcu_reset_launch_count(void);
 int lcu_launch_count(void);
