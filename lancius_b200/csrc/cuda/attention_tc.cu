@@ -29,8 +29,8 @@
 //              P_hi*[V_hi|V_lo] and P_lo*V_hi into O.
 //   warp 10    K producer, warp 11 V producer (one lane each): TMA of the raw key tile
 //              (= the hi operand: the MMA reads only the TF32 bits).
-//   warps 12-13 K and V splitters: lo = x - hi(x) of each landed tile into the stage's lo
-//              half, then the stage is released to the issuers. (LCU_ATTN_SPLIT_PASS=1
+//   warps 12-15 splitters (12-13 K, 14-15 V): lo = x - hi(x) of each landed tile into the
+//              stage's lo half, then the stage is released to the issuers. (LCU_ATTN_SPLIT_PASS=1
 //              instead runs a split pass over all of K and V first, whose lo copies the
 //              producers load by TMA; the kernel is then that pass's programmatic
 //              dependent. Measured 36.9 against 34.4 us per graph for the in-CTA split.)
@@ -43,8 +43,9 @@
 namespace {
 
 constexpr int D = 64, BQ = 128, BKV = 64, NSK = 3, NSV = 3, NBUF = 2;
-constexpr int W_S = 8, W_PV = 9, W_K = 10, W_V = 11, W_KS = 12, W_VS = 13;
-constexpr int THREADS = 448;
+constexpr int W_S = 8, W_PV = 9, W_K = 10, W_V = 11, W_KS = 12, W_VS = 14;   // splitters: 2 warps each
+constexpr int NSPLIT = 2;                       // splitter warps per operand
+constexpr int THREADS = 512;
 constexpr int NSOFT = 256;                      // softmax threads (warps 0-7)
 constexpr int KV_HALF = BKV * D * 4;            // 16 KB: one hi or lo tile
 constexpr int STAGE = 2 * KV_HALF;              // hi + lo
@@ -195,10 +196,10 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
     if (threadIdx.x == 0) {
         TRACE(62);
         for (int s = 0; s < NSK; s++) {
-            tc::mbar_init(&bar->k_full[s], 1); tc::mbar_init(&bar->k_empty[s], 1); tc::mbar_init(&bar->k_split[s], 1);
+            tc::mbar_init(&bar->k_full[s], 1); tc::mbar_init(&bar->k_empty[s], 1); tc::mbar_init(&bar->k_split[s], NSPLIT);
         }
         for (int s = 0; s < NSV; s++) {
-            tc::mbar_init(&bar->v_full[s], 1); tc::mbar_init(&bar->v_empty[s], 1); tc::mbar_init(&bar->v_split[s], 1);
+            tc::mbar_init(&bar->v_full[s], 1); tc::mbar_init(&bar->v_empty[s], 1); tc::mbar_init(&bar->v_split[s], NSPLIT);
         }
         for (int b = 0; b < NBUF; b++) {
             tc::mbar_init(&bar->s_full[b], 1); tc::mbar_init(&bar->p_ready[b], NSOFT); tc::mbar_init(&bar->pv_done[b], 1);
@@ -495,13 +496,14 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
             }
             asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
         }
-    } else if (warp == W_KS || warp == W_VS) {
-        // ======================= in-kernel split: warp 12 K, warp 13 V =======================
+    } else if (warp >= W_KS) {
+        // ======================= in-kernel split: warps 12-13 K, 14-15 V =======================
         // lo = x - hi(x) of each landed raw tile into the stage's lo half. Both halves share
         // the swizzle pattern (K: lo rows are hi rows + 64; V: lo chunks are hi chunks + 2),
         // so lo goes at the hi byte offset plus a constant.
         if (EXACT && INSPLIT) {
-            const bool is_k = warp == W_KS;
+            const bool is_k = warp < W_VS;
+            const int part = (warp - W_KS) % NSPLIT;      // this warp's share of the tile
             const int NSt = is_k ? NSK : NSV;
             uint8_t* base_st = is_k ? kst : vst;
             uint64_t* full = is_k ? bar->k_full : bar->v_full;
@@ -515,12 +517,13 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
                     if (!bwait(&full[st], (gt / NSt) & 1, abort, &g_attn_watchdog, 32)) { ok = false; break; }
                     uint8_t* dst = base_st + st * STAGE;
 #pragma unroll 1
-                    for (int u0 = 0; u0 < KV_HALF / 16 / 32; u0 += 8) {
+                    for (int u0 = 0; u0 < KV_HALF / 16 / 32 / NSPLIT; u0 += 8) {
                         float4 v[8];
                         uint8_t* src[8];
 #pragma unroll
                         for (int u = 0; u < 8; u++) {
-                            const int i = lane + 32 * (u0 + u);               // float4 index in the 16 KB hi data
+                            // float4 index in the 16 KB hi data
+                            const int i = lane + 32 * (part * (KV_HALF / 16 / 32 / NSPLIT) + u0 + u);
                             src[u] = is_k ? dst + (i >> 9) * (2 * BKV * 128) + (i & 511) * 16 : dst + i * 16;
                             v[u] = *reinterpret_cast<const float4*>(src[u]);
                         }
