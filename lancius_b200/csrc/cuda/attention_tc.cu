@@ -124,7 +124,7 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-struct Item { LcuAttnGroup p; int b, h, q0, T; };
+struct Item { int b, h, q0, T; };   // operand set (batch element), head, first query row, key tiles
 constexpr int NMAPS = LCU_ATTN_TC_MAPS;  // Q, K, V, K_lo, V_lo, O
 struct AttnMaps { CUtensorMap m[NMAPS]; };   // over [B][S][H][D] (per-op launches)
 
@@ -137,19 +137,17 @@ struct AttnMaps { CUtensorMap m[NMAPS]; };   // over [B][S][H][D] (per-op launch
 // heavy one, whose long run of tiles then keeps the tensor pipe busy to the end.
 __device__ __forceinline__ int next_slot(int x) { return (x & 1) ? x - 1 + 2 * (int)gridDim.x : x + 1; }
 
+// Everything an item needs comes from the slot index and the tensor maps: no global load
+// (the operand table, cold after an L2 flush, cost ~0.7 us at each role's start).
 __device__ __forceinline__ Item get_item(int x, const LcuAttnGroup* table, const LcuAttnGroup& base, size_t bstride,
                                          int B, int H, int nqt, int S, int causal) {
+    (void)table; (void)base; (void)bstride;
     Item it;
     const int per = B * H;
     const int pair = x >> 1, qp = pair / per, r = pair % per, b = r / H;
     const int qt = (x & 1) ? nqt - 1 - qp : qp;
     it.h = r % H;
     it.b = b;
-    if (table) it.p = table[b];
-    else {
-        size_t off = (size_t)b * bstride;
-        it.p.q = base.q + off; it.p.k = base.k + off; it.p.v = base.v + off; it.p.o = base.o + off;
-    }
     it.q0 = qt * BQ;
     const int kv_end = causal ? min(S, it.q0 + BQ) : S;
     it.T = (kv_end + BKV - 1) / BKV;
@@ -195,6 +193,16 @@ k_attn_tc(const LcuAttnGroup* __restrict__ table, LcuAttnGroup base, size_t bstr
 
     if (threadIdx.x == 0) {
         TRACE(62);
+        {   // the descriptors of this CTA's first pair of items, fetched while the CTA sets up
+            const int xs[2] = {2 * (int)blockIdx.x, 2 * (int)blockIdx.x + 1};
+            for (int i = 0; i < 2; i++) {
+                const int bb = ((xs[i] >> 1) % per) / H;
+                const CUtensorMap* mp = gmaps ? gmaps + NMAPS * bb : pm.m;
+                if (xs[i] < n_slots) {
+                    tc::prefetch_tmap(mp + 0); tc::prefetch_tmap(mp + 1); tc::prefetch_tmap(mp + 2); tc::prefetch_tmap(mp + 5);
+                }
+            }
+        }
         for (int s = 0; s < NSK; s++) {
             tc::mbar_init(&bar->k_full[s], 1); tc::mbar_init(&bar->k_empty[s], 1); tc::mbar_init(&bar->k_split[s], NSPLIT);
         }
