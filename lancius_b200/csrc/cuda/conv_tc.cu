@@ -628,7 +628,7 @@ extern "C" size_t lcu_conv_nhwc_scratch_bytes(LcuConvShape cs, int passes) {
 
 extern "C" lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const float* w, LcuConvShape cs, int relu,
                                             int mode, void* scratch, void* stream) {
-    return lcu_conv2d_tc_nhwc_ex(out, in, w, cs, relu, mode, scratch, stream, 0, 0, nullptr, nullptr);
+    return lcu_conv2d_tc_nhwc_ex(out, in, w, cs, relu, mode, scratch, stream, 0, 0, nullptr, nullptr, nullptr, nullptr);
 }
 
 static bool conv_pt_enabled() {
@@ -648,9 +648,21 @@ extern "C" lancius_error lcu_nhwc_to_nchw(void* out, const float* in, int n, int
 // in_nhwc: `in` already holds the input as NHWC FP32 (written by the previous conv);
 // in_lo: with in_nhwc, tf32_lo of that input (NHWC), loaded by TMA instead of split on chip;
 // out_nhwc: store the output NHWC (persistent kernel only); out_lo: also its tf32_lo.
+// The [Co][Kh][Kw][Ci] TF32 hi/lo copies of OIHW weights that the direct conv streams (a
+// weight cache refreshes them once per upload instead of once per run).
+extern "C" lancius_error lcu_conv_weight_split(const float* w, float* hi, float* lo, int co, int ci, int kh, int kw,
+                                               void* stream) {
+    const size_t we = (size_t)co * ci * kh * kw;
+    if (!we) return LANCIUS_ERROR_OK;
+    k_weight_khwc_split<<<lcu_blocks(we, 256), 256, 0, lcu_as_stream(stream)>>>(w, hi, lo, co, ci, kh, kw);
+    lcu_note_launch();
+    return lcu_launch_status();
+}
+
+// w_hi / w_lo: the weights already split (lcu_conv_weight_split), or NULL to split them here.
 extern "C" lancius_error lcu_conv2d_tc_nhwc_ex(float* out, const float* in, const float* w, LcuConvShape cs, int relu,
                                                int mode, void* scratch, void* stream, int in_nhwc, int out_nhwc,
-                                               const float* in_lo, float* out_lo) {
+                                               const float* in_lo, float* out_lo, const float* w_hi, const float* w_lo) {
     const int passes = mode == LCU_MODE_TF32 ? 1 : 3;
     if (!lcu_conv_nhwc_supported(cs) || !scratch) { lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP; }
     cudaStream_t st = lcu_as_stream(stream);
@@ -680,8 +692,13 @@ extern "C" lancius_error lcu_conv2d_tc_nhwc_ex(float* out, const float* in, cons
             in, xh, xl, cs.ci, cs.h, cs.w, raw ? 0 : 1);
         lcu_note_launch();
     }
-    k_weight_khwc_split<<<lcu_blocks(we, 256), 256, 0, st>>>(w, wh, wl, cs.co, cs.ci, cs.kh, cs.kw);
-    lcu_note_launch();
+    if (w_hi && (w_lo || passes == 1)) {
+        wh = const_cast<float*>(w_hi);
+        wl = const_cast<float*>(w_lo);
+    } else {
+        k_weight_khwc_split<<<lcu_blocks(we, 256), 256, 0, st>>>(w, wh, wl, cs.co, cs.ci, cs.kh, cs.kw);
+        lcu_note_launch();
+    }
     lancius_error e = lcu_launch_status();
     if (e != LANCIUS_ERROR_OK) return e;
 

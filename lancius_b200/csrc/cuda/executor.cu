@@ -92,8 +92,9 @@ struct lcu_ctx {
     int8_t* packed = nullptr;
     size_t packed_bytes = 0;
     // FP32 weights (INPUT nodes) feeding tensor-core MATMULs, kept as TF32 hi/lo copies
-    // ([Gb][K][pad4(N)] per step, lo after hi) and refreshed by every upload of the node
-    struct WSplit { uint32_t node; size_t hi_off, lo_off, K, N, Np; };
+    // ([Gb][K][pad4(N)] per step, lo after hi) and refreshed by every upload of the node;
+    // conv weights (conv != 0) are kept as [Co][Kh][Kw][Ci] hi/lo copies the same way
+    struct WSplit { uint32_t node; size_t hi_off, lo_off, K, N, Np; int conv = 0, co = 0, ci = 0, kh = 0, kw = 0; };
     std::vector<WSplit> wsplits;
     float* wsplit = nullptr;
     size_t wsplit_floats = 0;
@@ -570,6 +571,15 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                         std::vector<LcuGemmGroup> t{LcuGemmGroup{ptr_token(O(wt)), ptr_token(O(in)), (float*)ptr_token(O(n)),
                                                                  nullptr, nullptr}};
                         st.table_off = b.add_table(t);
+                        // weights that only uploads write are split once per upload, not per run
+                        if (lcu_conv_nhwc_supported(cs) && wt->op == LANCIUS_OP_INPUT && !lcu_no_weight_cache()) {
+                            const size_t we = st.co * st.K;
+                            st.wsplit_off = c->wsplit_floats;
+                            lcu_ctx::WSplit ws{wt->id, st.wsplit_off, st.wsplit_off + align_up(we, 64), st.K, st.co, st.co};
+                            ws.conv = 1; ws.co = (int)st.co; ws.ci = (int)st.ci; ws.kh = (int)st.kh; ws.kw = (int)st.kw;
+                            c->wsplits.push_back(ws);
+                            c->wsplit_floats += 2 * align_up(we, 64);
+                        }
                     }
                 } break;
                 case LANCIUS_OP_SUM: case LANCIUS_OP_SUM_AXIS0: case LANCIUS_OP_TRANSPOSE: case LANCIUS_OP_RELU_BWD:
@@ -913,7 +923,10 @@ static bool node_slot(lcu_ctx* c, const lancius_node* n, float** p, size_t* E) {
 static lancius_error refresh_weight_splits(lcu_ctx* c, uint32_t id, const float* d) {
     for (const auto& w : c->wsplits)
         if (w.node == id) {
-            lancius_error e = lcu_tf32_split_rows(d, w.K, w.N, w.Np, c->wsplit + w.hi_off, c->wsplit + w.lo_off, c->stream);
+            lancius_error e = w.conv ? lcu_conv_weight_split(d, c->wsplit + w.hi_off, c->wsplit + w.lo_off, w.co, w.ci,
+                                                             w.kh, w.kw, c->stream)
+                                     : lcu_tf32_split_rows(d, w.K, w.N, w.Np, c->wsplit + w.hi_off, c->wsplit + w.lo_off,
+                                                           c->stream);
             if (e != LANCIUS_ERROR_OK) return e;
         }
     return LANCIUS_ERROR_OK;
@@ -1126,7 +1139,10 @@ static lancius_error run_steps(lcu_ctx* c) {
                     if (lcu_conv_nhwc_supported(cs) && !lcu_conv_force_im2col()) {
                         e = lcu_conv2d_tc_nhwc_ex(F(s.out), F(s.in0), F(s.in1), cs, s.relu, lcu_contraction_mode(c->mode), c->scratch, st,
                                                   s.in_nhwc, s.out_nhwc, s.in_lo != NPOS ? c->lo_buf + s.in_lo : nullptr,
-                                                  s.out_lo != NPOS ? c->lo_buf + s.out_lo : nullptr);
+                                                  s.out_lo != NPOS ? c->lo_buf + s.out_lo : nullptr,
+                                                  s.wsplit_off != NPOS ? c->wsplit + s.wsplit_off : nullptr,
+                                                  s.wsplit_off != NPOS ? c->wsplit + s.wsplit_off + align_up((size_t)s.co * s.K, 64)
+                                                                       : nullptr);
                         break;
                     }
                     LcuTcGemmPlan& p = c->tc_plans[s.plan_idx];

@@ -140,3 +140,43 @@ def test_gemm_epilogue_shapes(device, m, k, n, groups):
         assert_close(out[i], np.maximum(xa[i] @ wa + ba, 0) + ra[i], 1e-4, k=min(k, 8192))
     device.execute(s)                         # a rerun gives the same bytes
     assert all(np.array_equal(device.download(y), a) for y, a in zip(ys, out))
+
+
+def conv_ref(x, w, stride, pad):
+    t = torch.nn.functional.conv2d(torch.from_numpy(x), torch.from_numpy(w), stride=stride, padding=pad)
+    return t.numpy()
+
+
+def test_conv_weights_reupload_refresh_and_per_run(device):
+    """The tensor-core conv reads [Co][Kh][Kw][Ci] hi/lo weight copies made at upload time:
+    a re-upload and lcu_refresh_weights remake them, and the bytes equal splitting per run."""
+    n, ci, hw, co = 2, 32, 32, 64           # 64 x 2048 x 288 multiply-adds per image: tensor cores
+    g = L.Graph()
+    x, w = g.input_4d(n, ci, hw, hw), g.input_4d(co, ci, 3, 3)
+    y = g.relu(g.conv2d(x, w, 1, 1))
+    s = g.schedule()
+    xa, w1, w2 = rnd(81, n, ci, hw, hw), rnd(82, co, ci, 3, 3), rnd(83, co, ci, 3, 3)
+    kk = ci * 9
+
+    def run(wa):
+        device.bind(s)
+        device.upload(x, xa)
+        device.upload(w, wa)
+        device.execute(s)
+        return device.download(y, np.float32)
+
+    cached = run(w1)
+    assert_close(cached, np.maximum(conv_ref(xa, w1, 1, 1), 0), 1e-4, k=kk)
+    device.upload(w, w2)                      # a new upload re-splits the weight
+    device.execute(s)
+    assert_close(device.download(y), np.maximum(conv_ref(xa, w2, 1, 1), 0), 1e-4, k=kk)
+    assert device.lib.lcu_fill(device.device_ptr(w), 0.25, co * kk, device.stream) == 0
+    device.refresh_weights()
+    device.execute(s)
+    assert_close(device.download(y), np.maximum(conv_ref(xa, np.full(w1.shape, 0.25), 1, 1), 0), 1e-4, k=kk)
+    os.environ["LCU_NO_WEIGHT_CACHE"] = "1"
+    try:
+        per_run = run(w1)
+    finally:
+        del os.environ["LCU_NO_WEIGHT_CACHE"]
+    assert np.array_equal(cached, per_run)
