@@ -104,6 +104,22 @@ def test_attention(lib, orc, B, S, H, D, causal):
     assert_close(y, ref, 1e-4)
 
 
+@pytest.mark.parametrize("growth,causal", [(0.02, 1), (0.02, 0)])
+def test_attention_running_max_raised(lib, orc, growth, causal):
+    """Scores that grow along the keys raise a row's running max after its first key tile, so
+    O is rescaled in TMEM mid-item. The scores reach ~40 (natural units), so their FP32
+    rounding alone (~|s| * 2^-23 per term) moves outputs by a few 1e-6 of max|ref|: the
+    elementwise abs term is 1e-5 here, the normwise bound stays 1e-4."""
+    B, S, H, D = 2, 512, 4, 64
+    q = data.normal(17, (B, S, H, D))
+    k = data.normal(18, (B, S, H, D)) * (1.0 + growth * np.arange(S))[None, :, None, None]
+    v = data.normal(19, (B, S, H, D))
+    ref = np.stack([orc.attention(q[i], k[i], v[i], bool(causal)) for i in range(B)])
+    out = torch.empty((B, S, H, D), device="cuda")
+    run(lib.lcu_attention(P(out), P(dev(q)), P(dev(k)), P(dev(v)), B, S, H, D, causal, MODE_FP32_EXACT, None))
+    assert_close(out.cpu().numpy(), ref, 1e-4, elem_abs=1e-5)
+
+
 @pytest.mark.parametrize("M,K,N", [(1024, 3072, 768), (520, 768, 1000)])
 def test_matmul_tile_widths(lib, orc, M, K, N):
     """The tensor-core GEMM's 256 x 192 tiles (chosen when they take fewer rounds of the SMs,
