@@ -53,6 +53,8 @@ struct ConvArgs {
     int tma_out;     // with out_nhwc: the epilogue stages 32 x 32 blocks and stores them by TMA (maps to_hi/to_lo)
     float* out_lo;   // with out_nhwc: also store tf32_lo of every output there (NHWC), so the next
                      // conv loads hi (the value itself) and lo by TMA and needs no splitter
+    float* gap;      // NCHW output (persistent kernel): also store each tile's per-channel sum of
+                     // its outputs at gap[(img * tiles_per_img + tile) * Co + co], for a global pool
 };
 
 __device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
@@ -400,9 +402,18 @@ k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
             const int co0 = m0 + 32 * q;
             const uint32_t tbase = tmem + ((uint32_t)(32 * q) << 16) + (uint32_t)b * 256;
             uint32_t va[32];
+            float gsum = 0.f;                            // this channel's sum over the tile's pixels
             tc::tmem_ld32_issue(tbase, va);
             for (int c = 0; c < bn; c += 32) {
                 tc::tmem_ld_wait(va);
+                if (a.gap) {
+#pragma unroll
+                    for (int px = 0; px < 32; px++) {
+                        float x = __uint_as_float(va[px]);
+                        if (a.relu) x = fmaxf(x, 0.f);
+                        if (c + px < valid) gsum += x;
+                    }
+                }
                 if (a.tma_out) {
                     // NHWC by TMA: lane = channel; the block is staged as 32 pixel rows of 32
                     // channels (128-byte swizzle) in hi and lo halves and stored as one box
@@ -474,6 +485,8 @@ k_conv_pt(const __grid_constant__ CUtensorMap tw_hi, const __grid_constant__ CUt
                 }
                 __syncwarp();
             }
+            if (a.gap && co0 + lane < a.co)
+                a.gap[((size_t)img * tiles_per_img + ho0 / a.rows) * a.co + co0 + lane] = gsum;
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&sm->acc_empty[b]);
@@ -628,7 +641,8 @@ extern "C" size_t lcu_conv_nhwc_scratch_bytes(LcuConvShape cs, int passes) {
 
 extern "C" lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const float* w, LcuConvShape cs, int relu,
                                             int mode, void* scratch, void* stream) {
-    return lcu_conv2d_tc_nhwc_ex(out, in, w, cs, relu, mode, scratch, stream, 0, 0, nullptr, nullptr, nullptr, nullptr);
+    return lcu_conv2d_tc_nhwc_ex(out, in, w, cs, relu, mode, scratch, stream, 0, 0, nullptr, nullptr, nullptr, nullptr,
+                                 nullptr, nullptr);
 }
 
 static bool conv_pt_enabled() {
@@ -659,10 +673,39 @@ extern "C" lancius_error lcu_conv_weight_split(const float* w, float* hi, float*
     return lcu_launch_status();
 }
 
+// Per-channel tile sums for a global average pool after the conv: the tiles of an image and
+// their [img][tile][Co] sums (lcu_conv2d_tc_nhwc_ex's gap buffer).
+extern "C" int lcu_conv_tiles_per_image(LcuConvShape cs) {
+    const int rows = pick_rows(cs.wo, cs.ho, cs.stride);
+    return rows ? (cs.ho + rows - 1) / rows : 0;
+}
+
+__global__ void k_sum_tile_partials(float* __restrict__ out, const float* __restrict__ part, int n, int co, int tiles) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n * co) return;
+    const int img = i / co, c = i - img * co;
+    const float* p = part + (size_t)img * tiles * co + c;
+    float s = 0.f;
+    for (int t = 0; t < tiles; t++) s += p[(size_t)t * co];
+    out[i] = s;
+}
+
+// out[img * Co + c] = sum over the image's tiles of gap[(img * tiles + t) * Co + c]
+extern "C" lancius_error lcu_conv_gap_sum(float* out, const float* gap, int n, int co, int tiles, void* stream) {
+    if (n <= 0 || co <= 0) return LANCIUS_ERROR_OK;
+    k_sum_tile_partials<<<(unsigned)((n * co + 255) / 256), 256, 0, lcu_as_stream(stream)>>>(out, gap, n, co, tiles);
+    lcu_note_launch();
+    return lcu_launch_status();
+}
+
 // w_hi / w_lo: the weights already split (lcu_conv_weight_split), or NULL to split them here.
+// gap: where the persistent kernel with an NCHW output also stores per-tile channel sums
+// ([img][tile][Co], lcu_conv_tiles_per_image tiles); *gap_written tells whether it did.
 extern "C" lancius_error lcu_conv2d_tc_nhwc_ex(float* out, const float* in, const float* w, LcuConvShape cs, int relu,
                                                int mode, void* scratch, void* stream, int in_nhwc, int out_nhwc,
-                                               const float* in_lo, float* out_lo, const float* w_hi, const float* w_lo) {
+                                               const float* in_lo, float* out_lo, const float* w_hi, const float* w_lo,
+                                               float* gap, int* gap_written) {
+    if (gap_written) *gap_written = 0;
     const int passes = mode == LCU_MODE_TF32 ? 1 : 3;
     if (!lcu_conv_nhwc_supported(cs) || !scratch) { lancius_set_error(LANCIUS_ERROR_UNSUPPORTED_OP); return LANCIUS_ERROR_UNSUPPORTED_OP; }
     cudaStream_t st = lcu_as_stream(stream);
@@ -752,7 +795,11 @@ extern "C" lancius_error lcu_conv2d_tc_nhwc_ex(float* out, const float* in, cons
     if (!tma_out) mo_hi = mw_hi;
     if (!tma_out || !out_lo) mo_lo = mo_hi;
     ConvArgs a{cs.n, cs.ci, cs.co, cs.kh, cs.kw, cs.stride, cs.pad, cs.ho, cs.wo, rows, cs.co > 128 ? 2 : 1, passes, relu, raw,
-               out_nhwc, tma_out, out_nhwc ? out_lo : nullptr};
+               out_nhwc, tma_out, out_nhwc ? out_lo : nullptr, nullptr};
+    if (pt && !out_nhwc && gap) {
+        a.gap = gap;
+        if (gap_written) *gap_written = 1;
+    }
     if (pt) {
         const long long T = (long long)cs.n * ((cs.ho + rows - 1) / rows) * ((cs.co + PT_BM - 1) / PT_BM);
         k_conv_pt<<<(unsigned)std::min<long long>(T, n_sm), PT_THREADS, PT_SMEM_BYTES, st>>>(mw_hi, mw_lo, mx_hi, mx_lo, out, a, mo_hi, mo_lo);

@@ -54,6 +54,11 @@ struct Step {
     int out_nhwc = 0;          // S_CONV: store the output NHWC for the convs that read it
     size_t in_lo = (size_t)-1; // S_CONV: tf32_lo of the NHWC input in ctx->lo_buf (float offset)
     size_t out_lo = (size_t)-1;// S_CONV: where to store tf32_lo of the NHWC output
+    size_t gap_off = (size_t)-1;  // S_CONV: per-tile channel sums for a global pool (ctx->gap_buf);
+                                  // S_SUMAX1: the same sums, added up instead of reading the conv output
+    int gap_tiles = 0;            // tiles per image of those sums
+    mutable int gap_done = 0;     // S_CONV: the last run stored them (the persistent kernel ran)
+    int gap_src = -1;             // S_SUMAX1: index of the conv step that stores them
     const lancius_node* node0 = nullptr;   // first node of the step's group
     size_t table2_off = 0;     // S_MLP2: the second product's group table
     size_t N2 = 0;             // S_MLP2: columns of the second product (its K is N)
@@ -104,6 +109,8 @@ struct lcu_ctx {
     std::vector<uint8_t> nhwc;          // node id -> 1: a conv output stored NHWC (only convs read it)
     float* lo_buf = nullptr;            // tf32_lo copies of NHWC-kept conv outputs
     size_t lo_floats = 0;
+    float* gap_buf = nullptr;           // per-tile channel sums of convs feeding a global pool
+    size_t gap_floats = 0;
     std::vector<LcuTcGemmPlan> tc_plans;
     std::vector<size_t> off;            // node id -> byte offset in dmem (NPOS: no storage)
     std::vector<Step> steps;
@@ -133,6 +140,8 @@ static void release_binding(lcu_ctx* c) {
     c->nhwc.clear();
     if (c->lo_buf) { cudaFree(c->lo_buf); c->lo_buf = nullptr; }
     c->lo_floats = 0;
+    if (c->gap_buf) { cudaFree(c->gap_buf); c->gap_buf = nullptr; }
+    c->gap_floats = 0;
     c->off.clear(); c->steps.clear();
     c->g = nullptr; c->s = nullptr;
 }
@@ -526,10 +535,15 @@ static lancius_error build_steps(Builder& b, std::vector<size_t>& off, bool fuse
                     st.kind = S_SOFTMAX; st.rows = n->shape[0]; st.cols = n->shape[1];
                     st.out = O(n); st.in0 = O(n->inputs[0]);
                     break;
-                case LANCIUS_OP_SUM_AXIS1:
+                case LANCIUS_OP_SUM_AXIS1: {
                     st.kind = S_SUMAX1; st.rows = n->inputs[0]->shape[0]; st.cols = n->inputs[0]->shape[1];
                     st.out = O(n); st.in0 = O(n->inputs[0]);
-                    break;
+                    const lancius_node* src = n->inputs[0];   // through reshapes to the node that holds the data
+                    while ((src->op == LANCIUS_OP_RESHAPE || src->op == LANCIUS_OP_FLATTEN) && src->input_count == 1 &&
+                           lancius_node_elements(src) == lancius_node_elements(src->inputs[0]))
+                        src = src->inputs[0];
+                    st.in_id = src->id;
+                } break;
                 case LANCIUS_OP_BROADCAST: {
                     size_t ie = lancius_node_elements(n->inputs[0]);
                     if (ie != 1 && ie < n->shape[1]) return fail(LANCIUS_ERROR_SHAPE_MISMATCH);
@@ -719,6 +733,30 @@ static void plan_nhwc_handoff(lcu_ctx* c, const Builder& b) {
     }
 }
 
+// A global average pool over a tensor-core conv's NCHW output (SUM_AXIS1 over [N*Co][Ho*Wo],
+// through reshapes) adds up per-tile channel sums that the conv's epilogue stores beside its
+// output, instead of reading the output again. The output is still stored (any node can be
+// downloaded). LCU_NO_GAP_FUSE=1 turns this off.
+static void plan_gap_fusion(lcu_ctx* c) {
+    const char* env = getenv("LCU_NO_GAP_FUSE");
+    if (env && env[0] == '1') return;
+    for (size_t i = 0; i < c->steps.size(); i++) {
+        Step& q = c->steps[i];
+        if (q.kind != S_SUMAX1) continue;
+        for (size_t k = 0; k < i; k++) {
+            Step& p = c->steps[k];
+            if (p.kind != S_CONV || p.node_id != q.in_id || !reads_nhwc_path(p) || p.out_nhwc || p.gap_off != NPOS) continue;
+            const LcuConvShape cs = conv_shape(p);
+            const int tiles = lcu_conv_tiles_per_image(cs);
+            if (tiles <= 0 || q.rows != (size_t)cs.n * cs.co || q.cols != (size_t)cs.ho * cs.wo) continue;
+            p.gap_off = q.gap_off = c->gap_floats;
+            p.gap_tiles = q.gap_tiles = tiles;
+            q.gap_src = (int)k;
+            c->gap_floats += align_up((size_t)cs.n * tiles * cs.co, 64);
+        }
+    }
+}
+
 extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_graph* g, const lancius_memory_plan* plan) {
     if (!c || !s || !g) return fail(LANCIUS_ERROR_NULL_PTR);
     cudaSetDevice(c->device);
@@ -782,6 +820,7 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
     if (own) lancius_memory_plan_destroy(own);
     if (e != LANCIUS_ERROR_OK) { c->steps.clear(); return e; }
     if (fused) plan_nhwc_handoff(c, b);
+    if (fused) plan_gap_fusion(c);
 
     size_t table_base = align_up(cursor, SLOT_ALIGN);
     size_t total = table_base + align_up(b.tables.size(), SLOT_ALIGN);
@@ -879,6 +918,10 @@ extern "C" lancius_error lcu_bind_plan(lcu_ctx* c, lancius_schedule* s, lancius_
         // zero until the first upload, like the node slots of never-uploaded inputs
         ce = cudaMemsetAsync(c->wsplit, 0, c->wsplit_floats * sizeof(float), c->stream);
         if (ce != cudaSuccess) { release_binding(c); return cuda_fail(ce); }
+    }
+    if (c->gap_floats) {
+        ce = cudaMalloc(&c->gap_buf, c->gap_floats * sizeof(float));
+        if (ce != cudaSuccess) { cudaGetLastError(); release_binding(c); return fail(LANCIUS_ERROR_OOM); }
     }
     if (c->lo_floats) {
         ce = cudaMalloc(&c->lo_buf, c->lo_floats * sizeof(float));
@@ -1129,9 +1172,16 @@ static lancius_error run_steps(lcu_ctx* c) {
                 e = lcu_eltwise_grouped(s.op, (const LcuEltGroup*)(base + s.table_off), s.count, s.n, s.vec, st);
                 break;
             case S_SOFTMAX: e = lcu_softmax(F(s.out), F(s.in0), s.rows, s.cols, st); break;
-            case S_SUMAX1: e = lcu_sum_axis1(F(s.out), F(s.in0), s.rows, s.cols, st); break;
+            case S_SUMAX1:
+                if (s.gap_src >= 0 && c->steps[s.gap_src].gap_done)
+                    e = lcu_conv_gap_sum(F(s.out), c->gap_buf + s.gap_off, (int)c->steps[s.gap_src].cn,
+                                         (int)c->steps[s.gap_src].co, s.gap_tiles, st);
+                else
+                    e = lcu_sum_axis1(F(s.out), F(s.in0), s.rows, s.cols, st);
+                break;
             case S_BCAST: e = lcu_broadcast(F(s.out), F(s.in0), s.in_elems, s.rows, s.cols, st); break;
             case S_CONV:
+                s.gap_done = 0;
                 if (s.tc) {
                     const size_t ho = (s.h + 2 * s.pad - s.kh) / s.stride + 1, wo = (s.w + 2 * s.pad - s.kw) / s.stride + 1;
                     const LcuConvShape cs{(int)s.cn, (int)s.ci, (int)s.h, (int)s.w, (int)s.co, (int)s.kh, (int)s.kw,
@@ -1142,7 +1192,8 @@ static lancius_error run_steps(lcu_ctx* c) {
                                                   s.out_lo != NPOS ? c->lo_buf + s.out_lo : nullptr,
                                                   s.wsplit_off != NPOS ? c->wsplit + s.wsplit_off : nullptr,
                                                   s.wsplit_off != NPOS ? c->wsplit + s.wsplit_off + align_up((size_t)s.co * s.K, 64)
-                                                                       : nullptr);
+                                                                       : nullptr,
+                                                  s.gap_off != NPOS ? c->gap_buf + s.gap_off : nullptr, &s.gap_done);
                         break;
                     }
                     LcuTcGemmPlan& p = c->tc_plans[s.plan_idx];

@@ -106,7 +106,9 @@ lancius_error lcu_conv2d_tc_nhwc(float* out, const float* in, const float* w, Lc
 lancius_error lcu_conv_weight_split(const float* w, float* hi, float* lo, int co, int ci, int kh, int kw, void* stream);
 lancius_error lcu_conv2d_tc_nhwc_ex(float* out, const float* in, const float* w, LcuConvShape cs, int relu, int mode,
                                    void* scratch, void* stream, int in_nhwc, int out_nhwc, const float* in_lo,
-                                   float* out_lo, const float* w_hi, const float* w_lo);
+                                   float* out_lo, const float* w_hi, const float* w_lo, float* gap, int* gap_written);
+int lcu_conv_tiles_per_image(LcuConvShape cs);
+lancius_error lcu_conv_gap_sum(float* out, const float* gap, int n, int co, int tiles, void* stream);
 int lcu_conv_nhwc_out_ok(LcuConvShape cs);
 // NHWC FP32 -> NCHW FP32 (f64 = 0) or FP64 (f64 = 1)
 lancius_error lcu_nhwc_to_nchw(void* out, const float* in, int n, int c, int h, int w, int f64, void* stream);

@@ -79,6 +79,47 @@ def test_conv_stack_reduced(device, orc):
     assert_close(y, ref, 1e-4, k=128 * 9)
 
 
+@pytest.mark.parametrize("replay", [False, True])
+def test_conv_global_pool_from_tile_sums(device, replay):
+    """A global average pool over a tensor-core conv's NCHW output adds up per-tile channel
+    sums stored by the conv's epilogue. Ragged on both axes: Co = 96 fills part of a
+    128-channel tile, and Ho = 24 is 10 + 10 + 4 output rows. Checked against FP64 and
+    against reading the conv output (LCU_NO_GAP_FUSE=1); the conv output itself is still
+    stored and downloadable."""
+    import os
+    from lancius_b200 import data
+    n, ci, hw, co = 4, 64, 24, 96
+    xa = data.normal(71, (n, ci, hw, hw))
+    wa = data.normal(72, (co, ci, 3, 3), 0.0, 0.06)
+
+    def run():
+        g = L.Graph()
+        x, w = g.input_4d(n, ci, hw, hw), g.input_4d(co, ci, 3, 3)
+        h = g.relu(g.conv2d(x, w, 1, 1))
+        pooled = g.sum_axis1(g.reshape(h, n * co, hw * hw))
+        g.optimize_fusion()
+        s = g.schedule()
+        device.set_graph_replay(replay)
+        device.bind(s)
+        device.upload(x, xa)
+        device.upload(w, wa)
+        device.execute(s)
+        conv = [m for m in g.nodes() if m.op in ("CONV2D", "CONV2D_RELU_FUSED")][0]
+        return device.download(pooled), device.download(conv)
+
+    y, conv_out = run()
+    os.environ["LCU_NO_GAP_FUSE"] = "1"
+    try:
+        y_ref_path, _ = run()
+    finally:
+        del os.environ["LCU_NO_GAP_FUSE"]
+    t = torch.nn.functional.conv2d(torch.from_numpy(xa), torch.from_numpy(wa), padding=1).clamp_min(0).numpy()
+    assert_close(conv_out, t, 1e-4, k=ci * 9)
+    ref = t.reshape(n * co, hw * hw).sum(axis=1)
+    assert_close(y.reshape(-1), ref, 1e-4, k=ci * 9 * hw * hw)
+    assert_close(y, y_ref_path, 1e-5, elem_rel=1e-5, elem_abs=1e-6)
+
+
 def test_encoder_reduced(device, orc):
     b = configs.encoder(L.Graph(), batch=2, seq=128, layers=2)
     ys, _ = run_gpu(device, b)
